@@ -1,0 +1,448 @@
+#!/usr/bin/env python
+"""Display-refinement step throughput on B200.
+
+One step = ``display_token_statistics`` over display logits [B, L, V] followed
+by ``refine_display_from_statistics`` on the same rows, all on the device with
+no host sync (the "fused display-stats + refine step").
+
+* N=1 workload: logits bf16 [32, 1024, 128256] = bf16(2 N(0,1)), 10% of rows
+  with a +8 peak, 1% with an exact two-way max tie, display positions masked
+  with probability 0.6 and one EOS per row (synthetic data, seeded).
+* ``value`` = logits bytes of all ranks / device time of the timed steps
+  (GB/s, inputs resident in HBM; 8.4 GB of logits per step, far above the
+  126 MB L2, so no flush is needed between steps).
+* ``e2e`` = the same metric through the public API from pinned host buffers,
+  host->device copies of every step's logits and ids and the device->host
+  read of the refined ids inside the timed region (copies overlapped with the
+  statistics kernel in row chunks by ``cid_engine.host_pipeline``).
+* ``roofline`` = the statistics kernel's algorithmic bytes per launch / its
+  CUDA-event duration, against the measured HBM copy bandwidth.
+* ``cpu_baseline`` = the reference's own CPU backend (built from its sources
+  into oracle/_ref) on a bounded sample, in a separate process.
+* ``refine_loop`` = config-5 decode loop: B=256, L=512, V=32000 bf16, 128
+  slots, stats -> refine -> rollout -> live occupancy -> snapshot per step,
+  64 steps, steps/s.
+
+``--impl reference`` times the reference CPU backend on the host cores with
+the same workload, metric and unit.  Multi-GPU (torchrun, N>1): vocabulary-
+parallel statistics of [64, 4096, 152064] bf16 sharded over the ranks' GPUs
+(records all-gathered over NCCL, combined on every rank), then refinement.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "cid-engine_b200"))
+sys.path.insert(0, str(ROOT))
+
+MASK_ID, EOS_ID = 0, 1
+REVEAL, REVISION, MARGIN = 0.25, 0.1, 0.05
+CFG2 = dict(B=32, L=1024, V=128256)
+CFG4 = dict(B=64, L=4096, V=152064)
+CFG5 = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64)
+# DRAM bytes (read + write) per launch of the statistics kernel measured by
+# ncu on the cfg2 row shape (summary: profiles/display_stats_bf16_cfg2.md);
+# None until captured.
+NCU_TRAFFIC_PER_ROW = None
+
+
+def _peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs
+# ---------------------------------------------------------------------------
+
+
+def display_inputs(B, L, V, seed, device, dtype=None):
+    """bf16(2 N(0,1)) logits with planted peaks/ties, display ids with masked
+    positions (p=0.6) and one EOS per row."""
+    import torch
+
+    dtype = dtype or torch.bfloat16
+    g = torch.Generator(device=device).manual_seed(seed)
+    logits = torch.randn((B, L, V), generator=g, device=device, dtype=dtype)
+    logits.mul_(2.0)
+    rows = B * L
+    flat = logits.view(rows, V)
+    peak_rows = torch.nonzero(torch.rand(rows, generator=g, device=device) < 0.10).flatten()
+    peak_cols = torch.randint(V, (peak_rows.numel(),), generator=g, device=device)
+    flat[peak_rows, peak_cols] = (flat[peak_rows, peak_cols].float() + 8.0).to(dtype)
+    tie_rows = torch.nonzero(torch.rand(rows, generator=g, device=device) < 0.01).flatten()
+    if tie_rows.numel():
+        top = flat[tie_rows].float().amax(dim=1) + 1.0
+        c1 = torch.randint(V, (tie_rows.numel(),), generator=g, device=device)
+        c2 = (c1 + 1 + torch.randint(V - 1, (tie_rows.numel(),), generator=g, device=device)) % V
+        flat[tie_rows, c1] = top.to(dtype)
+        flat[tie_rows, c2] = top.to(dtype)
+    ids = torch.randint(2, V, (B, L), generator=g, device=device)
+    ids[torch.rand((B, L), generator=g, device=device) < 0.6] = MASK_ID
+    eos_at = torch.randint(L // 2, L, (B,), generator=g, device=device)
+    pos = torch.arange(L, device=device).expand(B, L)
+    ids[pos == eos_at[:, None]] = EOS_ID
+    ids[pos > eos_at[:, None]] = MASK_ID
+    return ids, logits
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.send_signal(signal.SIGTERM)
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        else:
+            self.lines = []
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference CPU backend (separate process: it registers torch.ops.cid_engine)
+# ---------------------------------------------------------------------------
+
+
+def cpu_reference_worker(args) -> None:
+    import torch
+
+    lib = ROOT / "oracle" / "_ref" / "libcid_engine_ref.so"
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    B, L, V = args.sample_b, args.sample_l, args.sample_v
+    ids, logits = display_inputs(B, L, V, seed=1, device="cpu")
+    if lib.exists():
+        torch.ops.load_library(str(lib))
+        kind = "reference"
+
+        def step():
+            c, p, u = torch.ops.cid_engine.display_token_statistics(ids, logits)
+            torch.ops.cid_engine.refine_display_from_statistics(
+                ids, c, p, u, MASK_ID, EOS_ID, REVEAL, REVISION, MARGIN)
+    else:
+        from oracle import oracle
+
+        kind = "port"
+
+        def step():
+            c, p, u = oracle.display_token_statistics(ids, logits)
+            oracle.refine_display_from_statistics(ids, c, p, u, MASK_ID, EOS_ID, REVEAL,
+                                                  REVISION, MARGIN)
+
+    step()  # warm-up
+    times = []
+    t_end = time.perf_counter() + args.cpu_seconds
+    while time.perf_counter() < t_end or len(times) < args.cpu_min_reps:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    nbytes = logits.numel() * logits.element_size()
+    print(json.dumps({
+        "value": nbytes / per / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
+        "ms_per_step": per * 1e3, "reps": len(times),
+        "sample": f"stats+refine on logits bf16 [{B},{L},{V}] ({nbytes / 1e9:.3f} GB) per step, "
+                  f"median of {len(times)} reps",
+    }))
+
+
+def run_cpu_baseline(sample=(1, 1024, 128256), seconds=10.0) -> dict | None:
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--cpu-worker", "--sample-b", str(sample[0]),
+           "--sample-l", str(sample[1]), "--sample-v", str(sample[2]),
+           "--cpu-seconds", str(seconds)]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600)
+        return json.loads(res.stdout.strip().splitlines()[-1])
+    except Exception as exc:  # the baseline is reported, never fatal
+        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+
+
+def time_device_steps(step, K, W, stream, kernel_events=None):
+    import torch
+
+    for _ in range(W):
+        step(None)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    pairs = []
+    start.record(stream)
+    for _ in range(K):
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        pairs.append(ev)
+        step(ev)
+    end.record(stream)
+    torch.cuda.synchronize()
+    total_ms = start.elapsed_time(end)
+    kern = [a.elapsed_time(b) for a, b in pairs]
+    return total_ms, kern
+
+
+def bench_single(args) -> dict:
+    import torch
+
+    import cid_engine
+    from cid_engine import host_pipeline
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, L, V = CFG2["B"], CFG2["L"], CFG2["V"]
+    ids, logits = display_inputs(B, L, V, seed=1, device=dev)
+    stream = torch.cuda.current_stream()
+    ops = torch.ops.cid_engine
+
+    def step(ev):
+        if ev is not None:
+            ev[0].record(stream)
+        c, p, u = ops.display_token_statistics(ids, logits)
+        if ev is not None:
+            ev[1].record(stream)
+        ops.refine_display_from_statistics(ids, c, p, u, MASK_ID, EOS_ID, REVEAL, REVISION, MARGIN)
+
+    K, W = args.steps, args.warmup
+    with ClockSampler(0) as clk:
+        total_ms, kern = time_device_steps(step, K, W, stream)
+    clocks = clk.summary()
+    nbytes = logits.numel() * logits.element_size()
+    ms = total_ms / K
+    value = nbytes / (ms * 1e-3) / 1e9
+    rows = B * L
+    alg_bytes = nbytes + rows * (8 + 4 + 8 + 4)  # logits + ids in, conf/pred/cur out
+    kern_ms = statistics.mean(kern)
+    peak, peak_kind = _peaks()
+    achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
+    traffic = None if NCU_TRAFFIC_PER_ROW is None else NCU_TRAFFIC_PER_ROW * rows
+
+    # end-to-end through the public API from pinned host memory
+    e2e = None
+    if not args.no_e2e:
+        e2e = host_pipeline.bench_e2e(ids, logits, steps=max(3, min(K, args.e2e_steps)),
+                                      warmup=2, mask_id=MASK_ID, eos_id=EOS_ID,
+                                      reveal=REVEAL, revision=REVISION, margin=MARGIN)
+    del logits
+    torch.cuda.empty_cache()
+
+    loop = None if args.no_loop else bench_refine_loop(dev)
+    cpu = None if args.no_cpu_baseline else run_cpu_baseline(seconds=args.cpu_seconds)
+    line = {
+        "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded bf16 2*N(0,1) logits, 10% planted peaks, 1% exact ties)",
+        "config": {"workload": "display stats + refine, logits bf16 [32,1024,128256]",
+                   "batch": B, "tokens": L, "vocab": V, "parallelism": "single GPU",
+                   "l2": "inputs 8.4 GB per step >> 126 MB L2; no flush needed"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "display_stats_kernel<bf16>", "peak_kind": peak_kind,
+                     "kernel_ms": round(kern_ms, 4),
+                     "algorithmic_bytes_per_launch": alg_bytes},
+        "e2e": e2e,
+        "gpu_launches": 2 * K,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "refine_loop": loop,
+    }
+    return line
+
+
+def bench_refine_loop(dev) -> dict:
+    """Config 5: 64 consecutive steps of the fused chain, no host sync."""
+    import torch
+
+    from cid_engine.step import SlotInputs, refine_step
+
+    c = CFG5
+    B, L, V, S = c["B"], c["L"], c["V"], c["S"]
+    ring = []
+    for k in range(3):  # ring of pre-generated logits (each 8.4 GB > L2)
+        g = torch.Generator(device=dev).manual_seed(4 + k)
+        lg = torch.randn((B, L, V), generator=g, device=dev, dtype=torch.bfloat16)
+        lg.mul_(3.0)
+        ring.append(lg)
+    g = torch.Generator(device=dev).manual_seed(4)
+    ids0 = torch.randint(2, V, (B, L), generator=g, device=dev)
+    ids0[torch.rand((B, L), generator=g, device=dev) < 0.6] = MASK_ID
+    occ = (torch.rand((B, S, 1), generator=g, device=dev) < 0.4).float()
+    slot = SlotInputs(
+        occupancy=occ,
+        allocation_logits=torch.randn((B, S), generator=g, device=dev),
+        lifecycle_logits=torch.randn((B, S, c["F"]), generator=g, device=dev),
+        revision_logits=torch.randn((B, S, c["Rv"]), generator=g, device=dev),
+        input_lifecycle=torch.randn((B, S, c["F"]), generator=g, device=dev),
+        semantic=torch.randn((B, S, c["H"]), generator=g, device=dev),
+        role_logits=torch.randn((B, S, c["Rr"]), generator=g, device=dev),
+        uncertainty=torch.rand((B, S, 1), generator=g, device=dev),
+        noise_delta=torch.randn((B, S, 1), generator=g, device=dev),
+        semantic_indices=torch.randint(0, c["H"], (c["K"],), generator=g, device=dev),
+        threshold=0.5, max_allocations=8, retired_index=3,
+    )
+
+    def run(nsteps):
+        ids = ids0
+        for s in range(nsteps):
+            out = refine_step(ids, ring[s % len(ring)], mask_token_id=MASK_ID, eos_token_id=EOS_ID,
+                              reveal_fraction=REVEAL, revision_fraction=REVISION,
+                              revision_margin=MARGIN, slots=slot)
+            ids = out.token_ids
+            slot.occupancy = out.next_occupancy
+        return ids
+
+    run(3)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    run(c["steps"])
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / c["steps"]
+    logits_bytes = B * L * V * 2
+    peak, _ = _peaks()
+    del ring
+    torch.cuda.empty_cache()
+    return {"workload": "refine loop B=256 L=512 V=32000 bf16, S=128, 64 steps",
+            "steps_per_s": round(1e3 / ms, 2), "ms_per_step": round(ms, 4),
+            "logits_GBps": round(logits_bytes / (ms * 1e-3) / 1e9, 1),
+            "roofline_steps_per_s": round(peak * 1e9 / logits_bytes, 1),
+            "launches_per_step": 6}
+
+
+def bench_reference(args) -> dict:
+    """Reference CPU backend on the host cores, same workload/metric."""
+    B, L, V = CFG2["B"], CFG2["L"], CFG2["V"]
+    res = run_cpu_baseline(seconds=args.cpu_seconds)
+    val = res.get("value") if res else None
+    return {
+        "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
+        "value": None if val is None else round(val, 3),
+        "unit": "GB/s",
+        "impl": "reference",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": None if not res or "ms_per_step" not in res else round(res["ms_per_step"], 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "display stats + refine, logits bf16 [32,1024,128256]",
+                   "batch": B, "tokens": L, "vocab": V, "parallelism": "host CPU",
+                   "sample": res.get("sample") if res else None},
+        "cpu_baseline": res,
+        "e2e": {"value": None if val is None else round(val, 3), "unit": "GB/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-loop", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-min-reps", type=int, default=3)
+    ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--sample-b", type=int, default=1)
+    ap.add_argument("--sample-l", type=int, default=1024)
+    ap.add_argument("--sample-v", type=int, default=128256)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.cpu_worker:
+        cpu_reference_worker(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(bench_reference(args)))
+        return
+    if world > 1:
+        from cid_engine import parallel
+
+        line = parallel.bench_vocab_parallel(args, display_inputs, ClockSampler, _peaks,
+                                             run_cpu_baseline)
+        if rank == 0:
+            print(json.dumps(line))
+        return
+    print(json.dumps(bench_single(args)))
+
+
+if __name__ == "__main__":
+    main()

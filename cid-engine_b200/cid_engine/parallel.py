@@ -1,0 +1,179 @@
+"""Vocabulary-parallel display statistics over several GPUs of one node.
+
+The display logits of a row are split by contiguous vocabulary ranges, one
+range per rank (rank r owns columns [offsets[r], offsets[r+1])).  Each rank
+reduces its shard to one 16-byte record per row — (max, sum exp(x - max),
+global first argmax, current-token logit) — the records of all ranks are
+all-gathered over NCCL (16 bytes x rows x world: a few MB, against GBs of
+logits streamed per rank), and every rank merges them with the combine kernel
+into the unsharded statistics: M = max_r m_r (lowest rank on ties, which
+holds the lowest columns), S = sum_r s_r exp(m_r - M), confidence = 1/S,
+current = exp(x_id - M)/S.  Every rank then holds identical statistics and
+can run the refinement policy without a further collective.
+
+NCCL has no user-defined reduction operator, so the "packed reduction" is
+an all-gather of records followed by a deterministic device-side merge.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import statistics as pystats
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+
+def shard_offsets(total_vocab: int, world: int) -> list[int]:
+    """Contiguous, balanced column ranges: rank r owns [o[r], o[r+1])."""
+    return [r * total_vocab // world for r in range(world + 1)]
+
+
+def gather_records(records: Tensor, group=None) -> Tensor:
+    """All-gather ``[rows, 4]`` int32 records of every rank into a
+    ``[world, rows, 4]`` tensor in rank order (NCCL on CUDA tensors, any
+    backend on host tensors)."""
+    world = dist.get_world_size(group)
+    rows = records.shape[0]
+    out = torch.empty((world * rows, *records.shape[1:]), dtype=records.dtype,
+                      device=records.device)
+    dist.all_gather_into_tensor(out, records.contiguous(), group=group)
+    return out.view(world, rows, *records.shape[1:])
+
+
+def vocab_parallel_statistics(token_ids: Tensor, logits_shard: Tensor, *, total_vocab: int,
+                              group=None) -> tuple[Tensor, Tensor, Tensor]:
+    """``display_token_statistics`` of logits sharded by vocabulary over the
+    ranks of ``group`` (this rank's shard: ``logits_shard`` [B, L, V_r], the
+    columns given by ``shard_offsets(total_vocab, world)[rank]``).  Returns
+    the unsharded (confidence, predicted, current_confidence) on every rank."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    offs = shard_offsets(total_vocab, world)
+    assert logits_shard.shape[-1] == offs[rank + 1] - offs[rank], "shard width mismatch"
+    ops = torch.ops.cid_engine
+    records = ops.display_shard_records(token_ids, logits_shard, offs[rank], total_vocab)
+    gathered = gather_records(records, group)
+    return ops.display_combine_records(gathered, token_ids, offs)
+
+
+# ---------------------------------------------------------------------------
+# multi-GPU bench arm (launched by bench.py under torchrun)
+# ---------------------------------------------------------------------------
+
+
+def sharded_display_inputs(B, L, V, rank, world, seed, device):
+    """This rank's vocabulary shard of the config-4 logits: bf16(2 N(0,1))
+    with a +8 peak in 5% of rows at a column drawn once for all ranks."""
+    offs = shard_offsets(V, world)
+    lo, hi = offs[rank], offs[rank + 1]
+    g = torch.Generator(device=device).manual_seed(seed * 1000 + rank)
+    logits = torch.randn((B, L, hi - lo), generator=g, device=device, dtype=torch.bfloat16)
+    logits.mul_(2.0)
+    gs = torch.Generator(device=device).manual_seed(seed)  # shared by all ranks
+    rows = B * L
+    peak = torch.rand(rows, generator=gs, device=device) < 0.05
+    col = torch.randint(V, (rows,), generator=gs, device=device)
+    mine = torch.nonzero(peak & (col >= lo) & (col < hi)).flatten()
+    flat = logits.view(rows, hi - lo)
+    flat[mine, col[mine] - lo] = (flat[mine, col[mine] - lo].float() + 8.0).to(torch.bfloat16)
+    # display ids (identical on every rank): masked with p=0.6, one EOS per row
+    ids = torch.randint(2, V, (B, L), generator=gs, device=device)
+    ids[torch.rand((B, L), generator=gs, device=device) < 0.6] = 0
+    eos_at = torch.randint(L // 2, L, (B,), generator=gs, device=device)
+    pos = torch.arange(L, device=device).expand(B, L)
+    ids[pos == eos_at[:, None]] = 1
+    ids[pos > eos_at[:, None]] = 0
+    return ids, logits, offs
+
+
+def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_baseline) -> dict:
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        B, L, V = 64, 4096, 152064
+        ids, logits, offs = sharded_display_inputs(B, L, V, rank, world, 3, dev)
+        ops = torch.ops.cid_engine
+        stream = torch.cuda.current_stream()
+
+        def step(ev):
+            if ev is not None:
+                ev[0].record(stream)
+            rec = ops.display_shard_records(ids, logits, offs[rank], V)
+            if ev is not None:
+                ev[1].record(stream)
+            gathered = gather_records(rec)
+            c, p, u = ops.display_combine_records(gathered, ids, offs)
+            ops.refine_display_from_statistics(ids, c, p, u, 0, 1, 0.25, 0.1, 0.05)
+
+        K, W = args.steps, args.warmup
+        for _ in range(W):
+            step(None)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                 for _ in range(K)]
+        with ClockSampler(local) as clk:
+            a.record()
+            for k in range(K):
+                step(pairs[k])
+            b.record()
+            torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms_local = a.elapsed_time(b) / K
+        kern_local = pystats.mean(x.elapsed_time(y) for x, y in pairs)
+        t = torch.tensor([ms_local, kern_local], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, kern_ms = float(t[0]), float(t[1])
+        total_bytes = B * L * V * 2
+        shard_bytes = logits.numel() * 2
+        peak, peak_kind = peaks()
+        rows = B * L
+        alg = shard_bytes + rows * (8 + 16)
+        achieved = alg / (kern_ms * 1e-3) / 1e9
+        line = {
+            "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
+            "value": round(total_bytes / (ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": W,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded bf16 2*N(0,1) logits, 5% planted peaks)",
+            "config": {"workload": "vocab-parallel display stats + refine, logits bf16 [64,4096,152064]",
+                       "batch": B, "tokens": L, "vocab": V,
+                       "parallelism": f"vocab-sharded x{world} (NCCL all-gather of 16 B row records)",
+                       "l2": f"{shard_bytes / 1e9:.1f} GB per rank per step >> 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "display_stats_kernel<bf16, records> (per rank, max over ranks)",
+                         "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
+                         "algorithmic_bytes_per_launch": alg},
+            "e2e": None,
+            "gpu_launches": 3 * K,
+            "clocks": clk.summary(),
+        }
+        if rank == 0 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = run_cpu_baseline(sample=(1, 512, V), seconds=args.cpu_seconds)
+        dist.barrier()
+        return line
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":  # pragma: no cover
+    print(json.dumps(shard_offsets(152064, 8)))

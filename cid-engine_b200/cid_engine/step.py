@@ -1,0 +1,92 @@
+"""One display-refinement decode step as a single device-resident launch chain.
+
+The reference leaves the per-step sequencing to the external CID scheduler
+(``benchmarks/README.md:29-43`` of fwerkor/cid-engine v1.1.0): statistics, the
+refinement policy (a host round trip there), slot transition, live occupancy
+and the materialisation snapshot.  ``refine_step`` enqueues the same chain of
+operators on the current stream with no host synchronisation anywhere, so a
+caller can run many steps back to back or capture them in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+
+@dataclass
+class SlotInputs:
+    """Thought-slot inputs of one step (shapes as the reference operators)."""
+
+    occupancy: Tensor  # [B, S] or [B, S, 1]
+    allocation_logits: Tensor  # [B, S]
+    lifecycle_logits: Tensor  # [B, S, F]
+    revision_logits: Tensor  # [B, S, Rv]
+    input_lifecycle: Tensor  # [B, S, F]
+    semantic: Tensor  # [B, S, H]
+    role_logits: Tensor  # [B, S, R]
+    uncertainty: Tensor  # [B, S, 1]
+    noise_delta: Tensor  # [B, S, 1]
+    semantic_indices: Tensor  # [K] int64
+    threshold: float = 0.5
+    max_allocations: int = 8
+    retired_index: int = 3
+
+
+@dataclass
+class StepOutputs:
+    token_ids: Tensor  # refined display ids [B, L]
+    confidence: Tensor
+    predicted: Tensor
+    current_confidence: Tensor
+    next_occupancy: Tensor | None = None
+    live_occupancy: Tensor | None = None
+    snapshot: Tensor | None = None
+    rollout: tuple[Tensor, ...] | None = None
+
+
+def refine_step(
+    token_ids: Tensor,
+    logits: Tensor,
+    *,
+    mask_token_id: int,
+    eos_token_id: int | None,
+    reveal_fraction: float,
+    revision_fraction: float,
+    revision_margin: float,
+    slots: SlotInputs | None = None,
+) -> StepOutputs:
+    """stats -> refine (-> rollout -> live occupancy -> snapshot), enqueued
+    on the current stream without any host synchronisation."""
+    ops = torch.ops.cid_engine
+    conf, pred, cur = ops.display_token_statistics(token_ids, logits)
+    refined = ops.refine_display_from_statistics(
+        token_ids, conf, pred, cur, mask_token_id, eos_token_id,
+        reveal_fraction, revision_fraction, revision_margin,
+    )
+    out = StepOutputs(refined, conf, pred, cur)
+    if slots is None:
+        return out
+    roll = ops.rollout_slot_transition(
+        slots.occupancy, slots.allocation_logits, slots.lifecycle_logits,
+        slots.revision_logits, slots.input_lifecycle, slots.threshold,
+        slots.max_allocations, slots.retired_index,
+    )
+    next_occ = roll[0]
+    live_slots = roll[5]
+    # live occupancy of the next state: retired slots masked out
+    live = ops.live_slot_occupancy(
+        next_occ.unsqueeze(-1).to(slots.lifecycle_logits.dtype),
+        slots.lifecycle_logits, slots.retired_index,
+    )
+    snap = ops.materialize_cell_snapshot(
+        slots.semantic, slots.role_logits, slots.uncertainty, slots.noise_delta,
+        slots.lifecycle_logits, live_slots, slots.semantic_indices,
+    )
+    out.next_occupancy = next_occ
+    out.live_occupancy = live
+    out.snapshot = snap
+    out.rollout = roll
+    return out

@@ -1,0 +1,148 @@
+// Shared device/host helpers for the sm_100a kernels behind the C ABI.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "cid_engine_b200.h"
+
+namespace cid {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------------------
+// Host-side helpers
+// ---------------------------------------------------------------------------
+
+// Records the CUDA error (for cid_last_cuda_error) and maps it to a result.
+int record_cuda_error(cudaError_t err);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool is_float_dtype(cid_dtype_t dt) {
+  return dt == CID_DTYPE_F32 || dt == CID_DTYPE_F64 || dt == CID_DTYPE_F16 ||
+         dt == CID_DTYPE_BF16;
+}
+
+inline bool is_known_dtype(int dt) { return dt >= 0 && dt <= CID_DTYPE_I16; }
+
+inline int dtype_size(cid_dtype_t dt) {
+  switch (dt) {
+    case CID_DTYPE_F64:
+    case CID_DTYPE_I64: return 8;
+    case CID_DTYPE_F32:
+    case CID_DTYPE_I32: return 4;
+    case CID_DTYPE_F16:
+    case CID_DTYPE_BF16:
+    case CID_DTYPE_I16: return 2;
+    default: return 1;
+  }
+}
+
+// Checks the launch that was just enqueued.
+inline int launch_result() { return record_cuda_error(cudaGetLastError()); }
+
+inline int sm_count() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+// ---------------------------------------------------------------------------
+// Device-side helpers
+// ---------------------------------------------------------------------------
+
+// 2^x with the SFU (ex2.approx.ftz.f32: a few ulp of relative error).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float bf16_bits_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_bits_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Value of element i of an array of runtime dtype `dt`, as float.  Used by
+// the small slot/snapshot kernels, whose inputs come in any dtype.
+__device__ __forceinline__ float load_float(cid_dtype_t dt, const void* p, int64_t i) {
+  switch (dt) {
+    case CID_DTYPE_F32: return static_cast<const float*>(p)[i];
+    case CID_DTYPE_F64: return static_cast<float>(static_cast<const double*>(p)[i]);
+    case CID_DTYPE_F16: return __half2float(static_cast<const __half*>(p)[i]);
+    case CID_DTYPE_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    case CID_DTYPE_BOOL:
+    case CID_DTYPE_U8: return static_cast<float>(static_cast<const uint8_t*>(p)[i]);
+    case CID_DTYPE_I8: return static_cast<float>(static_cast<const int8_t*>(p)[i]);
+    case CID_DTYPE_I16: return static_cast<float>(static_cast<const int16_t*>(p)[i]);
+    case CID_DTYPE_I32: return static_cast<float>(static_cast<const int32_t*>(p)[i]);
+    case CID_DTYPE_I64: return static_cast<float>(static_cast<const int64_t*>(p)[i]);
+  }
+  return __int_as_float(0x7fc00000);
+}
+
+__device__ __forceinline__ double load_double(cid_dtype_t dt, const void* p, int64_t i) {
+  if (dt == CID_DTYPE_F64) return static_cast<const double*>(p)[i];
+  if (dt == CID_DTYPE_I64) return static_cast<double>(static_cast<const int64_t*>(p)[i]);
+  return static_cast<double>(load_float(dt, p, i));
+}
+
+// `tensor.to(torch.bool)`: non-zero (NaN included) is true.
+__device__ __forceinline__ bool load_truthy(cid_dtype_t dt, const void* p, int64_t i) {
+  switch (dt) {
+    case CID_DTYPE_BOOL:
+    case CID_DTYPE_U8:
+    case CID_DTYPE_I8: return static_cast<const uint8_t*>(p)[i] != 0;
+    case CID_DTYPE_I16: return static_cast<const int16_t*>(p)[i] != 0;
+    case CID_DTYPE_F16:
+    case CID_DTYPE_BF16: return (static_cast<const uint16_t*>(p)[i] & 0x7fffu) != 0;
+    case CID_DTYPE_I32: return static_cast<const int32_t*>(p)[i] != 0;
+    case CID_DTYPE_F32: return (static_cast<const uint32_t*>(p)[i] & 0x7fffffffu) != 0;
+    case CID_DTYPE_I64: return static_cast<const int64_t*>(p)[i] != 0;
+    case CID_DTYPE_F64:
+      return (static_cast<const uint64_t*>(p)[i] & 0x7fffffffffffffffull) != 0;
+  }
+  return false;
+}
+
+// Round a float result to the storage type of `dt` and back (ATen evaluates
+// half/bfloat16 elementwise ops in float and rounds the result).
+__device__ __forceinline__ float round_to(cid_dtype_t dt, float x) {
+  if (dt == CID_DTYPE_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  if (dt == CID_DTYPE_F16) return __half2float(__float2half_rn(x));
+  return x;
+}
+
+__device__ __forceinline__ void store_float(cid_dtype_t dt, void* p, int64_t i, float x) {
+  switch (dt) {
+    case CID_DTYPE_F32: static_cast<float*>(p)[i] = x; break;
+    case CID_DTYPE_F16: static_cast<__half*>(p)[i] = __float2half_rn(x); break;
+    case CID_DTYPE_BF16: static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(x); break;
+    case CID_DTYPE_F64: static_cast<double*>(p)[i] = static_cast<double>(x); break;
+    default: break;
+  }
+}
+
+// float32 sigmoid as 1 / (1 + exp(-x)) with each step rounded to float32 and
+// exp evaluated in double (correctly rounded to float32 but for vanishingly
+// rare double-rounding cases).  ATen's scalar sigmoid loop agrees with this;
+// its vectorised loop can differ by up to two ulps.
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  const float e = static_cast<float>(exp(-static_cast<double>(x)));
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+}
+
+// ATen max/argmax order: NaN first (lowest index), then larger value, then
+// lower index.  Returns true when (v, i) should replace (bv, bi).
+__device__ __forceinline__ bool argmax_better(float v, int64_t i, float bv, int64_t bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn != bn) return vn;
+  if (vn) return i < bi;
+  return v > bv || (v == bv && i < bi);
+}
+
+}  // namespace cid

@@ -1,0 +1,384 @@
+// Training-corruption kernels (fwerkor/cid-engine v1.1.0 semantics):
+//  * masked diffusion (csrc/ops.cpp:394-444): one CTA per row, mask =
+//    u < ratio, empty-row fallback on argmin(u); the two metrics are summed
+//    by a second one-block kernel in a fixed order from per-row counts kept
+//    in a caller-provided workspace, so they are bit-identical run to run
+//    (the reference CUDA kernel adds them with float atomics);
+//  * thought corruption (csrc/ops.cpp:258-290): one CTA per slot row, alpha
+//    computed once per row, every arithmetic step rounded to the storage
+//    dtype as ATen does;
+//  * display corruption (csrc/ops.cpp:292-391): one CTA per row.
+#include <climits>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace cid {
+namespace {
+
+constexpr int kT = 256;
+constexpr int kWarps = kT / 32;
+
+// ---------------------------------------------------------------------------
+// masked diffusion
+// ---------------------------------------------------------------------------
+
+struct MaskedParams {
+  const int64_t* clean;
+  const float* ratio_random;
+  const float* mask_random;
+  int64_t batch, tokens, mask_id;
+  float span;  // float32(max - min)
+  float lo;    // float32(min)
+  int64_t* corrupted;
+  uint8_t* masked;
+  float* ratio;
+  float* metrics;
+  int64_t* counts;  // workspace: per-row masked count
+};
+
+// NaN-first argmin order of ATen min(1).
+__device__ __forceinline__ bool min_better(float v, int64_t i, float bv, int64_t bi) {
+  const bool vn = v != v, bn = bv != bv;
+  if (vn != bn) return vn;
+  if (vn) return i < bi;
+  return v < bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(kT) masked_diffusion_kernel(MaskedParams p) {
+  __shared__ int64_t s_cnt[kWarps];
+  __shared__ float s_min[kWarps];
+  __shared__ int64_t s_idx[kWarps];
+  const int64_t row = blockIdx.x;
+  const int64_t base = row * p.tokens;
+  // ratio = float32(float32(r * span) + lo) (ops.cpp:424-425)
+  const float r = __fadd_rn(__fmul_rn(p.ratio_random[row], p.span), p.lo);
+  int64_t cnt = 0;
+  float bv = __int_as_float(0x7f800000);  // +inf
+  int64_t bi = LLONG_MAX;
+  for (int64_t t = threadIdx.x; t < p.tokens; t += kT) {
+    const float u = p.mask_random[base + t];
+    const bool m = u < r;  // ops.cpp:426
+    p.masked[base + t] = m;
+    p.corrupted[base + t] = m ? p.mask_id : p.clean[base + t];
+    cnt += m;
+    if (bi == LLONG_MAX || min_better(u, t, bv, bi)) {
+      bv = u;
+      bi = t;
+    }
+  }
+  // block reductions (count; NaN-first argmin)
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    cnt += __shfl_down_sync(0xffffffffu, cnt, d);
+    const float ov = __shfl_down_sync(0xffffffffu, bv, d);
+    const int64_t oi = __shfl_down_sync(0xffffffffu, bi, d);
+    if (oi != LLONG_MAX && (bi == LLONG_MAX || min_better(ov, oi, bv, bi))) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    s_cnt[warp] = cnt;
+    s_min[warp] = bv;
+    s_idx[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t total = 0;
+    float mv = s_min[0];
+    int64_t mi = s_idx[0];
+    for (int w = 0; w < kWarps; ++w) {
+      total += s_cnt[w];
+      if (s_idx[w] != LLONG_MAX && (mi == LLONG_MAX || min_better(s_min[w], s_idx[w], mv, mi))) {
+        mv = s_min[w];
+        mi = s_idx[w];
+      }
+    }
+    if (total == 0) {  // ops.cpp:431-438 empty-row fallback
+      p.masked[base + mi] = 1;
+      p.corrupted[base + mi] = p.mask_id;
+      total = 1;
+    }
+    p.ratio[row] = r;
+    p.counts[row] = total;
+  }
+}
+
+// metrics = [mean(masked), mean(ratio)] (ops.cpp:441-442), fixed-order sums.
+__global__ void __launch_bounds__(kT) masked_metrics_kernel(const int64_t* counts,
+                                                            const float* ratio, int64_t batch,
+                                                            int64_t tokens, float* metrics) {
+  __shared__ int64_t s_c[kWarps];
+  __shared__ double s_r[kWarps];
+  int64_t c = 0;
+  double rs = 0.0;
+  for (int64_t b = threadIdx.x; b < batch; b += kT) {
+    c += counts[b];
+    rs += static_cast<double>(ratio[b]);
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    c += __shfl_down_sync(0xffffffffu, c, d);
+    rs += __shfl_down_sync(0xffffffffu, rs, d);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    s_c[threadIdx.x >> 5] = c;
+    s_r[threadIdx.x >> 5] = rs;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t tc = 0;
+    double tr = 0.0;
+    for (int w = 0; w < kWarps; ++w) {
+      tc += s_c[w];
+      tr += s_r[w];
+    }
+    metrics[0] = static_cast<float>(static_cast<double>(tc) / static_cast<double>(batch * tokens));
+    metrics[1] = static_cast<float>(tr / static_cast<double>(batch));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// thought corruption
+// ---------------------------------------------------------------------------
+
+struct ThoughtParams {
+  cid_dtype_t sdt;  // semantic dtype
+  const void* sem;
+  cid_dtype_t tdt;
+  const void* ts;
+  cid_dtype_t odt;
+  const void* occ;
+  const void* eps;
+  int64_t rows, hidden;
+  void* corrupted;
+  void* local_noise;
+  void* masked_eps;
+};
+
+// alpha = cos(t * pi/2)^2 evaluated in the timestep dtype (ops.cpp:277-281),
+// returned in double (exact for every storage dtype).
+__device__ double thought_alpha(cid_dtype_t tdt, const void* ts, int64_t row) {
+  const double half_pi = 1.57079632679489661923;
+  if (tdt == CID_DTYPE_F64) {
+    const double t = static_cast<const double*>(ts)[row];
+    const double c = cos(__dmul_rn(t, half_pi));
+    return __dmul_rn(c, c);
+  }
+  const float t = load_float(tdt, ts, row);
+  const float arg = round_to(tdt, __fmul_rn(t, static_cast<float>(half_pi)));
+  const float c = round_to(tdt, static_cast<float>(cos(static_cast<double>(arg))));
+  return static_cast<double>(round_to(tdt, __fmul_rn(c, c)));
+}
+
+__global__ void __launch_bounds__(kT) thought_kernel(ThoughtParams p) {
+  const int64_t row = blockIdx.x;
+  const bool occ = load_truthy(p.odt, p.occ, row);
+  const int64_t base = row * p.hidden;
+  if (p.sdt == CID_DTYPE_F64) {
+    const double* x = static_cast<const double*>(p.sem);
+    const double* e = static_cast<const double*>(p.eps);
+    double* out = static_cast<double*>(p.corrupted);
+    double* me = static_cast<double*>(p.masked_eps);
+    const double a = thought_alpha(p.tdt, p.ts, row);  // .to(float64) is exact
+    const double sa = __dsqrt_rn(a), sb = __dsqrt_rn(__dsub_rn(1.0, a));
+    for (int64_t h = threadIdx.x; h < p.hidden; h += kT) {
+      const double ev = e[base + h];
+      out[base + h] = occ ? __dadd_rn(__dmul_rn(sa, x[base + h]), __dmul_rn(sb, ev)) : 0.0;
+      me[base + h] = occ ? ev : 0.0;
+    }
+    if (threadIdx.x == 0)
+      static_cast<double*>(p.local_noise)[row] = occ ? load_double(p.tdt, p.ts, row) : 0.0;
+    return;
+  }
+  // float32 / float16 / bfloat16 semantic: float arithmetic rounded per op
+  const cid_dtype_t S = p.sdt;
+  const float a = round_to(S, static_cast<float>(thought_alpha(p.tdt, p.ts, row)));
+  const float sa = round_to(S, __fsqrt_rn(a));
+  const float sb = round_to(S, __fsqrt_rn(round_to(S, __fsub_rn(1.0f, a))));
+  for (int64_t h = threadIdx.x; h < p.hidden; h += kT) {
+    const float x = load_float(S, p.sem, base + h);
+    const float ev = load_float(S, p.eps, base + h);
+    const float v = round_to(S, __fadd_rn(round_to(S, __fmul_rn(sa, x)), round_to(S, __fmul_rn(sb, ev))));
+    store_float(S, p.corrupted, base + h, occ ? v : 0.0f);
+    store_float(S, p.masked_eps, base + h, occ ? ev : 0.0f);
+  }
+  if (threadIdx.x == 0) {
+    const float t = p.tdt == CID_DTYPE_F64 ? static_cast<float>(static_cast<const double*>(p.ts)[row])
+                                           : load_float(p.tdt, p.ts, row);
+    store_float(S, p.local_noise, row, occ ? t : 0.0f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// display corruption
+// ---------------------------------------------------------------------------
+
+struct DisplayCorruptParams {
+  const int64_t* ids;
+  cid_dtype_t tdt;
+  const void* ts;
+  cid_dtype_t edt;
+  const void* elig;
+  cid_dtype_t rdt;
+  const void* crand;
+  cid_dtype_t pdt;
+  const void* rrand;
+  const int64_t* roff;
+  int64_t batch, tokens, mask_id, eos_id, vocab;
+  int has_eos;
+  int replace;
+  float repl_thr;
+  int64_t* corrupted;
+  int64_t* labels;
+  uint8_t* masked;
+  uint8_t* replaced;
+};
+
+__device__ __forceinline__ int64_t floor_mod(int64_t a, int64_t m) {
+  const int64_t r = a % m;
+  return (r != 0 && ((r < 0) != (m < 0))) ? r + m : r;
+}
+
+__global__ void __launch_bounds__(kT) display_corrupt_kernel(DisplayCorruptParams p) {
+  __shared__ int s_any[kWarps];
+  __shared__ int64_t s_first[kWarps];
+  const int64_t row = blockIdx.x;
+  const int64_t base = row * p.tokens;
+  const float t = load_float(p.tdt, p.ts, row);  // timesteps.to(float)
+  int any_corrupt = 0;
+  int64_t first_elig = LLONG_MAX;
+  for (int64_t k = threadIdx.x; k < p.tokens; k += kT) {
+    const bool el = load_truthy(p.edt, p.elig, base + k);
+    const float u = load_float(p.rdt, p.crand, base + k);
+    any_corrupt |= (u < t) && el;  // ops.cpp:326-328
+    if (el && k < first_elig) first_elig = k;
+  }
+  any_corrupt = __syncthreads_or(any_corrupt);
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) first_elig = min(first_elig, __shfl_down_sync(0xffffffffu, first_elig, d));
+  if ((threadIdx.x & 31) == 0) s_first[threadIdx.x >> 5] = first_elig;
+  __syncthreads();
+  int64_t fe = s_first[0];
+  for (int w = 1; w < kWarps; ++w) fe = min(fe, s_first[w]);
+  // ops.cpp:330-337 first-eligible fallback
+  const int64_t fallback = (!any_corrupt && t > 0.0f && fe != LLONG_MAX) ? fe : -1;
+  (void)s_any;
+  for (int64_t k = threadIdx.x; k < p.tokens; k += kT) {
+    const int64_t i = base + k;
+    const bool el = load_truthy(p.edt, p.elig, i);
+    const float u = load_float(p.rdt, p.crand, i);
+    const bool pos = ((u < t) && el) || k == fallback;
+    const int64_t id = p.ids[i];
+    bool rep = false;
+    int64_t value = id;
+    if (p.replace) {
+      rep = pos && (load_float(p.pdt, p.rrand, i) < p.repl_thr);  // ops.cpp:362-363
+      int64_t cand = floor_mod(id + p.roff[i], p.vocab);             // ops.cpp:364-365
+      for (int it = 0; it < 3; ++it) {                               // ops.cpp:366-376
+        const bool forbidden = cand == p.mask_id || cand == id || (p.has_eos && cand == p.eos_id);
+        if (forbidden) cand = floor_mod(cand + 1, p.vocab);
+      }
+      if (rep) value = cand;
+    }
+    const bool msk = pos && !rep;
+    if (msk) value = p.mask_id;
+    p.corrupted[i] = value;
+    p.labels[i] = pos ? id : -100;  // ops.cpp:386-389
+    p.masked[i] = msk;
+    p.replaced[i] = rep;
+  }
+}
+
+}  // namespace
+}  // namespace cid
+
+using namespace cid;
+
+extern "C" size_t cid_masked_diffusion_workspace_bytes(int64_t batch) {
+  return batch > 0 ? static_cast<size_t>(batch) * sizeof(int64_t) : 0;
+}
+
+extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const float* ratio_random,
+                                            const float* mask_random, int64_t batch,
+                                            int64_t tokens, int64_t mask_token_id,
+                                            double min_mask_ratio, double max_mask_ratio,
+                                            int64_t* corrupted, uint8_t* masked, float* ratio,
+                                            float* metrics, void* workspace, void* stream) {
+  if (batch <= 0 || tokens <= 0 || batch > INT_MAX) return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:406
+  if (!(min_mask_ratio > 0.0 && min_mask_ratio <= max_mask_ratio && max_mask_ratio <= 1.0))
+    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:416-420
+  if (!clean_ids || !ratio_random || !mask_random || !corrupted || !masked || !ratio ||
+      !metrics || !workspace)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0) return CID_ERR_MISALIGNED;
+  MaskedParams p;
+  p.clean = clean_ids;
+  p.ratio_random = ratio_random;
+  p.mask_random = mask_random;
+  p.batch = batch;
+  p.tokens = tokens;
+  p.mask_id = mask_token_id;
+  p.span = static_cast<float>(max_mask_ratio - min_mask_ratio);
+  p.lo = static_cast<float>(min_mask_ratio);
+  p.corrupted = corrupted;
+  p.masked = masked;
+  p.ratio = ratio;
+  p.metrics = metrics;
+  p.counts = static_cast<int64_t*>(workspace);
+  cudaStream_t s = as_stream(stream);
+  masked_diffusion_kernel<<<static_cast<unsigned>(batch), kT, 0, s>>>(p);
+  int rc = launch_result();
+  if (rc != CID_OK) return rc;
+  masked_metrics_kernel<<<1, kT, 0, s>>>(p.counts, ratio, batch, tokens, metrics);
+  return launch_result();
+}
+
+extern "C" int cid_thought_corrupt(cid_dtype_t sem_dtype, const void* semantic,
+                                   cid_dtype_t t_dtype, const void* timesteps,
+                                   cid_dtype_t occ_dtype, const void* occupancy,
+                                   const void* epsilon, int64_t rows, int64_t hidden,
+                                   void* corrupted, void* local_noise, void* masked_epsilon,
+                                   void* stream) {
+  if (!is_float_dtype(sem_dtype) || !is_float_dtype(t_dtype) || !is_known_dtype(occ_dtype))
+    return CID_ERR_UNSUPPORTED_DTYPE;
+  if (rows < 0 || hidden < 0 || rows > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return CID_OK;
+  ThoughtParams p{sem_dtype, semantic, t_dtype, timesteps, occ_dtype, occupancy, epsilon,
+                  rows, hidden, corrupted, local_noise, masked_epsilon};
+  thought_kernel<<<static_cast<unsigned>(rows), kT, 0, as_stream(stream)>>>(p);
+  return launch_result();
+}
+
+extern "C" int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype,
+                                   const void* timesteps, cid_dtype_t elig_dtype,
+                                   const void* eligible, cid_dtype_t rand_dtype,
+                                   const void* corruption_random, cid_dtype_t repl_dtype,
+                                   const void* replacement_random,
+                                   const int64_t* replacement_offsets, int64_t batch,
+                                   int64_t tokens, int64_t mask_token_id, int has_eos,
+                                   int64_t eos_token_id, int64_t vocab_size,
+                                   double replacement_fraction, int64_t* corrupted,
+                                   int64_t* labels, uint8_t* masked, uint8_t* replaced,
+                                   void* stream) {
+  if (!(replacement_fraction >= 0.0 && replacement_fraction <= 1.0))
+    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:320-322
+  const int replace = replacement_fraction > 0.0;
+  if (replace && (vocab_size < 3 || !replacement_random || !replacement_offsets))
+    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:343-348
+  if (!is_float_dtype(t_dtype) || !is_known_dtype(elig_dtype) || !is_float_dtype(rand_dtype) ||
+      (replace && !is_float_dtype(repl_dtype)))
+    return CID_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || tokens < 0 || batch > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || tokens == 0) return CID_OK;
+  DisplayCorruptParams p{token_ids, t_dtype, timesteps, elig_dtype, eligible, rand_dtype,
+                         corruption_random, repl_dtype, replacement_random,
+                         replacement_offsets, batch, tokens, mask_token_id, eos_token_id,
+                         vocab_size, has_eos, replace,
+                         static_cast<float>(replacement_fraction), corrupted, labels, masked,
+                         replaced};
+  display_corrupt_kernel<<<static_cast<unsigned>(batch), kT, 0, as_stream(stream)>>>(p);
+  return launch_result();
+}

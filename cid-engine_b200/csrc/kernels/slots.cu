@@ -1,0 +1,243 @@
+// Thought-slot state kernels: first-free prefix allocation, the rollout slot
+// transition and live occupancy.  One warp per batch row: slot decisions are
+// made 32 at a time with warp ballots (first blocking slot = first set bit,
+// allocation rank = popcount prefix), so a row of S slots takes ceil(S/32)
+// steps instead of the reference kernel's single-thread scan
+// (csrc/cuda/prefix_allocation.cu:14-49 of fwerkor/cid-engine v1.1.0).
+#include <climits>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace cid {
+namespace {
+
+constexpr int kWarpsPerBlock = 4;
+
+__device__ __forceinline__ unsigned lanemask_le() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_le;" : "=r"(m));
+  return m;
+}
+
+// ATen max(-1) index over n values of `dt` starting at element `base`:
+// first NaN, else first maximum (compared in double, exact for every dtype).
+__device__ __forceinline__ int64_t argmax_first(cid_dtype_t dt, const void* p, int64_t base,
+                                                int64_t n) {
+  double bv = load_double(dt, p, base);
+  int64_t bi = 0;
+  for (int64_t k = 1; k < n; ++k) {
+    if (bv != bv) break;
+    const double v = load_double(dt, p, base + k);
+    if (v != v || v > bv) {
+      bv = v;
+      bi = k;
+    }
+  }
+  return bi;
+}
+
+// Shared warp-level prefix allocation over one row, 32 slots per step
+// (semantics of csrc/ops.cpp:41-65).  occ(s) -> bool, logit(s) -> float;
+// emit(s, selected) is called for every slot s < slots by lane s % 32.
+template <typename Occ, typename Logit, typename Emit>
+__device__ __forceinline__ void warp_prefix_allocation(int64_t slots, float thr,
+                                                       int64_t max_allocations, Occ occ,
+                                                       Logit logit, Emit emit) {
+  const int lane = threadIdx.x & 31;
+  int64_t rank = 0;
+  bool blocked = false;
+  for (int64_t s0 = 0; s0 < slots; s0 += 32) {
+    const int64_t s = s0 + lane;
+    const bool in = s < slots;
+    const bool occupied = in && occ(s);
+    const bool is_free = in && !occupied;
+    bool elig = false;
+    if (is_free && !blocked) elig = sigmoid_f32(logit(s)) >= thr;  // ops.cpp:59
+    // blocked = cumsum(free & !eligible) > 0, the blocking slot included
+    const unsigned bl = __ballot_sync(0xffffffffu, is_free && !elig);
+    const int first_block = bl ? __ffs(bl) - 1 : 32;
+    const bool sel = !blocked && is_free && elig && lane < first_block;
+    const unsigned sm = __ballot_sync(0xffffffffu, sel);
+    const int64_t r = rank + __popc(sm & lanemask_le());
+    if (in) emit(s, sel && r <= max_allocations);  // ops.cpp:63-64
+    rank += __popc(sm);
+    if (bl) blocked = true;
+  }
+}
+
+struct PrefixParams {
+  cid_dtype_t occ_dtype;
+  const void* occ;
+  int64_t ors, ocs;
+  cid_dtype_t logit_dtype;
+  const void* logits;
+  int64_t lrs, lcs;
+  int64_t batch, slots;
+  float thr;
+  int64_t max_alloc;
+  uint8_t* out;
+};
+
+__global__ void prefix_allocation_kernel(PrefixParams p) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= p.batch) return;
+  warp_prefix_allocation(
+      p.slots, p.thr, p.max_alloc,
+      [&](int64_t s) { return load_truthy(p.occ_dtype, p.occ, row * p.ors + s * p.ocs); },
+      [&](int64_t s) { return load_float(p.logit_dtype, p.logits, row * p.lrs + s * p.lcs); },
+      [&](int64_t s, bool v) { p.out[row * p.slots + s] = v; });
+}
+
+struct RolloutParams {
+  cid_dtype_t occ_dtype;
+  const void* occ;
+  cid_dtype_t dtype;
+  const void* alloc;
+  const void* life;
+  const void* rev;
+  const void* in_life;
+  int64_t batch, slots, F, Rv;
+  float thr;
+  int64_t max_alloc, retired;
+  uint8_t* next;
+  int64_t* life_idx;
+  int64_t* rev_idx;
+  int64_t* in_idx;
+  uint8_t* present;
+  uint8_t* live;
+};
+
+// csrc/ops.cpp:184-256 fused into one pass per row.
+__global__ void rollout_kernel(RolloutParams p) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
+  if (row >= p.batch) return;
+  const int64_t base = row * p.slots;
+  warp_prefix_allocation(
+      p.slots, p.thr, p.max_alloc,
+      [&](int64_t s) { return load_truthy(p.occ_dtype, p.occ, base + s); },
+      [&](int64_t s) { return load_float(p.dtype, p.alloc, base + s); },
+      [&](int64_t s, bool alloc) {
+        const int64_t i = base + s;
+        const bool occ = load_truthy(p.occ_dtype, p.occ, i);
+        const bool nxt = occ || alloc;
+        const int64_t li = argmax_first(p.dtype, p.life, i * p.F, p.F);
+        const int64_t ri = argmax_first(p.dtype, p.rev, i * p.Rv, p.Rv);
+        const int64_t ii = argmax_first(p.dtype, p.in_life, i * p.F, p.F);
+        bool present = false;  // abs().sum(-1).ne(0): any non-zero (NaN included)
+        for (int64_t k = 0; k < p.F; ++k) present = present || load_truthy(p.dtype, p.in_life, i * p.F + k);
+        const bool prev_retired = occ && ii == p.retired;
+        const bool newly = nxt && !occ;
+        const bool pred_retired = li == p.retired;
+        p.next[i] = nxt;
+        p.life_idx[i] = li;
+        p.rev_idx[i] = ri;
+        p.in_idx[i] = ii;
+        p.present[i] = present;
+        p.live[i] = nxt && !prev_retired && (!pred_retired || newly);
+      });
+}
+
+struct LiveParams {
+  cid_dtype_t dtype;
+  const void* occ;
+  const void* life;
+  int64_t rows, F, retired;
+  void* out;
+};
+
+__device__ __forceinline__ float clamp01f(float x) { return x != x ? x : fminf(fmaxf(x, 0.0f), 1.0f); }
+__device__ __forceinline__ double clamp01d(double x) { return x != x ? x : fmin(fmax(x, 0.0), 1.0); }
+
+// csrc/ops.cpp:12-39: clamp(occ, 0, 1) * (1 - clamp(lifecycle[..., r], 0, 1)),
+// each op rounded to the storage dtype.
+__global__ void live_kernel(LiveParams p) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < p.rows;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (p.dtype == CID_DTYPE_F64) {
+      const double o = clamp01d(static_cast<const double*>(p.occ)[i]);
+      double v = o;
+      if (p.life) {
+        const double r = clamp01d(static_cast<const double*>(p.life)[i * p.F + p.retired]);
+        v = __dmul_rn(o, __dsub_rn(1.0, r));
+      }
+      static_cast<double*>(p.out)[i] = v;
+    } else {
+      const float o = clamp01f(load_float(p.dtype, p.occ, i));
+      float v = o;
+      if (p.life) {
+        const float r = clamp01f(load_float(p.dtype, p.life, i * p.F + p.retired));
+        const float keep = round_to(p.dtype, __fsub_rn(1.0f, r));
+        v = __fmul_rn(o, keep);
+      }
+      store_float(p.dtype, p.out, i, v);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace cid
+
+using namespace cid;
+
+extern "C" int cid_prefix_allocation_mask(cid_dtype_t occ_dtype, const void* occupancy,
+                                          int64_t occ_row_stride, int64_t occ_col_stride,
+                                          cid_dtype_t logit_dtype, const void* logits,
+                                          int64_t logit_row_stride, int64_t logit_col_stride,
+                                          int64_t batch, int64_t slots, double threshold,
+                                          int64_t max_allocations, uint8_t* out, void* stream) {
+  if (!(threshold >= 0.0 && threshold <= 1.0)) return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:50
+  if (max_allocations <= 0) return CID_ERR_INVALID_ARGUMENT;                      // ops.cpp:51
+  if (!is_known_dtype(occ_dtype) || !is_float_dtype(logit_dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || slots < 0) return CID_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || slots == 0) return CID_OK;
+  if (!occupancy || !logits || !out) return CID_ERR_INVALID_ARGUMENT;
+  PrefixParams p{occ_dtype, occupancy, occ_row_stride, occ_col_stride, logit_dtype, logits,
+                 logit_row_stride, logit_col_stride, batch, slots,
+                 static_cast<float>(threshold), max_allocations, out};
+  const int64_t blocks = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  prefix_allocation_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0,
+                             as_stream(stream)>>>(p);
+  return launch_result();
+}
+
+extern "C" int cid_rollout_slot_transition(
+    cid_dtype_t occ_dtype, const void* occupancy, cid_dtype_t dtype,
+    const void* allocation_logits, const void* lifecycle_logits, const void* revision_logits,
+    const void* input_lifecycle, int64_t batch, int64_t slots, int64_t lifecycles,
+    int64_t revisions, double threshold, int64_t max_allocations, int64_t retired_index,
+    uint8_t* next_occupancy, int64_t* lifecycle_indices, int64_t* revision_indices,
+    int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present, uint8_t* live_slots,
+    void* stream) {
+  if (retired_index < 0 || retired_index >= lifecycles) return CID_ERR_INVALID_ARGUMENT;
+  if (!(threshold >= 0.0 && threshold <= 1.0)) return CID_ERR_INVALID_ARGUMENT;
+  if (max_allocations <= 0 || revisions <= 0) return CID_ERR_INVALID_ARGUMENT;
+  if (!is_known_dtype(occ_dtype) || !is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || slots < 0) return CID_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || slots == 0) return CID_OK;
+  RolloutParams p{occ_dtype, occupancy, dtype, allocation_logits, lifecycle_logits,
+                  revision_logits, input_lifecycle, batch, slots, lifecycles, revisions,
+                  static_cast<float>(threshold), max_allocations, retired_index,
+                  next_occupancy, lifecycle_indices, revision_indices, input_lifecycle_indices,
+                  input_lifecycle_present, live_slots};
+  const int64_t blocks = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  rollout_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, as_stream(stream)>>>(p);
+  return launch_result();
+}
+
+extern "C" int cid_live_slot_occupancy(cid_dtype_t dtype, const void* occupancy,
+                                       const void* lifecycle, int64_t rows, int64_t features,
+                                       int64_t retired_index, void* out, void* stream) {
+  if (!is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
+  if (lifecycle && (retired_index < 0 || retired_index >= features))
+    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:31-33
+  if (rows < 0) return CID_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return CID_OK;
+  if (!occupancy || !out) return CID_ERR_INVALID_ARGUMENT;
+  LiveParams p{dtype, occupancy, lifecycle, rows, features, retired_index, out};
+  const int threads = 256;
+  int64_t blocks = (rows + threads - 1) / threads;
+  if (blocks > 4096) blocks = 4096;
+  live_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(p);
+  return launch_result();
+}

@@ -1,0 +1,264 @@
+/*
+ * cid_engine_b200.h — C ABI of the B200 (sm_100a) display-refinement kernels.
+ *
+ * Plain pointers, sizes and enums; no torch or C++ types.  Every entry point
+ * is asynchronous: it validates its arguments on the host, enqueues its
+ * kernel(s) on `stream` (a cudaStream_t passed as void*, NULL = legacy default
+ * stream) for the device that is current on the calling thread, and returns
+ * a cid_result_t.  Device pointers must belong to that device.
+ *
+ * Each entry point replaces one reference operator (fwerkor/cid-engine
+ * v1.1.0); the reference interface is cited beside it.  Argument meaning and
+ * output semantics are those of the reference CPU backend.
+ *
+ * Device-side status.  Conditions that the reference CPU backend turns into
+ * exceptions but that a device kernel cannot raise without a host sync (an
+ * out-of-range token id, a snapshot index outside the semantic width) are
+ * reported by OR-ing CID_STATUS_* bits into an optional device word
+ * `status` (may be NULL); the affected outputs are written as NaN (floats)
+ * and no out-of-bounds access is made.
+ */
+#ifndef CID_ENGINE_B200_H
+#define CID_ENGINE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CID_API __attribute__((visibility("default")))
+#else
+#define CID_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CID_ENGINE_B200_ABI_VERSION 1
+
+typedef enum cid_dtype {
+  CID_DTYPE_F32 = 0,
+  CID_DTYPE_F64 = 1,
+  CID_DTYPE_F16 = 2,
+  CID_DTYPE_BF16 = 3,
+  CID_DTYPE_BOOL = 4,
+  CID_DTYPE_I64 = 5,
+  CID_DTYPE_I32 = 6,
+  CID_DTYPE_U8 = 7,
+  CID_DTYPE_I8 = 8,
+  CID_DTYPE_I16 = 9
+} cid_dtype_t;
+
+typedef enum cid_result {
+  CID_OK = 0,
+  CID_ERR_INVALID_ARGUMENT = 1,
+  CID_ERR_UNSUPPORTED_DTYPE = 2,
+  CID_ERR_LAUNCH = 3,
+  CID_ERR_MISALIGNED = 4,
+  CID_ERR_CUDA = 5
+} cid_result_t;
+
+/* Bits OR-ed into the optional device status word. */
+#define CID_STATUS_TOKEN_ID_OUT_OF_RANGE 0x1u
+#define CID_STATUS_SEMANTIC_INDEX_OUT_OF_RANGE 0x2u
+#define CID_STATUS_REPETITION_ID_OUT_OF_RANGE 0x4u
+
+CID_API int cid_abi_version(void);
+CID_API const char* cid_result_string(int result);
+/* Message of the last CUDA error seen by this thread inside the library. */
+CID_API const char* cid_last_cuda_error(void);
+
+/* ---------------------------------------------------------------------- */
+/* Display statistics                                                      */
+/* ---------------------------------------------------------------------- */
+
+/* display_token_statistics — replaces
+ *   csrc/registration.cpp:33-35 (schema), csrc/cpu/display_stats.cpp:54-126
+ *   (CPU semantics), csrc/cuda/display_stats.cu:168-220 (CUDA launcher).
+ * logits: rows x vocab of `dtype` (F32/F64/F16/BF16), row r at
+ *   logits + r*row_stride elements, unit stride along the vocabulary.
+ * Outputs per row: confidence = max softmax probability, predicted = argmax
+ *   (first NaN, else lowest index of the maximum), current_confidence =
+ *   softmax probability of token_ids[r].  rows may be 0. */
+CID_API int cid_display_token_statistics(cid_dtype_t dtype, const void* logits,
+                                 int64_t row_stride, const int64_t* token_ids,
+                                 int64_t rows, int64_t vocab, float* confidence,
+                                 int64_t* predicted, float* current_confidence,
+                                 uint32_t* status, void* stream);
+
+/* display_token_statistics_with_repetition — replaces
+ *   csrc/registration.cpp:36-39, csrc/ops.cpp:477-552,
+ *   csrc/cuda/display_stats.cu:222-283.
+ * token_ids/logits as above with rows = batch*tokens (row b*tokens+p).
+ * has_eos = 0 means eos_token_id is None.  multiplier in (0, 1]. */
+CID_API int cid_display_token_statistics_with_repetition(
+    cid_dtype_t dtype, const void* logits, int64_t row_stride,
+    const int64_t* token_ids, int64_t batch, int64_t tokens, int64_t vocab,
+    int64_t mask_token_id, int has_eos, int64_t eos_token_id,
+    double multiplier, float* confidence, int64_t* predicted,
+    float* current_confidence, uint32_t* status, void* stream);
+
+/* Vocabulary-parallel statistics.  A rank holding columns
+ * [vocab_offset, vocab_offset + shard_vocab) of a total_vocab-wide row
+ * writes one 16-byte record per row; the records of all ranks (gathered in
+ * rank order, ranks holding ascending contiguous ranges) are merged by
+ * cid_display_combine_records into the unsharded statistics.  This is the
+ * multi-GPU form of display_token_statistics (no reference counterpart
+ * beyond the operator it decomposes). */
+typedef struct cid_shard_record {
+  float max_logit;   /* shard maximum (ignores NaN) */
+  float sum_exp;     /* sum over the shard of exp(x - max_logit) */
+  int32_t index;     /* global column of the first maximum; bit 31 set
+                        when the shard holds a NaN, the low bits then give
+                        the global column of its first NaN */
+  float current;     /* logit of token_ids[r] when this shard owns it */
+} cid_shard_record_t;
+
+CID_API int cid_display_shard_records(cid_dtype_t dtype, const void* logits,
+                              int64_t row_stride, const int64_t* token_ids,
+                              int64_t rows, int64_t shard_vocab,
+                              int64_t vocab_offset, int64_t total_vocab,
+                              cid_shard_record_t* records, uint32_t* status,
+                              void* stream);
+
+/* records: world x rows (rank-major).  shard_offsets: world+1 ascending
+ * column offsets on the HOST (shard r owns [offsets[r], offsets[r+1])). */
+CID_API int cid_display_combine_records(const cid_shard_record_t* records, int world,
+                                const int64_t* shard_offsets_host,
+                                const int64_t* token_ids, int64_t rows,
+                                float* confidence, int64_t* predicted,
+                                float* current_confidence, uint32_t* status,
+                                void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Refinement policy                                                       */
+/* ---------------------------------------------------------------------- */
+
+/* refine_display_from_statistics — replaces csrc/registration.cpp:40-44 and
+ * csrc/refine.cpp:222-429 (which copies to the host and back every call);
+ * here one CTA per row runs the whole policy on the device.
+ * All arrays batch x tokens, contiguous. `out` must not alias the inputs. */
+CID_API int cid_refine_display(const int64_t* token_ids, const float* confidence,
+                       const int64_t* predicted,
+                       const float* current_confidence, int64_t batch,
+                       int64_t tokens, int64_t mask_token_id, int has_eos,
+                       int64_t eos_token_id, double reveal_fraction,
+                       double revision_fraction, double revision_margin,
+                       int64_t* out, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Thought-slot state                                                      */
+/* ---------------------------------------------------------------------- */
+
+/* prefix_allocation_mask — replaces csrc/registration.cpp:9-11,
+ * csrc/ops.cpp:41-65, csrc/cuda/prefix_allocation.cu:81-132.
+ * occupancy: batch x slots of occ_dtype (any), element (b,s) at
+ *   occupancy + b*occ_row_stride + s*occ_col_stride;
+ * logits: same shape of logit_dtype (F32/F64/F16/BF16), strided likewise;
+ * out: batch x slots bool (uint8), contiguous. */
+CID_API int cid_prefix_allocation_mask(cid_dtype_t occ_dtype, const void* occupancy,
+                               int64_t occ_row_stride, int64_t occ_col_stride,
+                               cid_dtype_t logit_dtype, const void* logits,
+                               int64_t logit_row_stride,
+                               int64_t logit_col_stride, int64_t batch,
+                               int64_t slots, double threshold,
+                               int64_t max_allocations, uint8_t* out,
+                               void* stream);
+
+/* rollout_slot_transition — replaces csrc/registration.cpp:14-18,
+ * csrc/ops.cpp:184-256, csrc/cuda/rollout_state.cu:134-281.
+ * allocation_logits (batch x slots), lifecycle_logits and input_lifecycle
+ * (batch x slots x lifecycles), revision_logits (batch x slots x revisions):
+ * contiguous, all of `dtype`.  Outputs contiguous batch x slots. */
+CID_API int cid_rollout_slot_transition(
+    cid_dtype_t occ_dtype, const void* occupancy, cid_dtype_t dtype,
+    const void* allocation_logits, const void* lifecycle_logits,
+    const void* revision_logits, const void* input_lifecycle, int64_t batch,
+    int64_t slots, int64_t lifecycles, int64_t revisions, double threshold,
+    int64_t max_allocations, int64_t retired_index, uint8_t* next_occupancy,
+    int64_t* lifecycle_indices, int64_t* revision_indices,
+    int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present,
+    uint8_t* live_slots, void* stream);
+
+/* live_slot_occupancy — replaces csrc/registration.cpp:6-8 and
+ * csrc/ops.cpp:12-39.  occupancy: rows (= batch*slots) of `dtype`;
+ * lifecycle: rows x features of `dtype` or NULL; out: rows of `dtype`. */
+CID_API int cid_live_slot_occupancy(cid_dtype_t dtype, const void* occupancy,
+                            const void* lifecycle, int64_t rows,
+                            int64_t features, int64_t retired_index, void* out,
+                            void* stream);
+
+/* materialize_cell_snapshot — replaces csrc/registration.cpp:45-48,
+ * csrc/ops.cpp:556-615, csrc/cuda/materialize_snapshot.cu:71-184.
+ * rows = batch*slots; every input contiguous with its own dtype; selected
+ * bool; indices int64 on the device; out rows x (4+roles+nindices) f32. */
+CID_API int cid_materialize_cell_snapshot(
+    cid_dtype_t sem_dtype, const void* semantic, int64_t hidden,
+    cid_dtype_t role_dtype, const void* roles, int64_t nroles,
+    cid_dtype_t unc_dtype, const void* uncertainty, cid_dtype_t noise_dtype,
+    const void* noise_delta, cid_dtype_t life_dtype, const void* lifecycle,
+    int64_t lifecycles, const uint8_t* selected, const int64_t* indices,
+    int64_t nindices, int64_t rows, float* out, uint32_t* status,
+    void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Training corruption                                                     */
+/* ---------------------------------------------------------------------- */
+
+/* Scratch bytes cid_masked_diffusion_corrupt needs in `workspace`. */
+CID_API size_t cid_masked_diffusion_workspace_bytes(int64_t batch);
+
+/* masked_diffusion_corrupt_from_random — replaces
+ * csrc/registration.cpp:28-32, csrc/ops.cpp:394-444,
+ * csrc/cuda/masked_diffusion.cu:100-170.
+ * clean_ids batch x tokens int64; ratio_random batch (F32); mask_random
+ * batch x tokens (F32); outputs corrupted (int64), masked (bool), ratio
+ * (batch f32), metrics (2 f32: mean mask, mean ratio; summed in a fixed
+ * order, so repeated calls give identical metrics).  workspace: device
+ * scratch of cid_masked_diffusion_workspace_bytes(batch) bytes, 16-byte
+ * aligned, contents need not be initialised. */
+CID_API int cid_masked_diffusion_corrupt(const int64_t* clean_ids,
+                                 const float* ratio_random,
+                                 const float* mask_random, int64_t batch,
+                                 int64_t tokens, int64_t mask_token_id,
+                                 double min_mask_ratio, double max_mask_ratio,
+                                 int64_t* corrupted, uint8_t* masked,
+                                 float* ratio, float* metrics, void* workspace,
+                                 void* stream);
+
+/* thought_corrupt_from_epsilon — replaces csrc/registration.cpp:19-21,
+ * csrc/ops.cpp:258-290, csrc/cuda/thought_corruption.cu:72-157.
+ * semantic/epsilon/corrupted/masked_epsilon: rows x hidden of sem_dtype;
+ * timesteps: rows of t_dtype; occupancy: rows of occ_dtype; local_noise:
+ * rows of sem_dtype.  All contiguous. */
+CID_API int cid_thought_corrupt(cid_dtype_t sem_dtype, const void* semantic,
+                        cid_dtype_t t_dtype, const void* timesteps,
+                        cid_dtype_t occ_dtype, const void* occupancy,
+                        const void* epsilon, int64_t rows, int64_t hidden,
+                        void* corrupted, void* local_noise,
+                        void* masked_epsilon, void* stream);
+
+/* display_corrupt_from_random — replaces csrc/registration.cpp:22-27,
+ * csrc/ops.cpp:292-391, csrc/cuda/display_corruption.cu.
+ * token_ids batch x tokens int64; timesteps batch (t_dtype); eligible
+ * batch x tokens (elig_dtype); corruption_random and replacement_random
+ * batch x tokens (float dtypes; replacement_* may be NULL when
+ * replacement_fraction == 0); replacement_offsets int64.  Outputs int64
+ * corrupted and labels, bool masked and replaced. */
+CID_API int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype,
+                        const void* timesteps, cid_dtype_t elig_dtype,
+                        const void* eligible, cid_dtype_t rand_dtype,
+                        const void* corruption_random, cid_dtype_t repl_dtype,
+                        const void* replacement_random,
+                        const int64_t* replacement_offsets, int64_t batch,
+                        int64_t tokens, int64_t mask_token_id, int has_eos,
+                        int64_t eos_token_id, int64_t vocab_size,
+                        double replacement_fraction, int64_t* corrupted,
+                        int64_t* labels, uint8_t* masked, uint8_t* replaced,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CID_ENGINE_B200_H */

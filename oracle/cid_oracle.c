@@ -792,3 +792,107 @@ int cid_oracle_display_corrupt(const int64_t* ids, int t_dtype,
   }
   return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Vocabulary-sharded statistics: the decomposition of                       */
+/* display_token_statistics (csrc/cpu/display_stats.cpp:14-126) over         */
+/* contiguous column ranges.  Record layout as cid_shard_record_t.           */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  float max_logit;
+  float sum_exp;
+  int32_t index;
+  float current;
+} oracle_record_t;
+
+int cid_oracle_shard_records(int dtype, const void* logits, const int64_t* ids,
+                             int64_t rows, int64_t shard_vocab,
+                             int64_t vocab_offset, void* records_out) {
+  oracle_record_t* out = (oracle_record_t*)records_out;
+  if (shard_vocab <= 0) return -1;
+#pragma omp parallel
+  {
+    float* buf = (float*)malloc(sizeof(float) * (size_t)shard_vocab);
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      row_to_float(dtype, logits, r, shard_vocab, buf);
+      int64_t first_nan = -1, first_max = 0;
+      float m = -INFINITY;
+      int seen = 0;
+      for (int64_t v = 0; v < shard_vocab; ++v) {
+        float x = buf[v];
+        if (isnan(x)) {
+          if (first_nan < 0) first_nan = v;
+          continue;
+        }
+        if (!seen || x > m) {
+          m = x;
+          first_max = v;
+          seen = 1;
+        }
+      }
+      oracle_record_t rec;
+      rec.max_logit = m;
+      double s = 0.0;
+      if (isfinite(m))
+        for (int64_t v = 0; v < shard_vocab; ++v) s += exp((double)buf[v] - (double)m);
+      rec.sum_exp = first_nan >= 0 ? NAN : (m == -INFINITY ? 0.0f : (isfinite(m) ? (float)s : NAN));
+      rec.index = (int32_t)(vocab_offset + (first_nan >= 0 ? first_nan : first_max));
+      if (first_nan >= 0) rec.index |= (int32_t)0x80000000u;
+      int64_t local = ids[r] - vocab_offset;
+      rec.current = (local >= 0 && local < shard_vocab) ? buf[local] : 0.0f;
+      out[r] = rec;
+    }
+    free(buf);
+  }
+  return 0;
+}
+
+int cid_oracle_combine_records(const void* records_in, int world,
+                               const int64_t* offsets, const int64_t* ids,
+                               int64_t rows, float* confidence,
+                               int64_t* predicted, float* current) {
+  const oracle_record_t* rec = (const oracle_record_t*)records_in;
+  for (int64_t r = 0; r < rows; ++r) {
+    int done = 0;
+    for (int k = 0; k < world && !done; ++k) {
+      oracle_record_t x = rec[(int64_t)k * rows + r];
+      if (x.index < 0) { /* lowest rank holding a NaN: its first NaN */
+        predicted[r] = x.index & 0x7fffffff;
+        confidence[r] = NAN;
+        current[r] = NAN;
+        done = 1;
+      }
+    }
+    if (done) continue;
+    float M = -INFINITY;
+    int32_t idx = rec[r].index;
+    for (int k = 0; k < world; ++k) {
+      oracle_record_t x = rec[(int64_t)k * rows + r];
+      if (x.max_logit > M) {
+        M = x.max_logit;
+        idx = x.index;
+      }
+    }
+    predicted[r] = idx;
+    if (!isfinite(M)) {
+      confidence[r] = NAN;
+      current[r] = NAN;
+      continue;
+    }
+    double S = 0.0;
+    for (int k = 0; k < world; ++k) {
+      oracle_record_t x = rec[(int64_t)k * rows + r];
+      if (x.max_logit == -INFINITY) continue;
+      S += (double)x.sum_exp * exp((double)x.max_logit - (double)M);
+    }
+    int owner = -1;
+    for (int k = 0; k < world; ++k)
+      if (ids[r] >= offsets[k] && ids[r] < offsets[k + 1]) owner = k;
+    confidence[r] = (float)(1.0 / S);
+    current[r] = owner < 0 ? NAN
+                           : (float)(exp((double)rec[(int64_t)owner * rows + r].current - (double)M) / S);
+  }
+  return 0;
+}

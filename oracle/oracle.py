@@ -297,3 +297,34 @@ def display_corrupt_from_random(
 def set_num_threads(n: int) -> None:
     """OpenMP thread count used by the C restatement."""
     os.environ["OMP_NUM_THREADS"] = str(n)
+
+
+def display_shard_records(token_ids, logits_shard, vocab_offset, total_vocab):
+    """Per-row (max, sum exp(x - max), first argmax | NaN flag, current logit)
+    record of one contiguous vocabulary shard, as int32 [rows, 4]."""
+    ids = _host(token_ids)
+    lg = _host(logits_shard)
+    rows = ids.numel()
+    out = torch.empty((rows, 4), dtype=torch.int32)
+    if rows:
+        rc = lib().cid_oracle_shard_records(
+            DT[lg.dtype], _p(lg), _p(ids), _i(rows), _i(lg.shape[-1]), _i(vocab_offset), _p(out)
+        )
+        _check(rc, "invalid shard")
+    return out
+
+
+def display_combine_records(records, token_ids, shard_offsets):
+    """Merge [world, rows, 4] records into the unsharded statistics."""
+    rec = _host(records)
+    ids = _host(token_ids)
+    offs = torch.tensor(list(shard_offsets), dtype=torch.int64)
+    conf = torch.empty(ids.shape, dtype=torch.float32)
+    cur = torch.empty(ids.shape, dtype=torch.float32)
+    pred = torch.empty(ids.shape, dtype=torch.int64)
+    if ids.numel():
+        lib().cid_oracle_combine_records(
+            _p(rec), ctypes.c_int(rec.shape[0]), _p(offs), _p(ids), _i(ids.numel()),
+            _p(conf), _p(pred), _p(cur),
+        )
+    return conf, pred, cur
