@@ -14,7 +14,9 @@
 //    2^(max*log2e - off) / sum with the exponent formed by one fma, so the
 //    rounding of `off` cancels exactly between numerator and denominator
 //    (this keeps rows like 1e4 + N(0, 0.25) accurate);
-//  * 16-byte streaming loads (ld.global.cs), four in flight per thread;
+//  * 16-byte streaming loads (ld.global.cs), CID_STATS_UNROLL in flight per
+//    thread; the chunk maximum is taken on the packed words (max.bf16x2 /
+//    max.f16x2) and each value is converted once, for its exp2 term;
 //  * rows shorter than the device's appetite are split across a thread-block
 //    cluster; partial states are merged through distributed shared memory in
 //    cluster-rank order (deterministic);
@@ -33,8 +35,14 @@ namespace cg = cooperative_groups;
 namespace cid {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kUnroll = 4;
+#ifndef CID_STATS_THREADS
+#define CID_STATS_THREADS 256
+#endif
+#ifndef CID_STATS_UNROLL
+#define CID_STATS_UNROLL 4
+#endif
+constexpr int kThreads = CID_STATS_THREADS;  // threads per CTA
+constexpr int kUnroll = CID_STATS_UNROLL;    // 16-byte loads in flight per thread
 constexpr int kNoIndex = INT_MAX;
 constexpr int kMaxCluster = 8;
 
@@ -83,6 +91,11 @@ template <> struct VecTraits<float> {
   __device__ static float scalar(const void* p, int64_t i) {
     return static_cast<const float*>(p)[i];
   }
+  // maximum of the vector's values (NaN ignored)
+  __device__ static float vmax(const uint4& v) {
+    return fmaxf(fmaxf(__uint_as_float(v.x), __uint_as_float(v.y)),
+                 fmaxf(__uint_as_float(v.z), __uint_as_float(v.w)));
+  }
   static constexpr uint32_t kNegInfWord = 0xff800000u;
 };
 template <> struct VecTraits<__nv_bfloat16> {
@@ -97,6 +110,15 @@ template <> struct VecTraits<__nv_bfloat16> {
   }
   __device__ static float scalar(const void* p, int64_t i) {
     return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  }
+  // maximum on packed bf16x2 (max.bf16x2 ignores NaN), converted once
+  __device__ static float vmax(const uint4& v) {
+    const __nv_bfloat162 a = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&v.x),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&v.y));
+    const __nv_bfloat162 b = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&v.z),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&v.w));
+    const __nv_bfloat162 c = __hmax2(a, b);
+    return fmaxf(__low2float(c), __high2float(c));
   }
   static constexpr uint32_t kNegInfWord = 0xff80ff80u;
 };
@@ -115,6 +137,14 @@ template <> struct VecTraits<__half> {
   __device__ static float scalar(const void* p, int64_t i) {
     return __half2float(static_cast<const __half*>(p)[i]);
   }
+  __device__ static float vmax(const uint4& v) {
+    const __half2 a = __hmax2(*reinterpret_cast<const __half2*>(&v.x),
+                              *reinterpret_cast<const __half2*>(&v.y));
+    const __half2 b = __hmax2(*reinterpret_cast<const __half2*>(&v.z),
+                              *reinterpret_cast<const __half2*>(&v.w));
+    const __half2 c = __hmax2(a, b);
+    return fmaxf(__low2float(c), __high2float(c));
+  }
   static constexpr uint32_t kNegInfWord = 0xfc00fc00u;
 };
 template <> struct VecTraits<double> {
@@ -126,7 +156,11 @@ template <> struct VecTraits<double> {
   __device__ static float scalar(const void* p, int64_t i) {
     return static_cast<float>(static_cast<const double*>(p)[i]);
   }
-  static constexpr uint32_t kNegInfWord = 0u;  // unused: f64 fills per element
+  __device__ static float vmax(const uint4& v) {
+    float f[2];
+    to_float(v, f);
+    return fmaxf(f[0], f[1]);
+  }
 };
 
 struct StatsParams {
@@ -264,34 +298,69 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
         d[k] = make_uint4(VT::kNegInfWord, VT::kNegInfWord, VT::kNegInfWord, VT::kNegInfWord);
       }
     }
-    float x[kUnroll][N];
-#pragma unroll
-    for (int k = 0; k < kUnroll; ++k) VT::to_float(d[k], x[k]);
     if (kRep) {
+      // repetition variant: patched values take part in the maximum
+      float x[kUnroll][N];
 #pragma unroll
       for (int k = 0; k < kUnroll; ++k) {
+        VT::to_float(d[k], x[k]);
         const int64_t c0 = head + (v + static_cast<int64_t>(k) * kThreads) * N;
 #pragma unroll
         for (int j = 0; j < N; ++j) x[k][j] = patched(pt, c0 + j, x[k][j]);
       }
-    }
-    float cm = x[0][0];
-#pragma unroll
-    for (int k = 0; k < kUnroll; ++k)
-#pragma unroll
-      for (int j = 0; j < N; ++j) cm = fmaxf(cm, x[k][j]);
-    if (cm > st.m) {
-      // new running maximum: its first column, in ascending column order
-      int64_t col = 0;
-      bool found = false;
+      float cm = x[0][0];
 #pragma unroll
       for (int k = 0; k < kUnroll; ++k)
 #pragma unroll
+        for (int j = 0; j < N; ++j) cm = fmaxf(cm, x[k][j]);
+      if (cm > st.m) {
+        int64_t col = 0;
+        bool found = false;
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k)
+#pragma unroll
+          for (int j = 0; j < N; ++j)
+            if (!found && x[k][j] == cm) {
+              found = true;
+              col = head + (v + static_cast<int64_t>(k) * kThreads) * N + j;
+            }
+        const float noff = offset_of(cm);
+        st.s = rescale(st.s + ((acc0 + acc1) + (acc2 + acc3)), st.m, st.off, noff);
+        acc0 = acc1 = acc2 = acc3 = 0.f;
+        st.m = cm;
+        st.off = noff;
+        st.idx = static_cast<int>(col);
+      }
+      const float noff = -st.off;
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k)
+#pragma unroll
+        for (int j = 0; j < N; j += 2) {
+          const float e0 = ex2(fmaf(x[k][j], kLog2e, noff));
+          const float e1 = ex2(fmaf(x[k][j + 1], kLog2e, noff));
+          if ((k & 1) == 0) { acc0 += e0; acc1 += e1; } else { acc2 += e0; acc3 += e1; }
+        }
+      continue;
+    }
+    // chunk maximum on the packed words, then one conversion per term
+    float cm = VT::vmax(d[0]);
+#pragma unroll
+    for (int k = 1; k < kUnroll; ++k) cm = fmaxf(cm, VT::vmax(d[k]));
+    if (cm > st.m) {
+      // new running maximum (rare): its first column, in ascending order
+      int64_t col = 0;
+      bool found = false;
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        float x[N];
+        VT::to_float(d[k], x);
+#pragma unroll
         for (int j = 0; j < N; ++j)
-          if (!found && x[k][j] == cm) {
+          if (!found && x[j] == cm) {
             found = true;
             col = head + (v + static_cast<int64_t>(k) * kThreads) * N + j;
           }
+      }
       const float noff = offset_of(cm);
       st.s = rescale(st.s + ((acc0 + acc1) + (acc2 + acc3)), st.m, st.off, noff);
       acc0 = acc1 = acc2 = acc3 = 0.f;
@@ -301,13 +370,16 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
     }
     const float noff = -st.off;
 #pragma unroll
-    for (int k = 0; k < kUnroll; ++k)
+    for (int k = 0; k < kUnroll; ++k) {
+      float x[N];
+      VT::to_float(d[k], x);
 #pragma unroll
       for (int j = 0; j < N; j += 2) {
-        const float e0 = ex2(fmaf(x[k][j], kLog2e, noff));
-        const float e1 = ex2(fmaf(x[k][j + 1], kLog2e, noff));
+        const float e0 = ex2(fmaf(x[j], kLog2e, noff));
+        const float e1 = ex2(fmaf(x[j + 1], kLog2e, noff));
         if ((k & 1) == 0) { acc0 += e0; acc1 += e1; } else { acc2 += e0; acc3 += e1; }
       }
+    }
   }
   // fold the vector accumulators (all relative to st.off) before the tail can
   // move the offset
