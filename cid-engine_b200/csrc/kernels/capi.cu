@@ -30,6 +30,8 @@ extern "C" const char* cid_result_string(int result) {
     case CID_ERR_LAUNCH: return "kernel launch failed (configuration or resources)";
     case CID_ERR_MISALIGNED: return "misaligned pointer";
     case CID_ERR_CUDA: return "CUDA runtime error";
+    case CID_ERR_SCRATCH_LIMIT:
+      return "batch exceeds the allocation-free entry point's fixed scratch (CID_NO_ALLOC_MAX_BATCH rows)";
     default: return "unknown result";
   }
 }

@@ -10,6 +10,7 @@
 //  * display corruption (csrc/ops.cpp:292-391): one CTA per row.
 #include <climits>
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -331,6 +332,89 @@ extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const floa
   cudaStream_t s = as_stream(stream);
   masked_diffusion_kernel<<<static_cast<unsigned>(batch), kT, 0, s>>>(p);
   int rc = launch_result();
+  if (rc != CID_OK) return rc;
+  masked_metrics_kernel<<<1, kT, 0, s>>>(p.counts, ratio, batch, tokens, metrics);
+  return launch_result();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free masked diffusion.
+//
+// Some callers cannot hand this library device memory for scratch: a host
+// program that reserves all device memory up front for its own pool and
+// forbids third-party cudaMalloc, a serving loop that must not pay
+// cudaMalloc's latency and implicit synchronisation on its request path, or
+// a thin FFI binding with no device allocator to draw a workspace from.
+// For them the per-row counts live in a fixed array in the library's own
+// device image.  Every GPU that loads the library holds the array until the
+// process exits.  Calls on one device share it, so calls that overlap on the
+// GPU (e.g. on two streams) race on it.  Each call writes the count of every
+// row before the metrics kernel reads it, so nothing needs clearing between
+// calls.
+// ---------------------------------------------------------------------------
+
+namespace cid {
+namespace {
+
+static __device__ __align__(256) int64_t g_no_alloc_counts[CID_NO_ALLOC_MAX_BATCH];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_no_alloc_mutex;
+int64_t* g_no_alloc_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  Host code only
+// holds a host-side stand-in for the symbol, so the address is looked up once
+// per device, with that device current.
+int no_alloc_scratch(int64_t** out) {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return record_cuda_error(err);
+  if (dev < 0 || dev >= kMaxDevices) return CID_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_no_alloc_mutex);
+  if (g_no_alloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_no_alloc_counts);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    g_no_alloc_addr[dev] = static_cast<int64_t*>(p);
+  }
+  *out = g_no_alloc_addr[dev];
+  return CID_OK;
+}
+
+}  // namespace
+}  // namespace cid
+
+extern "C" int cid_masked_diffusion_corrupt_no_alloc(
+    const int64_t* clean_ids, const float* ratio_random, const float* mask_random,
+    int64_t batch, int64_t tokens, int64_t mask_token_id, double min_mask_ratio,
+    double max_mask_ratio, int64_t* corrupted, uint8_t* masked, float* ratio, float* metrics,
+    void* stream) {
+  if (batch <= 0 || tokens <= 0) return CID_ERR_INVALID_ARGUMENT;
+  if (batch > CID_NO_ALLOC_MAX_BATCH) return CID_ERR_SCRATCH_LIMIT;
+  if (!(min_mask_ratio > 0.0 && min_mask_ratio <= max_mask_ratio && max_mask_ratio <= 1.0))
+    return CID_ERR_INVALID_ARGUMENT;
+  if (!clean_ids || !ratio_random || !mask_random || !corrupted || !masked || !ratio || !metrics)
+    return CID_ERR_INVALID_ARGUMENT;
+  int64_t* scratch = nullptr;
+  int rc = no_alloc_scratch(&scratch);
+  if (rc != CID_OK) return rc;
+  MaskedParams p;
+  p.clean = clean_ids;
+  p.ratio_random = ratio_random;
+  p.mask_random = mask_random;
+  p.batch = batch;
+  p.tokens = tokens;
+  p.mask_id = mask_token_id;
+  p.span = static_cast<float>(max_mask_ratio - min_mask_ratio);
+  p.lo = static_cast<float>(min_mask_ratio);
+  p.corrupted = corrupted;
+  p.masked = masked;
+  p.ratio = ratio;
+  p.metrics = metrics;
+  p.counts = scratch;
+  cudaStream_t s = as_stream(stream);
+  masked_diffusion_kernel<<<static_cast<unsigned>(batch), kT, 0, s>>>(p);
+  rc = launch_result();
   if (rc != CID_OK) return rc;
   masked_metrics_kernel<<<1, kT, 0, s>>>(p.counts, ratio, batch, tokens, metrics);
   return launch_result();

@@ -55,7 +55,8 @@ typedef enum cid_result {
   CID_ERR_UNSUPPORTED_DTYPE = 2,
   CID_ERR_LAUNCH = 3,
   CID_ERR_MISALIGNED = 4,
-  CID_ERR_CUDA = 5
+  CID_ERR_CUDA = 5,
+  CID_ERR_SCRATCH_LIMIT = 6
 } cid_result_t;
 
 /* Bits OR-ed into the optional device status word. */
@@ -225,6 +226,30 @@ CID_API int cid_masked_diffusion_corrupt(const int64_t* clean_ids,
                                  int64_t* corrupted, uint8_t* masked,
                                  float* ratio, float* metrics, void* workspace,
                                  void* stream);
+
+/* Allocation-free masked diffusion.  No counterpart in the reference: it is
+ * an extra way to call cid_masked_diffusion_corrupt for callers that cannot
+ * allocate device memory for a workspace — a host program that reserves all
+ * device memory for its own pool and forbids third-party cudaMalloc, a
+ * serving loop that must not pay cudaMalloc's latency and implicit
+ * synchronisation per request, or an FFI binding with no device allocator.
+ * Same arguments and outputs as cid_masked_diffusion_corrupt minus the
+ * workspace; the caller still passes every input and output.  Scratch is a
+ * fixed array inside the library's device image, CID_NO_ALLOC_MAX_BATCH rows
+ * (512 KiB), held by every GPU that loads the library until the process
+ * exits; batch > CID_NO_ALLOC_MAX_BATCH returns CID_ERR_SCRATCH_LIMIT.  The
+ * first call on a device looks up the array's device address (a
+ * cudaGetSymbolAddress with that device current), so make that first call
+ * before any stream capture.  Calls on one device share the array: calls
+ * that overlap on the GPU (on different streams) race on it.  Nothing in it
+ * needs clearing between calls. */
+#define CID_NO_ALLOC_MAX_BATCH 65536
+CID_API int cid_masked_diffusion_corrupt_no_alloc(
+    const int64_t* clean_ids, const float* ratio_random,
+    const float* mask_random, int64_t batch, int64_t tokens,
+    int64_t mask_token_id, double min_mask_ratio, double max_mask_ratio,
+    int64_t* corrupted, uint8_t* masked, float* ratio, float* metrics,
+    void* stream);
 
 /* thought_corrupt_from_epsilon — replaces csrc/registration.cpp:19-21,
  * csrc/ops.cpp:258-290, csrc/cuda/thought_corruption.cu:72-157.
