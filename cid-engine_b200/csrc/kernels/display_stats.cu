@@ -8,15 +8,21 @@
 // (csrc/cpu/display_stats.cpp:14-126 of fwerkor/cid-engine v1.1.0).
 //
 // Design (HBM-bound: every logit is read once, nothing else is large):
-//  * one pass with an online (max, offset, sum, argmax) state per thread;
-//    terms are 2^(x*log2e - off) where off = float(max*log2e) is the offset
-//    the running sum is kept relative to.  The final confidence is
+//  * one pass; each thread keeps (running max m, offset off, sums s) with
+//    terms 2^(x*log2e - off).  The offset is re-set only when the running
+//    maximum passes the maximum it was set from by more than kGap (terms stay
+//    below e^kGap), so the rescale branch is rare; the final confidence is
 //    2^(max*log2e - off) / sum with the exponent formed by one fma, so the
 //    rounding of `off` cancels exactly between numerator and denominator
 //    (this keeps rows like 1e4 + N(0, 0.25) accurate);
+//  * the argmax is tracked lazily: a thread records only WHICH chunk last
+//    raised its maximum (two predicated selects, no branch); once the row
+//    maximum is known, the threads holding it re-read that one chunk to find
+//    their first column and the smallest wins;
 //  * 16-byte streaming loads (ld.global.cs), CID_STATS_UNROLL in flight per
 //    thread; the chunk maximum is taken on the packed words (max.bf16x2 /
-//    max.f16x2) and each value is converted once, for its exp2 term;
+//    max.f16x2); the exp2 arguments and the sums use packed fma.rn.f32x2 /
+//    add.rn.f32x2 (sm_100);
 //  * rows shorter than the device's appetite are split across a thread-block
 //    cluster; partial states are merged through distributed shared memory in
 //    cluster-rank order (deterministic);
@@ -39,44 +45,88 @@ namespace {
 #define CID_STATS_THREADS 256
 #endif
 #ifndef CID_STATS_UNROLL
-#define CID_STATS_UNROLL 4
+#define CID_STATS_UNROLL 8
 #endif
 constexpr int kThreads = CID_STATS_THREADS;  // threads per CTA
 constexpr int kUnroll = CID_STATS_UNROLL;    // 16-byte loads in flight per thread
-constexpr int kNoIndex = INT_MAX;
 constexpr int kMaxCluster = 8;
+constexpr float kGap = 5.0f;  // natural-log units; terms stay <= e^5
+constexpr int64_t kNone = LLONG_MAX;
 
-struct Partial {
-  float m;    // running maximum (NaN ignored); -inf when nothing seen
-  float off;  // offset of the running sum: float(m * log2e), 0 while m = -inf
-  float s;    // sum of 2^(x*log2e - off)
-  int idx;    // column of the first maximum, kNoIndex when none
-};
-
-__device__ __forceinline__ float offset_of(float m) {
-  return m == -INFINITY ? 0.0f : m * kLog2e;
+// packed float32 pair ops (sm_100)
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %4};\n"
+      " mov.b64 rc, {%5, %5};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n .reg .b64 ra, rb;\n mov.b64 ra, {%0, %1};\n mov.b64 rb, {%2, %3};\n"
+      " add.rn.f32x2 ra, ra, rb;\n mov.b64 {%0, %1}, ra;\n}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
 }
 
-// Sum `s` (kept relative to `off`, state maximum `m`) re-expressed relative to
-// `new_off`.  A state that has seen only -inf/NaN carries 0 or NaN.
-__device__ __forceinline__ float rescale(float s, float m, float off, float new_off) {
-  if (m == -INFINITY) return s != s ? s : 0.0f;
+// Per-thread streaming state.
+struct Acc {
+  float m;       // running maximum (NaN ignored), -inf when nothing seen
+  float om;      // maximum the offset was set from; -inf = offset unset
+  float off;     // float(om * log2e), 0 while unset
+  float s0, s1;  // sums of 2^(x*log2e - off)
+  int64_t where; // chunk that last raised m: its first vector index (>= 0),
+                 // or -(column+1) for a scalar head/tail column
+};
+
+// Sum relative to `off` (state with offset maximum `om`) re-expressed
+// relative to `new_off`; a state without offset carries only 0 or NaN.
+__device__ __forceinline__ float rescale(float s, float om, float off, float new_off) {
+  if (om == -INFINITY) return s != s ? s : 0.0f;
   return s * ex2(off - new_off);
 }
 
+// Re-sets the offset when the running maximum has outgrown it (rare).
+__device__ __forceinline__ void maybe_reoffset(Acc& a) {
+  if (a.m > a.om + kGap) {
+    const float noff = a.m * kLog2e;
+    a.s0 = rescale(a.s0, a.om, a.off, noff);
+    a.s1 = rescale(a.s1, a.om, a.off, noff);
+    a.om = a.m;
+    a.off = noff;
+  }
+}
+
+// Reduced state of a group of threads: (m, om, off, s); the argmax column is
+// resolved separately.
+struct Partial {
+  float m, om, off, s;
+};
+
 __device__ __forceinline__ Partial merge(const Partial& a, const Partial& b) {
-  const bool take_b = b.m > a.m || (b.m == a.m && b.idx < a.idx);
-  Partial w = take_b ? b : a;
-  w.s = rescale(a.s, a.m, a.off, w.off) + rescale(b.s, b.m, b.off, w.off);
+  Partial w;
+  w.m = fmaxf(a.m, b.m);
+  if (a.om == -INFINITY && b.om == -INFINITY) {
+    w.om = -INFINITY;
+    w.off = 0.0f;
+    w.s = a.s + b.s;  // 0 or NaN
+    return w;
+  }
+  if (a.om == -INFINITY || (b.om != -INFINITY && b.off > a.off)) {
+    w.om = b.om;
+    w.off = b.off;
+  } else {
+    w.om = a.om;
+    w.off = a.off;
+  }
+  w.s = rescale(a.s, a.om, a.off, w.off) + rescale(b.s, b.om, b.off, w.off);
   return w;
 }
 
-__device__ __forceinline__ Partial shfl_down(const Partial& p, int delta) {
+__device__ __forceinline__ Partial shfl_xor(const Partial& p, int mask) {
   Partial q;
-  q.m = __shfl_down_sync(0xffffffffu, p.m, delta);
-  q.off = __shfl_down_sync(0xffffffffu, p.off, delta);
-  q.s = __shfl_down_sync(0xffffffffu, p.s, delta);
-  q.idx = __shfl_down_sync(0xffffffffu, p.idx, delta);
+  q.m = __shfl_xor_sync(0xffffffffu, p.m, mask);
+  q.om = __shfl_xor_sync(0xffffffffu, p.om, mask);
+  q.off = __shfl_xor_sync(0xffffffffu, p.off, mask);
+  q.s = __shfl_xor_sync(0xffffffffu, p.s, mask);
   return q;
 }
 
@@ -252,43 +302,35 @@ __device__ void repetition_patch(const StatsParams& p, int64_t row, Patch* out) 
   if (lane == 0) *out = pt;
 }
 
-template <typename T, bool kRep>
-__device__ __forceinline__ void consume_scalar(Partial& st, float& acc, float x, int64_t col,
-                                               const Patch& pt) {
+template <bool kRep>
+__device__ __forceinline__ void consume_scalar(Acc& a, float x, int64_t col, const Patch& pt) {
   if (kRep) x = patched(pt, col, x);
-  if (x > st.m) {
-    const float noff = offset_of(x);
-    st.s = rescale(st.s + acc, st.m, st.off, noff);
-    acc = 0.0f;
-    st.m = x;
-    st.off = noff;
-    st.idx = static_cast<int>(col);
-  }
-  acc += ex2(fmaf(x, kLog2e, -st.off));
+  const bool up = x > a.m;
+  a.m = up ? x : a.m;
+  a.where = up ? -(col + 1) : a.where;
+  maybe_reoffset(a);
+  a.s0 += ex2(fmaf(x, kLog2e, -a.off));
 }
 
-// Streams columns [c_beg, c_end) of one row into `st` (this thread's share).
-// Vector part: 16-byte vectors [v_beg, v_end) of the aligned region that
-// starts at column `head`; scalar part: the unaligned head and tail columns
-// owned by this CTA.
-template <typename T, bool kRep>
+// Streams this thread's share of one row: the unaligned head columns
+// [0, s_head_end), 16-byte vectors [v_beg, v_end) of the aligned region that
+// starts at column `head` (thread t takes v_beg + t, + stride, ...), and the
+// tail columns [s_tail_beg, s_tail_end) — in ascending column order, so a
+// strict `>` keeps each thread's first occurrence of its maximum.
+template <typename T, bool kRep, int kStride>
 __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_end,
                            int64_t s_head_end, int64_t s_tail_beg, int64_t s_tail_end,
-                           const Patch& pt, Partial& st) {
+                           const Patch& pt, Acc& a, int tid) {
   using VT = VecTraits<T>;
   constexpr int N = VT::N;
-  const int tid = threadIdx.x;
-  float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-  // head columns [0, s_head_end): lowest columns first
-  for (int64_t c = tid; c < s_head_end; c += kThreads)
-    consume_scalar<T, kRep>(st, acc0, VT::scalar(row, c), c, pt);
+  for (int64_t c = tid; c < s_head_end; c += kStride) consume_scalar<kRep>(a, VT::scalar(row, c), c, pt);
 
   const uint4* vrow = reinterpret_cast<const uint4*>(row + head);
-  for (int64_t v = v_beg + tid; v < v_end; v += kThreads * kUnroll) {
+  for (int64_t v = v_beg + tid; v < v_end; v += kStride * kUnroll) {
     uint4 d[kUnroll];
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
-      const int64_t vi = v + static_cast<int64_t>(k) * kThreads;
+      const int64_t vi = v + static_cast<int64_t>(k) * kStride;
       if (vi < v_end) {
         d[k] = __ldcs(vrow + vi);
       } else if constexpr (sizeof(T) == 8) {
@@ -301,118 +343,164 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
     if (kRep) {
       // repetition variant: patched values take part in the maximum
       float x[kUnroll][N];
+      float cm = -INFINITY;
 #pragma unroll
       for (int k = 0; k < kUnroll; ++k) {
         VT::to_float(d[k], x[k]);
-        const int64_t c0 = head + (v + static_cast<int64_t>(k) * kThreads) * N;
+        const int64_t c0 = head + (v + static_cast<int64_t>(k) * kStride) * N;
 #pragma unroll
-        for (int j = 0; j < N; ++j) x[k][j] = patched(pt, c0 + j, x[k][j]);
+        for (int j = 0; j < N; ++j) {
+          x[k][j] = patched(pt, c0 + j, x[k][j]);
+          cm = fmaxf(cm, x[k][j]);
+        }
       }
-      float cm = x[0][0];
-#pragma unroll
-      for (int k = 0; k < kUnroll; ++k)
-#pragma unroll
-        for (int j = 0; j < N; ++j) cm = fmaxf(cm, x[k][j]);
-      if (cm > st.m) {
-        int64_t col = 0;
-        bool found = false;
-#pragma unroll
-        for (int k = 0; k < kUnroll; ++k)
-#pragma unroll
-          for (int j = 0; j < N; ++j)
-            if (!found && x[k][j] == cm) {
-              found = true;
-              col = head + (v + static_cast<int64_t>(k) * kThreads) * N + j;
-            }
-        const float noff = offset_of(cm);
-        st.s = rescale(st.s + ((acc0 + acc1) + (acc2 + acc3)), st.m, st.off, noff);
-        acc0 = acc1 = acc2 = acc3 = 0.f;
-        st.m = cm;
-        st.off = noff;
-        st.idx = static_cast<int>(col);
-      }
-      const float noff = -st.off;
+      const bool up = cm > a.m;
+      a.m = up ? cm : a.m;
+      a.where = up ? v : a.where;
+      maybe_reoffset(a);
+      const float noff = -a.off;
 #pragma unroll
       for (int k = 0; k < kUnroll; ++k)
 #pragma unroll
         for (int j = 0; j < N; j += 2) {
-          const float e0 = ex2(fmaf(x[k][j], kLog2e, noff));
-          const float e1 = ex2(fmaf(x[k][j + 1], kLog2e, noff));
-          if ((k & 1) == 0) { acc0 += e0; acc1 += e1; } else { acc2 += e0; acc3 += e1; }
+          float t0, t1;
+          fma2(t0, t1, x[k][j], x[k][j + 1], kLog2e, noff);
+          add2(a.s0, a.s1, ex2(t0), ex2(t1));
         }
       continue;
     }
-    // chunk maximum on the packed words, then one conversion per term
     float cm = VT::vmax(d[0]);
 #pragma unroll
     for (int k = 1; k < kUnroll; ++k) cm = fmaxf(cm, VT::vmax(d[k]));
-    if (cm > st.m) {
-      // new running maximum (rare): its first column, in ascending order
-      int64_t col = 0;
-      bool found = false;
-#pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        float x[N];
-        VT::to_float(d[k], x);
-#pragma unroll
-        for (int j = 0; j < N; ++j)
-          if (!found && x[j] == cm) {
-            found = true;
-            col = head + (v + static_cast<int64_t>(k) * kThreads) * N + j;
-          }
-      }
-      const float noff = offset_of(cm);
-      st.s = rescale(st.s + ((acc0 + acc1) + (acc2 + acc3)), st.m, st.off, noff);
-      acc0 = acc1 = acc2 = acc3 = 0.f;
-      st.m = cm;
-      st.off = noff;
-      st.idx = static_cast<int>(col);
-    }
-    const float noff = -st.off;
+    const bool up = cm > a.m;  // lazy argmax: remember the chunk only
+    a.m = up ? cm : a.m;
+    a.where = up ? v : a.where;
+    maybe_reoffset(a);
+    const float noff = -a.off;
 #pragma unroll
     for (int k = 0; k < kUnroll; ++k) {
       float x[N];
       VT::to_float(d[k], x);
 #pragma unroll
       for (int j = 0; j < N; j += 2) {
-        const float e0 = ex2(fmaf(x[j], kLog2e, noff));
-        const float e1 = ex2(fmaf(x[j + 1], kLog2e, noff));
-        if ((k & 1) == 0) { acc0 += e0; acc1 += e1; } else { acc2 += e0; acc3 += e1; }
+        float t0, t1;
+        fma2(t0, t1, x[j], x[j + 1], kLog2e, noff);
+        add2(a.s0, a.s1, ex2(t0), ex2(t1));
       }
     }
   }
-  // fold the vector accumulators (all relative to st.off) before the tail can
-  // move the offset
-  st.s = st.s + ((acc0 + acc1) + (acc2 + acc3));
-  float acc = 0.f;
-  // tail columns [s_tail_beg, s_tail_end): highest columns last
-  for (int64_t c = s_tail_beg + tid; c < s_tail_end; c += kThreads)
-    consume_scalar<T, kRep>(st, acc, VT::scalar(row, c), c, pt);
-  st.s = st.s + acc;
+  for (int64_t c = s_tail_beg + tid; c < s_tail_end; c += kStride)
+    consume_scalar<kRep>(a, VT::scalar(row, c), c, pt);
 }
 
-// Block-wide merge of per-thread partials in a fixed order.
-__device__ Partial block_merge(Partial st, Partial* smem_warps) {
+// First column holding `target` among this thread's elements, from the chunk
+// recorded in `where` (re-read from memory); kNone when the thread's maximum
+// is not `target`.
+template <typename T, bool kRep, int kStride>
+__device__ int64_t first_column(const Acc& a, float target, const T* row, int64_t head,
+                                int64_t v_end, const Patch& pt) {
+  using VT = VecTraits<T>;
+  constexpr int N = VT::N;
+  if (!(a.m == target)) return kNone;
+  if (a.where < 0) return -a.where - 1;
+  const uint4* vrow = reinterpret_cast<const uint4*>(row + head);
+  for (int k = 0; k < kUnroll; ++k) {
+    const int64_t vi = a.where + static_cast<int64_t>(k) * kStride;
+    if (vi >= v_end) break;
+    float x[N];
+    VT::to_float(vrow[vi], x);
 #pragma unroll
-  for (int d = 16; d > 0; d >>= 1) st = merge(st, shfl_down(st, d));
+    for (int j = 0; j < N; ++j) {
+      const int64_t col = head + vi * N + j;
+      const float y = kRep ? patched(pt, col, x[j]) : x[j];
+      if (y == target) return col;
+    }
+  }
+  return kNone;
+}
+
+// Block-wide merge of per-thread partials in a fixed order (result valid in
+// every thread).
+__device__ Partial block_merge(Partial st, Partial* smem_warps, Partial* smem_out) {
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) st = merge(st, shfl_xor(st, d));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) smem_warps[warp] = st;
   __syncthreads();
-  Partial out = smem_warps[0];
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
+    Partial out = smem_warps[0];
     for (int w = 1; w < kThreads / 32; ++w) out = merge(out, smem_warps[w]);
-  return out;  // valid in thread 0
+    *smem_out = out;
+  }
+  __syncthreads();
+  return *smem_out;
 }
 
-__device__ __forceinline__ unsigned block_min_u32(unsigned v, unsigned* smem) {
-  v = __reduce_min_sync(0xffffffffu, v);
+__device__ __forceinline__ int64_t block_min_i64(int64_t v, int64_t* smem) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, d));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) smem[warp] = v;
   __syncthreads();
-  unsigned r = smem[0];
+  int64_t r = smem[0];
   for (int w = 1; w < kThreads / 32; ++w) r = min(r, smem[w]);
   __syncthreads();
   return r;
+}
+
+// Outputs of one row whose maximum is not finite or whose sum is NaN:
+// predicted = first NaN, else first maximum; statistics NaN.
+template <typename T, Mode kMode>
+__device__ void write_special(const StatsParams& p, int64_t row, const T* rowp, int64_t V,
+                              float m, int64_t first_nan, int64_t first_max) {
+  using VT = VecTraits<T>;
+  const float qnan = __int_as_float(0x7fffffff);
+  const int64_t local = first_nan != kNone ? first_nan : (first_max != kNone ? first_max : 0);
+  if (kMode == Mode::kFinal) {
+    p.predicted[row] = local;
+    p.confidence[row] = qnan;
+    p.current[row] = qnan;
+  } else {
+    cid_shard_record_t rec;
+    rec.max_logit = m;
+    rec.sum_exp = m == -INFINITY ? 0.0f : qnan;
+    rec.index = static_cast<int32_t>(p.vocab_offset + local) |
+                (first_nan != kNone ? static_cast<int32_t>(0x80000000u) : 0);
+    const int64_t id = p.ids[row] - p.vocab_offset;
+    rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
+    p.records[row] = rec;
+  }
+}
+
+// Outputs of one ordinary row from its merged partial and argmax column.
+template <typename T, bool kRep, Mode kMode>
+__device__ void write_normal(const StatsParams& p, int64_t row, const T* rowp, int64_t V,
+                             const Patch& pt, const Partial& fin, int64_t col) {
+  using VT = VecTraits<T>;
+  const float top = ex2(fmaf(fin.m, kLog2e, -fin.off));  // 2^(max*log2e - off)
+  if (kMode == Mode::kFinal) {
+    const int64_t id = p.ids[row];
+    float cur;
+    if (id >= 0 && id < V) {
+      float x = VT::scalar(rowp, id);
+      if (kRep) x = patched(pt, id, x);
+      cur = __fdiv_rn(ex2(fmaf(x, kLog2e, -fin.off)), fin.s);
+    } else {
+      cur = __int_as_float(0x7fffffff);
+      if (p.status) atomicOr(p.status, CID_STATUS_TOKEN_ID_OUT_OF_RANGE);
+    }
+    p.confidence[row] = __fdiv_rn(top, fin.s);
+    p.predicted[row] = col;
+    p.current[row] = cur;
+  } else {
+    cid_shard_record_t rec;
+    rec.max_logit = fin.m;
+    rec.sum_exp = __fdiv_rn(fin.s, top);  // sum of exp(x - max) over the shard
+    rec.index = static_cast<int32_t>(p.vocab_offset + col);
+    const int64_t id = p.ids[row] - p.vocab_offset;
+    rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
+    p.records[row] = rec;
+  }
 }
 
 template <typename T, bool kRep, Mode kMode>
@@ -420,10 +508,11 @@ __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) 
   using VT = VecTraits<T>;
   constexpr int N = VT::N;
   __shared__ Partial warp_parts[kThreads / 32];
-  __shared__ Partial cta_part;
+  __shared__ Partial cta_part;   // this CTA's merged partial
+  __shared__ Partial row_part;   // the row's merged partial (rank 0 -> all)
+  __shared__ int64_t red[kThreads / 32];
+  __shared__ int64_t cta_col;    // this CTA's first column of the maximum
   __shared__ Patch patch;
-  __shared__ unsigned red[kThreads / 32];
-  __shared__ int special;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int nrank = static_cast<int>(cluster.num_blocks());
@@ -451,83 +540,110 @@ __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) 
   const int64_t h_end = rank == 0 ? head : 0;
   const int64_t t_beg = rank == nrank - 1 ? tail_beg : V;
 
-  Partial st{-INFINITY, 0.0f, 0.0f, kNoIndex};
-  stream_row<T, kRep>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, st);
-  Partial merged = block_merge(st, warp_parts);
-  if (threadIdx.x == 0) cta_part = merged;
+  Acc a{-INFINITY, -INFINITY, 0.0f, 0.0f, 0.0f, kNone};
+  stream_row<T, kRep, kThreads>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
+  Partial mine{a.m, a.om, a.off, a.s0 + a.s1};
+  const Partial cta = block_merge(mine, warp_parts, &cta_part);
 
+  // the row's partial: merge the cluster's CTAs in rank order
+  Partial fin = cta;
   if (nrank > 1) {
     cluster.sync();  // every CTA's partial is visible cluster-wide
-    if (rank == 0 && threadIdx.x == 0) {
-      for (int r = 1; r < nrank; ++r) merged = merge(merged, *cluster.map_shared_rank(&cta_part, r));
-      cta_part = merged;
+    if (threadIdx.x == 0) {
+      Partial r = *cluster.map_shared_rank(&cta_part, 0);
+      for (int k = 1; k < nrank; ++k) r = merge(r, *cluster.map_shared_rank(&cta_part, k));
+      row_part = r;
     }
-    cluster.sync();  // remote partials have been read; other CTAs may exit
+    __syncthreads();
+    fin = row_part;
+  }
+  const bool special = !isfinite(fin.m) || (fin.s != fin.s);
+
+  // first column of the maximum: threads that hold it re-read their chunk
+  int64_t col = kNone;
+  if (!special) col = first_column<T, kRep, kThreads>(a, fin.m, rowp, head, v_end, pt);
+  col = block_min_i64(col, red);
+  if (threadIdx.x == 0) cta_col = col;
+  if (nrank > 1) {
+    cluster.sync();  // every CTA's column is visible
+    if (rank == 0 && threadIdx.x == 0)
+      for (int k = 1; k < nrank; ++k) col = min(col, *cluster.map_shared_rank(&cta_col, k));
+    cluster.sync();  // remote shared memory has been read; other CTAs may exit
     if (rank != 0) return;
   }
-  if (threadIdx.x == 0) {
-    const Partial m = cta_part;
-    special = !isfinite(m.m) || (m.s != m.s);
-  }
-  __syncthreads();
-  const Partial fin = cta_part;
 
   if (special) {
     // Rare path: first NaN column, else first column equal to the maximum.
-    unsigned first_nan = UINT_MAX, first_max = UINT_MAX;
+    int64_t first_nan = kNone, first_max = kNone;
     for (int64_t c = threadIdx.x; c < V; c += kThreads) {
       float x = VT::scalar(rowp, c);
       if (kRep) x = patched(pt, c, x);
-      if (x != x && first_nan == UINT_MAX) first_nan = static_cast<unsigned>(c);
-      if (x == fin.m && first_max == UINT_MAX) first_max = static_cast<unsigned>(c);
+      if (x != x && first_nan == kNone) first_nan = c;
+      if (x == fin.m && first_max == kNone) first_max = c;
     }
-    first_nan = block_min_u32(first_nan, red);
-    first_max = block_min_u32(first_max, red);
-    if (threadIdx.x == 0) {
-      const float qnan = __int_as_float(0x7fffffff);
-      if (kMode == Mode::kFinal) {
-        p.predicted[row] = first_nan != UINT_MAX ? first_nan : (first_max != UINT_MAX ? first_max : 0);
-        p.confidence[row] = qnan;
-        p.current[row] = qnan;
-      } else {
-        cid_shard_record_t rec;
-        rec.max_logit = fin.m;
-        rec.sum_exp = fin.m == -INFINITY ? 0.0f : qnan;
-        const int64_t local = first_nan != UINT_MAX ? first_nan : (first_max != UINT_MAX ? first_max : 0);
-        rec.index = static_cast<int32_t>(p.vocab_offset + local) |
-                    (first_nan != UINT_MAX ? static_cast<int32_t>(0x80000000u) : 0);
-        const int64_t id = p.ids[row] - p.vocab_offset;
-        rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
-        p.records[row] = rec;
-      }
-    }
+    first_nan = block_min_i64(first_nan, red);
+    first_max = block_min_i64(first_max, red);
+    if (threadIdx.x == 0) write_special<T, kMode>(p, row, rowp, V, fin.m, first_nan, first_max);
     return;
   }
-  if (threadIdx.x != 0) return;
-  const float top = ex2(fmaf(fin.m, kLog2e, -fin.off));  // 2^(max*log2e - off)
-  if (kMode == Mode::kFinal) {
-    const int64_t id = p.ids[row];
-    float cur;
-    if (id >= 0 && id < V) {
-      float x = VT::scalar(rowp, id);
-      if (kRep) x = patched(pt, id, x);
-      cur = __fdiv_rn(ex2(fmaf(x, kLog2e, -fin.off)), fin.s);
-    } else {
-      cur = __int_as_float(0x7fffffff);
-      if (p.status) atomicOr(p.status, CID_STATUS_TOKEN_ID_OUT_OF_RANGE);
-    }
-    p.confidence[row] = __fdiv_rn(top, fin.s);
-    p.predicted[row] = fin.idx;
-    p.current[row] = cur;
-  } else {
-    cid_shard_record_t rec;
-    rec.max_logit = fin.m;
-    rec.sum_exp = __fdiv_rn(fin.s, top);  // sum of exp(x - max) over the shard
-    rec.index = static_cast<int32_t>(p.vocab_offset + fin.idx);
-    const int64_t id = p.ids[row] - p.vocab_offset;
-    rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
-    p.records[row] = rec;
+  if (threadIdx.x == 0) write_normal<T, kRep, kMode>(p, row, rowp, V, pt, fin, col);
+}
+
+// One warp per row (no block barriers): for many rows of moderate length,
+// where a CTA per row would spend too much of its short life in block
+// reductions.
+constexpr int kRowWarps = 4;
+
+__device__ __forceinline__ int64_t warp_min_i64(int64_t v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, d));
+  return v;
+}
+
+template <typename T, bool kRep, Mode kMode>
+__global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(StatsParams p) {
+  using VT = VecTraits<T>;
+  constexpr int N = VT::N;
+  __shared__ Patch patches[kRowWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp;
+  if (row >= p.rows) return;  // uniform per warp
+  Patch pt;
+  pt.n = 0;
+  if (kRep) {
+    repetition_patch(p, row, &patches[warp]);
+    __syncwarp();
+    pt = patches[warp];
   }
+  const T* rowp = static_cast<const T*>(p.logits) + row * p.row_stride;
+  const int64_t V = p.vocab;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp);
+  int64_t head = static_cast<int64_t>(((16 - (addr & 15)) & 15) / sizeof(T));
+  if (head > V) head = V;
+  const int64_t nvec = (V - head) / N;
+  const int64_t tail_beg = head + nvec * N;
+
+  Acc a{-INFINITY, -INFINITY, 0.0f, 0.0f, 0.0f, kNone};
+  stream_row<T, kRep, 32>(rowp, head, 0, nvec, head, tail_beg, V, pt, a, lane);
+  Partial fin{a.m, a.om, a.off, a.s0 + a.s1};
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) fin = merge(fin, shfl_xor(fin, d));
+  const bool special = !isfinite(fin.m) || (fin.s != fin.s);
+  if (special) {
+    int64_t first_nan = kNone, first_max = kNone;
+    for (int64_t c = lane; c < V; c += 32) {
+      float x = VT::scalar(rowp, c);
+      if (kRep) x = patched(pt, c, x);
+      if (x != x && first_nan == kNone) first_nan = c;
+      if (x == fin.m && first_max == kNone) first_max = c;
+    }
+    first_nan = warp_min_i64(first_nan);
+    first_max = warp_min_i64(first_max);
+    if (lane == 0) write_special<T, kMode>(p, row, rowp, V, fin.m, first_nan, first_max);
+    return;
+  }
+  const int64_t col = warp_min_i64(first_column<T, kRep, 32>(a, fin.m, rowp, head, nvec, pt));
+  if (lane == 0) write_normal<T, kRep, kMode>(p, row, rowp, V, pt, fin, col);
 }
 
 // ---------------------------------------------------------------------------
@@ -601,19 +717,57 @@ __global__ void combine_records_kernel(CombineParams p) {
 // Launch helpers
 // ---------------------------------------------------------------------------
 
-// Cluster size: split rows until the grid has at least ~4 resident waves of
-// CTAs, keeping at least 64 vectors (1-2 KB) per CTA.
-int cluster_size(int64_t rows, int64_t vocab, int esize) {
-  const int64_t want = static_cast<int64_t>(sm_count()) * 8 * 4;
-  const int64_t vecs = vocab * esize / 16;
+// Cluster size: split rows over P CTAs (power of two, <= 8) until the grid
+// holds at least two waves of resident CTAs, while each CTA keeps at least
+// two full iterations of 16-byte loads.
+template <typename T, bool kRep, Mode kMode>
+int cluster_size(int64_t rows, int64_t vocab) {
+  static int resident_per_sm = 0;  // per template instance, from the occupancy API
+  if (resident_per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, display_stats_kernel<T, kRep, kMode>,
+                                                      kThreads, 0) != cudaSuccess || n <= 0)
+      n = 4;
+    resident_per_sm = n;
+  }
+  const int64_t want = 2LL * sm_count() * resident_per_sm;
+  const int64_t vecs = vocab * static_cast<int64_t>(sizeof(T)) / 16;
+  const int64_t min_vecs = 2LL * kThreads * kUnroll;
   int P = 1;
-  while (P < kMaxCluster && rows * P < want && vecs / (2 * P) >= 64) P *= 2;
+  while (P < kMaxCluster && rows * P < want && vecs / (2 * P) >= min_vecs) P *= 2;
   return P;
+}
+
+#ifndef CID_STATS_ROW_MODE
+#define CID_STATS_ROW_MODE 0  // 0: automatic, 1: CTA (cluster) per row, 2: warp per row
+#endif
+
+// Warp per row when the rows alone fill at least eight waves of resident
+// warps; a CTA (or cluster of CTAs) per row otherwise.
+template <typename T, bool kRep, Mode kMode>
+bool use_row_warps(int64_t rows) {
+  if (CID_STATS_ROW_MODE != 0) return CID_STATS_ROW_MODE == 2;
+  static int warps_per_sm = 0;
+  if (warps_per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, display_stats_rows_kernel<T, kRep, kMode>,
+                                                      kRowWarps * 32, 0) != cudaSuccess || n <= 0)
+      n = 8;
+    warps_per_sm = n * kRowWarps;
+  }
+  return rows >= 8LL * sm_count() * warps_per_sm;
 }
 
 template <typename T, bool kRep, Mode kMode>
 int launch_stats(const StatsParams& prm, cudaStream_t stream) {
-  const int P = cluster_size(prm.rows, prm.vocab, sizeof(T));
+  if (use_row_warps<T, kRep, kMode>(prm.rows)) {
+    const int64_t blocks = (prm.rows + kRowWarps - 1) / kRowWarps;
+    if (blocks > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+    display_stats_rows_kernel<T, kRep, kMode>
+        <<<static_cast<unsigned>(blocks), kRowWarps * 32, 0, stream>>>(prm);
+    return launch_result();
+  }
+  const int P = cluster_size<T, kRep, kMode>(prm.rows, prm.vocab);
   const int64_t blocks = prm.rows * P;
   if (blocks > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
   cudaLaunchConfig_t cfg = {};

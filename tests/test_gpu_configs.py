@@ -1,0 +1,239 @@
+"""GPU parity at the benchmark configurations' sizes, and device behaviours.
+
+Full-size inputs are generated on the device; rows small enough for the
+oracle are copied back and checked exactly (argmax, ids, decisions) or within
+the statistics tolerance; the rest is checked through size-independent
+properties (planted-tie rows must report the lower column, every argmax must
+hold the row maximum, sharded == unsharded, repeated calls are identical).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import cases
+import compare
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+STATS = "display_token_statistics"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _engine():
+    import cid_engine  # noqa: F401
+
+    assert torch.cuda.is_available()
+    yield
+    torch.cuda.empty_cache()
+
+
+def _check_stats(out, ids, logits, name):
+    expected = oracle.display_token_statistics(ids, logits)
+    compare.assert_matches(STATS, out, expected, name)
+
+
+def test_cfg2_full_size_rows_match_oracle() -> None:
+    """Config 2: bf16 [32, 1024, 128256] with planted peaks and exact ties."""
+    import bench
+
+    dev = torch.device("cuda", 0)
+    ids, logits = bench.display_inputs(32, 1024, 128256, seed=1, device=dev)
+    conf, pred, cur = torch.ops.cid_engine.display_token_statistics(ids, logits)
+    torch.cuda.synchronize()
+    flat = logits.view(-1, 128256)
+    # every argmax holds the row maximum (size-independent property)
+    row_max = flat.amax(dim=1)  # exact in bf16
+    got = flat.gather(1, pred.view(-1, 1)).view(-1)
+    assert torch.equal(got, row_max)
+    # rows with two equal maxima report the lower column (first maximum)
+    first = torch.max((flat == row_max[:, None]).to(torch.uint8), dim=1).indices
+    assert torch.equal(pred.view(-1), first)
+    del first
+    # 512 rows spread over the tensor against the oracle
+    sel = torch.linspace(0, 32 * 1024 - 1, 512, device=dev).long()
+    sub_ids = ids.view(-1)[sel].view(1, -1).cpu()
+    sub_lg = flat[sel].view(1, -1, 128256).cpu()
+    out = (conf.view(-1)[sel].view(1, -1), pred.view(-1)[sel].view(1, -1), cur.view(-1)[sel].view(1, -1))
+    _check_stats(out, sub_ids, sub_lg, "cfg2 rows")
+    assert bool(torch.isfinite(conf).all()) and bool(((conf > 0) & (conf <= 1)).all())
+    assert bool((cur <= conf * (1 + 1e-6)).all())
+
+
+def test_cfg1_chain_matches_oracle() -> None:
+    """Config 1: fp32 [4, 256, 32000] stats -> refine, S=32 slots, thought t=0.3."""
+    ids, logits = cases.cfg1_display()
+    conf, pred, cur = torch.ops.cid_engine.display_token_statistics(ids.cuda(), logits.cuda())
+    _check_stats((conf, pred, cur), ids, logits, "cfg1 stats")
+    refined = torch.ops.cid_engine.refine_display_from_statistics(
+        ids.cuda(), conf, pred, cur, 0, 1, 0.25, 0.1, 0.05)
+    expected = oracle.refine_display_from_statistics(ids, conf.cpu(), pred.cpu(), cur.cpu(),
+                                                     0, 1, 0.25, 0.1, 0.05)
+    assert torch.equal(refined.cpu(), expected)
+    g = torch.Generator().manual_seed(10)
+    occ = (torch.rand(4, 32, 1, generator=g) < 0.4).float()
+    life = torch.zeros(4, 32, 4)
+    life[..., 3] = (torch.rand(4, 32, generator=g) < 0.1).float()
+    live = torch.ops.cid_engine.live_slot_occupancy(occ.cuda(), life.cuda(), 3)
+    assert torch.equal(live.cpu(), oracle.live_slot_occupancy(occ, life, 3))
+    th = cases.cfg1_thought()
+    got = torch.ops.cid_engine.thought_corrupt_from_epsilon(*[t.cuda() for t in th])
+    compare.assert_matches("thought_corrupt_from_epsilon", got,
+                           oracle.thought_corrupt_from_epsilon(*th), "cfg1 thought")
+
+
+def test_cfg3_masked_diffusion_full_and_deterministic() -> None:
+    args = list(cases.cfg3_masked_diffusion())
+    dev_args = [a.cuda() if isinstance(a, torch.Tensor) else a for a in args]
+    out1 = torch.ops.cid_engine.masked_diffusion_corrupt_from_random(*dev_args)
+    out2 = torch.ops.cid_engine.masked_diffusion_corrupt_from_random(*dev_args)
+    for a, b in zip(out1, out2):
+        assert torch.equal(a, b)  # fixed-order metrics: bit-identical
+    compare.assert_matches("masked_diffusion_corrupt_from_random", out1,
+                           oracle.masked_diffusion_corrupt_from_random(*args), "cfg3")
+    assert bool(out1[1].any(dim=1).all())  # zero-ratio rows took the fallback
+
+
+@pytest.mark.parametrize("tokens", [512, 4096, 8192])
+def test_cfg5_refine_rows_match_oracle(tokens: int) -> None:
+    """Config-5 refine shape (B=256, L=512) plus long rows that exceed the
+    shared-memory staging (global-memory path)."""
+    batch = 256 if tokens == 512 else 4
+    ids, (conf, pred, cur) = cases.refine_inputs_large(77 + tokens, batch, tokens)
+    for reveal, revision, margin in ((0.25, 0.1, 0.05), (1.0, 1.0, 0.0)):
+        got = torch.ops.cid_engine.refine_display_from_statistics(
+            ids.cuda(), conf.cuda(), pred.cuda(), cur.cuda(), 0, 1, reveal, revision, margin)
+        exp = oracle.refine_display_from_statistics(ids, conf, pred, cur, 0, 1, reveal,
+                                                    revision, margin)
+        assert torch.equal(got.cpu(), exp)
+
+
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_vocab_sharded_records_equal_unsharded(world: int, dtype: torch.dtype) -> None:
+    """Vocabulary sharding emulated on one GPU: records of each shard,
+    combined, equal the unsharded statistics."""
+    from cid_engine import parallel
+
+    g = torch.Generator().manual_seed(world)
+    V = 152064 if world in (2, 8) else 4099
+    ids = torch.randint(V, (2, 40), generator=g)
+    lg = (torch.randn(2, 40, V, generator=g) * 2).to(dtype)
+    lg[0, 3, V - 1] = 40.0  # peak in the last shard
+    lg[1, 7, [5, V // 2 + 3]] = 50.0  # exact cross-shard tie: lowest column wins
+    lg[1, 9, 17] = float("nan")
+    lg[0, 11, :] = float("-inf")
+    lgd, idd = lg.cuda(), ids.cuda()
+    offs = parallel.shard_offsets(V, world)
+    recs = torch.stack([
+        torch.ops.cid_engine.display_shard_records(idd, lgd[..., offs[r]:offs[r + 1]], offs[r], V)
+        for r in range(world)
+    ])
+    got = torch.ops.cid_engine.display_combine_records(recs, idd, offs)
+    unsharded = torch.ops.cid_engine.display_token_statistics(idd, lgd)
+    assert torch.equal(got[1], unsharded[1])
+    torch.testing.assert_close(got[0], unsharded[0], rtol=2e-5, atol=2e-6, equal_nan=True)
+    torch.testing.assert_close(got[2], unsharded[2], rtol=2e-5, atol=2e-6, equal_nan=True)
+    compare.assert_matches(STATS, got, oracle.display_token_statistics(ids, lg), "sharded")
+    # the device records agree with the oracle's records
+    orc = torch.stack([oracle.display_shard_records(ids, lg[..., offs[r]:offs[r + 1]], offs[r], V)
+                       for r in range(world)])
+    assert torch.equal(recs[..., 2].cpu(), orc[..., 2])  # argmax / NaN flag exact
+
+
+def test_out_of_range_ids_set_status_and_nan() -> None:
+    import cid_engine
+
+    cid_engine.device_status(0, reset=True)
+    ids = torch.tensor([[3, 99, -1]], device="cuda")
+    lg = torch.randn(1, 3, 16, device="cuda")
+    conf, pred, cur = cid_engine.display_token_statistics(ids, lg)
+    assert bool(torch.isnan(cur[0, 1:]).all()) and bool(torch.isfinite(cur[0, 0]))
+    assert cid_engine.device_status(0) & cid_engine.STATUS_TOKEN_ID_OUT_OF_RANGE
+    idx = torch.tensor([0, 40], device="cuda")
+    snap = cid_engine.materialize_cell_snapshot(
+        torch.randn(1, 2, 8, device="cuda"), torch.randn(1, 2, 3, device="cuda"),
+        torch.rand(1, 2, 1, device="cuda"), torch.randn(1, 2, 1, device="cuda"),
+        torch.randn(1, 2, 4, device="cuda"), torch.ones(1, 2, dtype=torch.bool, device="cuda"), idx)
+    assert bool(torch.isnan(snap[..., -1]).all())
+    assert cid_engine.device_status(0, reset=True) & cid_engine.STATUS_SEMANTIC_INDEX_OUT_OF_RANGE
+    assert cid_engine.device_status(0) == 0
+
+
+def test_repetition_long_runs() -> None:
+    """Runs longer than a warp (the ballot scan loops) and runs touching the
+    sequence ends."""
+    ids = torch.full((2, 200), 7)
+    ids[0, 100:] = 9
+    ids[1, ::50] = 4
+    g = torch.Generator().manual_seed(3)
+    lg = torch.randn(2, 200, 64, generator=g) * 2
+    lg[..., 7] += 6
+    got = torch.ops.cid_engine.display_token_statistics_with_repetition(ids.cuda(), lg.cuda(), 0, 1, 0.9)
+    exp = oracle.display_token_statistics_with_repetition(ids, lg, 0, 1, 0.9)
+    compare.assert_matches("display_token_statistics_with_repetition", got, exp, "long runs")
+
+
+def test_unaligned_and_strided_rows() -> None:
+    """Row strides that break 16-byte alignment (odd vocab, sliced views)."""
+    g = torch.Generator().manual_seed(5)
+    base = torch.randn(3, 50, 4099, generator=g).to(torch.bfloat16)
+    view = base[:, :, 1:4098]  # unaligned start, row stride 4099
+    ids = torch.randint(4097, (3, 50), generator=g)
+    got = torch.ops.cid_engine.display_token_statistics(ids.cuda(), base.cuda()[:, :, 1:4098])
+    _check_stats(got, ids, view, "strided")
+
+
+def test_fused_step_chain_runs_without_host_sync() -> None:
+    from cid_engine.step import SlotInputs, refine_step
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1)
+    B, L, V, S = 4, 64, 1000, 16
+    ids = torch.randint(2, V, (B, L), generator=g, device=dev)
+    lg = torch.randn(B, L, V, generator=g, device=dev)
+    slots = SlotInputs(
+        occupancy=(torch.rand(B, S, 1, generator=g, device=dev) < 0.4).float(),
+        allocation_logits=torch.randn(B, S, generator=g, device=dev),
+        lifecycle_logits=torch.randn(B, S, 4, generator=g, device=dev),
+        revision_logits=torch.randn(B, S, 3, generator=g, device=dev),
+        input_lifecycle=torch.randn(B, S, 4, generator=g, device=dev),
+        semantic=torch.randn(B, S, 32, generator=g, device=dev),
+        role_logits=torch.randn(B, S, 6, generator=g, device=dev),
+        uncertainty=torch.rand(B, S, 1, generator=g, device=dev),
+        noise_delta=torch.randn(B, S, 1, generator=g, device=dev),
+        semantic_indices=torch.tensor([0, 5, 31], device=dev),
+    )
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        out = refine_step(ids, lg, mask_token_id=0, eos_token_id=1, reveal_fraction=0.5,
+                          revision_fraction=0.2, revision_margin=0.0, slots=slots)
+    stream.synchronize()
+    c, p, u = oracle.display_token_statistics(ids, lg)
+    assert torch.equal(out.token_ids.cpu(),
+                       oracle.refine_display_from_statistics(ids, c, p, u, 0, 1, 0.5, 0.2, 0.0))
+    roll = oracle.rollout_slot_transition(slots.occupancy, slots.allocation_logits,
+                                          slots.lifecycle_logits, slots.revision_logits,
+                                          slots.input_lifecycle, 0.5, 8, 3)
+    for a, b in zip(out.rollout, roll):
+        assert torch.equal(a.cpu(), b)
+    snap = oracle.materialize_cell_snapshot(slots.semantic, slots.role_logits, slots.uncertainty,
+                                            slots.noise_delta, slots.lifecycle_logits, roll[5],
+                                            slots.semantic_indices)
+    torch.testing.assert_close(out.snapshot.cpu(), snap, rtol=2.5e-7, atol=1e-12)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible CUDA devices")
+def test_tensor_device_not_current_device() -> None:
+    """reference tests/test_cuda.py:371-389: ops run on the tensors' device."""
+    import cid_engine
+
+    cur = torch.cuda.current_device()
+    dev = torch.device("cuda", 1 if cur == 0 else 0)
+    occ = torch.tensor([[0.0, 0.0, 1.0, 0.0]], device=dev)
+    lg = torch.tensor([[8.0, 7.0, -5.0, 6.0]], device=dev)
+    out = cid_engine.prefix_allocation_mask(occ, lg, threshold=0.5, max_allocations=2)
+    assert out.device == dev and torch.cuda.current_device() == cur
+    assert torch.equal(out.cpu(), oracle.prefix_allocation_mask(occ, lg, 0.5, 2))
