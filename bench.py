@@ -50,8 +50,9 @@ REVEAL, REVISION, MARGIN = 0.25, 0.1, 0.05
 CFG2 = dict(B=32, L=1024, V=128256)
 CFG4 = dict(B=64, L=4096, V=152064)
 CFG5 = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64)
-# DRAM bytes (read + write) per launch of the statistics kernel measured by
-# ncu on the cfg2 row shape (summary: profiles/display_stats_bf16_cfg2.md);
+# DRAM bytes (read + write) per row of the statistics kernel, measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum) on a [1, 4096, 128256] bf16
+# launch and divided by its 4096 rows; traffic grows in proportion to rows.
 # None until captured.
 NCU_TRAFFIC_PER_ROW = None
 

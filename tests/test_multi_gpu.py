@@ -1,0 +1,74 @@
+"""Vocabulary-parallel statistics over NCCL on 2+ GPUs of one node.
+
+Each rank holds one contiguous vocabulary shard of the same seeded logits;
+``cid_engine.parallel.vocab_parallel_statistics`` (device records -> NCCL
+all-gather -> device combine) must equal the unsharded statistics computed
+on one GPU: argmax exactly, confidences within the statistics tolerance.
+Ranks run as spawned child processes with NVLS off and a short process-group
+timeout.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    for p in (ROOT, ROOT / "tests" / "golden", ROOT / "cid-engine_b200"):
+        sys.path.insert(0, str(p))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    import cid_engine
+    from cid_engine import parallel
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        for V, dtype in ((50021, torch.bfloat16), (152064, torch.bfloat16), (9001, torch.float32)):
+            g = torch.Generator(device=dev).manual_seed(V)
+            logits = (torch.randn(2, 96, V, generator=g, device=dev) * 2).to(dtype)
+            logits[0, 5, V - 3] = 30.0
+            logits[1, 9, [1, V - 2]] = 40.0  # cross-shard tie: lowest column wins
+            logits[1, 10, V // 2] = float("nan")
+            ids = torch.randint(V, (2, 96), generator=g, device=dev)
+            offs = parallel.shard_offsets(V, world)
+            shard = logits[..., offs[rank]:offs[rank + 1]].contiguous()
+            conf, pred, cur = parallel.vocab_parallel_statistics(ids, shard, total_vocab=V)
+            e_conf, e_pred, e_cur = cid_engine.display_token_statistics(ids, logits)
+            assert torch.equal(pred, e_pred)
+            torch.testing.assert_close(conf, e_conf, rtol=2e-5, atol=2e-6, equal_nan=True)
+            torch.testing.assert_close(cur, e_cur, rtol=2e-5, atol=2e-6, equal_nan=True)
+        torch.cuda.synchronize()
+        Path(result_dir, f"ok{rank}").write_text("ok")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two visible CUDA devices")
+def test_vocab_parallel_statistics_over_nccl(tmp_path) -> None:
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 4)
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    assert sorted(p.name for p in tmp_path.iterdir()) == [f"ok{r}" for r in range(world)]
