@@ -53,8 +53,7 @@ CFG5 = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64
 # DRAM bytes (read + write) per row of the statistics kernel, measured by ncu
 # (dram__bytes_read.sum + dram__bytes_write.sum) on a [1, 4096, 128256] bf16
 # launch and divided by its 4096 rows; traffic grows in proportion to rows.
-# None until captured.
-NCU_TRAFFIC_PER_ROW = None
+NCU_TRAFFIC_PER_ROW = (1_051_941_000 + 3_446_016) / 4096
 
 
 def _peaks() -> tuple[float, str]:
@@ -274,7 +273,7 @@ def bench_single(args) -> dict:
     kern_ms = statistics.mean(kern)
     peak, peak_kind = _peaks()
     achieved = alg_bytes / (kern_ms * 1e-3) / 1e9
-    traffic = None if NCU_TRAFFIC_PER_ROW is None else NCU_TRAFFIC_PER_ROW * rows
+    traffic = None if NCU_TRAFFIC_PER_ROW is None else round(NCU_TRAFFIC_PER_ROW * rows)
 
     # end-to-end through the public API from pinned host memory
     e2e = None
@@ -359,20 +358,42 @@ def bench_refine_loop(dev) -> dict:
             slot.occupancy = out.next_occupancy
         return ids
 
+    occ0 = slot.occupancy.clone()
     run(3)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    slot.occupancy = occ0.clone()
     a.record()
     run(c["steps"])
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / c["steps"]
+    # the same 64 steps captured once in a CUDA graph and replayed
+    slot.occupancy = occ0.clone()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run(2)  # warm-up on the capture stream
+    torch.cuda.current_stream().wait_stream(side)
+    slot.occupancy = occ0.clone()
+    with torch.cuda.graph(graph):
+        run(c["steps"])
+    graph.replay()
+    torch.cuda.synchronize()
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms_graph = a.elapsed_time(b) / c["steps"]
+    del graph
     logits_bytes = B * L * V * 2
     peak, _ = _peaks()
     del ring
     torch.cuda.empty_cache()
     return {"workload": "refine loop B=256 L=512 V=32000 bf16, S=128, 64 steps",
             "steps_per_s": round(1e3 / ms, 2), "ms_per_step": round(ms, 4),
+            "graph_steps_per_s": round(1e3 / ms_graph, 2), "graph_ms_per_step": round(ms_graph, 4),
             "logits_GBps": round(logits_bytes / (ms * 1e-3) / 1e9, 1),
             "roofline_steps_per_s": round(peak * 1e9 / logits_bytes, 1),
             "launches_per_step": 6}
@@ -406,6 +427,24 @@ def bench_reference(args) -> dict:
     }
 
 
+def profile_case(name: str) -> None:
+    """Small launches for ncu: three statistics launches on a case just large
+    enough to leave L2 (CTA-per-row kernel: [1, 4096, 128256] bf16, 1.05 GB;
+    warp-per-row kernel: [1, 40960, 32000] bf16, 2.6 GB)."""
+    import torch
+
+    import cid_engine
+
+    shape = {"cta": (1, 4096, 128256), "rows": (1, 40960, 32000)}[name]
+    g = torch.Generator(device="cuda").manual_seed(1)
+    lg = torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) * 2
+    ids = torch.randint(0, shape[2], shape[:2], device="cuda")
+    for _ in range(3):
+        c, p, u = cid_engine.display_token_statistics(ids, lg)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": name, "shape": shape, "mean_conf": float(c.mean())}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -419,6 +458,8 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-min-reps", type=int, default=3)
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--profile-case", choices=("cta", "rows"), default=None,
+                    help="run a small statistics case for ncu and exit")
     ap.add_argument("--sample-b", type=int, default=1)
     ap.add_argument("--sample-l", type=int, default=1024)
     ap.add_argument("--sample-v", type=int, default=128256)
@@ -427,6 +468,9 @@ def main() -> None:
 
     if args.cpu_worker:
         cpu_reference_worker(args)
+        return
+    if args.profile_case:
+        profile_case(args.profile_case)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

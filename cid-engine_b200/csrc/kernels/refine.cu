@@ -14,10 +14,10 @@
 //      confidence, revise the top min(#candidates, ceil(n_visible * revision))
 //      visible positions by gain (float32 margin), and expand the EOS;
 //   4. mask every position after the first EOS of the result.
-// "Top-k by key, descending, stable" is computed as a 32-step radix select of
-// the k-th largest key (keys mapped to order-preserving integers) followed by
-// an index-ordered scan of the keys equal to it, which selects exactly the
-// positions std::stable_sort(>) would put first.
+// "Top-k by key, descending, stable" is computed as a radix select of the
+// k-th largest key (keys mapped to order-preserving integers, 8 bits per pass)
+// followed by an index-ordered scan of the keys equal to it, which selects
+// exactly the positions std::stable_sort(>) would put first.
 #include <climits>
 #include <cmath>
 
@@ -61,6 +61,9 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 struct Scratch {
   int64_t i64[kWarps];
   uint32_t u32[kWarps];
+  int hist[256];       // radix-select histogram
+  uint32_t sel_digit;  // radix-select result of the current pass
+  int64_t sel_above;
 };
 
 __device__ __forceinline__ int64_t block_sum(int64_t v, Scratch& s) {
@@ -106,20 +109,64 @@ __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, Scratch& s) {
 
 // Selects the k positions of [0, L) with elig(i) that come first in a stable
 // descending sort by key(i); calls take(i) for each (from any thread).
+// The k-th largest order key T is found by a 4-pass radix select (8 bits per
+// pass, most significant first, shared-memory histogram); every position with
+// a key above T is taken, and of those equal to T the first `need` in index
+// order.
 template <typename Elig, typename Key, typename Take>
 __device__ void select_top_k(int64_t L, int64_t k, Elig elig, Key key, Take take, Scratch& s) {
   if (k <= 0) return;
-  // k-th largest order key: largest T with count(key >= T) >= k
-  uint32_t T = 0u;
-  for (int b = 31; b >= 0; --b) {
-    const uint32_t trial = T | (1u << b);
-    int64_t c = 0;
-    for (int64_t i = threadIdx.x; i < L; i += kT) c += (elig(i) && order_key(key(i)) >= trial) ? 1 : 0;
-    if (block_sum(c, s) >= k) T = trial;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t prefix = 0u;  // decided high bits of T
+  int64_t above = 0;     // eligible keys strictly above the prefix range
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const uint32_t hi_mask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));
+    for (int i = threadIdx.x; i < 256; i += kT) s.hist[i] = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < L; i += kT) {
+      if (!elig(i)) continue;
+      const uint32_t u = order_key(key(i));
+      if ((u & hi_mask) == prefix) atomicAdd(&s.hist[(u >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l owns digits 255-8l .. 248-8l (descending); find the digit where
+      // the count from the top first reaches k
+      int h[8];
+      int sum = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        h[j] = s.hist[255 - (lane * 8 + j)];
+        sum += h[j];
+      }
+      int incl = sum;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += o;
+      }
+      int64_t running = above + (incl - sum);
+      const bool mine = running < k && running + sum >= k;
+      if (mine) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (running + h[j] >= k) {
+            s.sel_digit = static_cast<uint32_t>(255 - (lane * 8 + j));
+            s.sel_above = running;
+            break;
+          }
+          running += h[j];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= s.sel_digit << shift;
+    above = s.sel_above;
+    __syncthreads();
   }
-  int64_t gt = 0;
-  for (int64_t i = threadIdx.x; i < L; i += kT) gt += (elig(i) && order_key(key(i)) > T) ? 1 : 0;
-  const int64_t need = k - block_sum(gt, s);  // ties at T to take, by index
+  const uint32_t T = prefix;
+  const int64_t need = k - above;  // ties at T to take, by index
   for (int64_t i = threadIdx.x; i < L; i += kT)
     if (elig(i) && order_key(key(i)) > T) take(i);
   // ties: contiguous ownership so that the scan follows index order
