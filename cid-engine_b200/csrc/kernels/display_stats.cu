@@ -19,10 +19,10 @@
 //    raised its maximum (two predicated selects, no branch); once the row
 //    maximum is known, the threads holding it re-read that one chunk to find
 //    their first column and the smallest wins;
-//  * 16-byte streaming loads (ld.global.cs), CID_STATS_UNROLL in flight per
-//    thread; the chunk maximum is taken on the packed words (max.bf16x2 /
-//    max.f16x2); the exp2 arguments and the sums use packed fma.rn.f32x2 /
-//    add.rn.f32x2 (sm_100);
+//  * 32-byte streaming loads (sm_100 ld.global.nc.v8.b32; rows are peeled to
+//    32-byte alignment), 4 in flight per thread; the chunk maximum is
+//    taken on the packed words (max.bf16x2 / max.f16x2); the exp2 arguments
+//    and the sums use packed fma.rn.f32x2 / add.rn.f32x2 (sm_100);
 //  * rows shorter than the device's appetite are split across a thread-block
 //    cluster; partial states are merged through distributed shared memory in
 //    cluster-rank order (deterministic);
@@ -44,11 +44,7 @@ namespace {
 #ifndef CID_STATS_THREADS
 #define CID_STATS_THREADS 256
 #endif
-#ifndef CID_STATS_UNROLL
-#define CID_STATS_UNROLL 8
-#endif
 constexpr int kThreads = CID_STATS_THREADS;  // threads per CTA
-constexpr int kUnroll = CID_STATS_UNROLL;    // 16-byte loads in flight per thread
 constexpr int kMaxCluster = 8;
 constexpr float kGap = 5.0f;  // natural-log units; terms stay <= e^5
 constexpr int64_t kNone = LLONG_MAX;
@@ -312,41 +308,74 @@ __device__ __forceinline__ void consume_scalar(Acc& a, float x, int64_t col, con
   a.s0 += ex2(fmaf(x, kLog2e, -a.off));
 }
 
+// A 32-byte vector: two 16-byte halves, read with one sm_100 256-bit load on
+// the non-coherent path without L1 allocation (every logit is read once).
+struct Vec32 {
+  uint4 lo, hi;
+};
+constexpr int kVecBytes = 32;
+
+__device__ __forceinline__ Vec32 load_vec32(const Vec32* p) {
+  Vec32 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.lo.x), "=r"(v.lo.y), "=r"(v.lo.z), "=r"(v.lo.w), "=r"(v.hi.x),
+                 "=r"(v.hi.y), "=r"(v.hi.z), "=r"(v.hi.w)
+               : "l"(p));
+  return v;
+}
+
+// -inf in every element (fills the lanes past the end of a thread's range).
+template <typename T>
+__device__ __forceinline__ Vec32 neg_inf_vec32() {
+  if constexpr (sizeof(T) == 8) {
+    const uint4 h = make_uint4(0u, 0xfff00000u, 0u, 0xfff00000u);
+    return Vec32{h, h};
+  } else {
+    const uint32_t w = VecTraits<T>::kNegInfWord;
+    return Vec32{make_uint4(w, w, w, w), make_uint4(w, w, w, w)};
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float vmax32(const Vec32& v) {
+  return fmaxf(VecTraits<T>::vmax(v.lo), VecTraits<T>::vmax(v.hi));
+}
+
+template <typename T>
+__device__ __forceinline__ void to_float32(const Vec32& v, float* x) {
+  VecTraits<T>::to_float(v.lo, x);
+  VecTraits<T>::to_float(v.hi, x + VecTraits<T>::N);
+}
+
 // Streams this thread's share of one row: the unaligned head columns
-// [0, s_head_end), 16-byte vectors [v_beg, v_end) of the aligned region that
-// starts at column `head` (thread t takes v_beg + t, + stride, ...), and the
-// tail columns [s_tail_beg, s_tail_end) — in ascending column order, so a
-// strict `>` keeps each thread's first occurrence of its maximum.
-template <typename T, bool kRep, int kStride>
+// [0, s_head_end), 32-byte vectors [v_beg, v_end) of the aligned region that
+// starts at column `head` (thread t takes v_beg + t, + stride, ...; U loads
+// in flight), and the tail columns [s_tail_beg, s_tail_end) — in ascending
+// column order, so a strict `>` keeps each thread's first occurrence of its
+// maximum.
+template <typename T, bool kRep, int kStride, int U>
 __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_end,
                            int64_t s_head_end, int64_t s_tail_beg, int64_t s_tail_end,
                            const Patch& pt, Acc& a, int tid) {
   using VT = VecTraits<T>;
-  constexpr int N = VT::N;
+  constexpr int N = 2 * VT::N;  // values per 32-byte vector
   for (int64_t c = tid; c < s_head_end; c += kStride) consume_scalar<kRep>(a, VT::scalar(row, c), c, pt);
 
-  const uint4* vrow = reinterpret_cast<const uint4*>(row + head);
-  for (int64_t v = v_beg + tid; v < v_end; v += kStride * kUnroll) {
-    uint4 d[kUnroll];
+  const Vec32* vrow = reinterpret_cast<const Vec32*>(row + head);
+  for (int64_t v = v_beg + tid; v < v_end; v += kStride * U) {
+    Vec32 d[U];
 #pragma unroll
-    for (int k = 0; k < kUnroll; ++k) {
+    for (int k = 0; k < U; ++k) {
       const int64_t vi = v + static_cast<int64_t>(k) * kStride;
-      if (vi < v_end) {
-        d[k] = __ldcs(vrow + vi);
-      } else if constexpr (sizeof(T) == 8) {
-        const uint32_t hi = 0xfff00000u;  // -inf as double: 0xfff0000000000000
-        d[k] = make_uint4(0u, hi, 0u, hi);
-      } else {
-        d[k] = make_uint4(VT::kNegInfWord, VT::kNegInfWord, VT::kNegInfWord, VT::kNegInfWord);
-      }
+      d[k] = vi < v_end ? load_vec32(vrow + vi) : neg_inf_vec32<T>();
     }
     if (kRep) {
       // repetition variant: patched values take part in the maximum
-      float x[kUnroll][N];
+      float x[U][N];
       float cm = -INFINITY;
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        VT::to_float(d[k], x[k]);
+      for (int k = 0; k < U; ++k) {
+        to_float32<T>(d[k], x[k]);
         const int64_t c0 = head + (v + static_cast<int64_t>(k) * kStride) * N;
 #pragma unroll
         for (int j = 0; j < N; ++j) {
@@ -360,7 +389,7 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
       maybe_reoffset(a);
       const float noff = -a.off;
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k)
+      for (int k = 0; k < U; ++k)
 #pragma unroll
         for (int j = 0; j < N; j += 2) {
           float t0, t1;
@@ -369,18 +398,18 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
         }
       continue;
     }
-    float cm = VT::vmax(d[0]);
+    float cm = vmax32<T>(d[0]);
 #pragma unroll
-    for (int k = 1; k < kUnroll; ++k) cm = fmaxf(cm, VT::vmax(d[k]));
+    for (int k = 1; k < U; ++k) cm = fmaxf(cm, vmax32<T>(d[k]));
     const bool up = cm > a.m;  // lazy argmax: remember the chunk only
     a.m = up ? cm : a.m;
     a.where = up ? v : a.where;
     maybe_reoffset(a);
     const float noff = -a.off;
 #pragma unroll
-    for (int k = 0; k < kUnroll; ++k) {
+    for (int k = 0; k < U; ++k) {
       float x[N];
-      VT::to_float(d[k], x);
+      to_float32<T>(d[k], x);
 #pragma unroll
       for (int j = 0; j < N; j += 2) {
         float t0, t1;
@@ -396,19 +425,18 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
 // First column holding `target` among this thread's elements, from the chunk
 // recorded in `where` (re-read from memory); kNone when the thread's maximum
 // is not `target`.
-template <typename T, bool kRep, int kStride>
+template <typename T, bool kRep, int kStride, int U>
 __device__ int64_t first_column(const Acc& a, float target, const T* row, int64_t head,
                                 int64_t v_end, const Patch& pt) {
-  using VT = VecTraits<T>;
-  constexpr int N = VT::N;
+  constexpr int N = 2 * VecTraits<T>::N;
   if (!(a.m == target)) return kNone;
   if (a.where < 0) return -a.where - 1;
-  const uint4* vrow = reinterpret_cast<const uint4*>(row + head);
-  for (int k = 0; k < kUnroll; ++k) {
+  const Vec32* vrow = reinterpret_cast<const Vec32*>(row + head);
+  for (int k = 0; k < U; ++k) {
     const int64_t vi = a.where + static_cast<int64_t>(k) * kStride;
     if (vi >= v_end) break;
     float x[N];
-    VT::to_float(vrow[vi], x);
+    to_float32<T>(vrow[vi], x);
 #pragma unroll
     for (int j = 0; j < N; ++j) {
       const int64_t col = head + vi * N + j;
@@ -503,10 +531,10 @@ __device__ void write_normal(const StatsParams& p, int64_t row, const T* rowp, i
   }
 }
 
-template <typename T, bool kRep, Mode kMode>
+template <typename T, bool kRep, Mode kMode, int U>
 __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) {
   using VT = VecTraits<T>;
-  constexpr int N = VT::N;
+  constexpr int N = 2 * VT::N;
   __shared__ Partial warp_parts[kThreads / 32];
   __shared__ Partial cta_part;   // this CTA's merged partial
   __shared__ Partial row_part;   // the row's merged partial (rank 0 -> all)
@@ -531,7 +559,7 @@ __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) 
 
   // split the row: unaligned head, 16-byte vectors, tail
   const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp);
-  int64_t head = static_cast<int64_t>(((16 - (addr & 15)) & 15) / sizeof(T));
+  int64_t head = static_cast<int64_t>(((kVecBytes - (addr & (kVecBytes - 1))) & (kVecBytes - 1)) / sizeof(T));
   if (head > V) head = V;
   const int64_t nvec = (V - head) / N;
   const int64_t tail_beg = head + nvec * N;
@@ -541,7 +569,7 @@ __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) 
   const int64_t t_beg = rank == nrank - 1 ? tail_beg : V;
 
   Acc a{-INFINITY, -INFINITY, 0.0f, 0.0f, 0.0f, kNone};
-  stream_row<T, kRep, kThreads>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
+  stream_row<T, kRep, kThreads, U>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
   Partial mine{a.m, a.om, a.off, a.s0 + a.s1};
   const Partial cta = block_merge(mine, warp_parts, &cta_part);
 
@@ -561,7 +589,7 @@ __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) 
 
   // first column of the maximum: threads that hold it re-read their chunk
   int64_t col = kNone;
-  if (!special) col = first_column<T, kRep, kThreads>(a, fin.m, rowp, head, v_end, pt);
+  if (!special) col = first_column<T, kRep, kThreads, U>(a, fin.m, rowp, head, v_end, pt);
   col = block_min_i64(col, red);
   if (threadIdx.x == 0) cta_col = col;
   if (nrank > 1) {
@@ -600,10 +628,10 @@ __device__ __forceinline__ int64_t warp_min_i64(int64_t v) {
   return v;
 }
 
-template <typename T, bool kRep, Mode kMode>
+template <typename T, bool kRep, Mode kMode, int U>
 __global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(StatsParams p) {
   using VT = VecTraits<T>;
-  constexpr int N = VT::N;
+  constexpr int N = 2 * VT::N;
   __shared__ Patch patches[kRowWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kRowWarps + warp;
@@ -618,13 +646,13 @@ __global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(Stat
   const T* rowp = static_cast<const T*>(p.logits) + row * p.row_stride;
   const int64_t V = p.vocab;
   const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp);
-  int64_t head = static_cast<int64_t>(((16 - (addr & 15)) & 15) / sizeof(T));
+  int64_t head = static_cast<int64_t>(((kVecBytes - (addr & (kVecBytes - 1))) & (kVecBytes - 1)) / sizeof(T));
   if (head > V) head = V;
   const int64_t nvec = (V - head) / N;
   const int64_t tail_beg = head + nvec * N;
 
   Acc a{-INFINITY, -INFINITY, 0.0f, 0.0f, 0.0f, kNone};
-  stream_row<T, kRep, 32>(rowp, head, 0, nvec, head, tail_beg, V, pt, a, lane);
+  stream_row<T, kRep, 32, U>(rowp, head, 0, nvec, head, tail_beg, V, pt, a, lane);
   Partial fin{a.m, a.om, a.off, a.s0 + a.s1};
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) fin = merge(fin, shfl_xor(fin, d));
@@ -642,7 +670,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(Stat
     if (lane == 0) write_special<T, kMode>(p, row, rowp, V, fin.m, first_nan, first_max);
     return;
   }
-  const int64_t col = warp_min_i64(first_column<T, kRep, 32>(a, fin.m, rowp, head, nvec, pt));
+  const int64_t col = warp_min_i64(first_column<T, kRep, 32, U>(a, fin.m, rowp, head, nvec, pt));
   if (lane == 0) write_normal<T, kRep, kMode>(p, row, rowp, V, pt, fin, col);
 }
 
@@ -717,21 +745,25 @@ __global__ void combine_records_kernel(CombineParams p) {
 // Launch helpers
 // ---------------------------------------------------------------------------
 
+// 32-byte loads in flight per thread, both kernels (measured: 8 raises the
+// CTA kernel to 98 registers and 2 resident CTAs per SM, which is slower).
+constexpr int kUnroll = 4;
+
 // Cluster size: split rows over P CTAs (power of two, <= 8) until the grid
 // holds at least two waves of resident CTAs, while each CTA keeps at least
-// two full iterations of 16-byte loads.
+// two full iterations of 32-byte loads.
 template <typename T, bool kRep, Mode kMode>
 int cluster_size(int64_t rows, int64_t vocab) {
   static int resident_per_sm = 0;  // per template instance, from the occupancy API
   if (resident_per_sm == 0) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, display_stats_kernel<T, kRep, kMode>,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, display_stats_kernel<T, kRep, kMode, kUnroll>,
                                                       kThreads, 0) != cudaSuccess || n <= 0)
       n = 4;
     resident_per_sm = n;
   }
   const int64_t want = 2LL * sm_count() * resident_per_sm;
-  const int64_t vecs = vocab * static_cast<int64_t>(sizeof(T)) / 16;
+  const int64_t vecs = vocab * static_cast<int64_t>(sizeof(T)) / kVecBytes;
   const int64_t min_vecs = 2LL * kThreads * kUnroll;
   int P = 1;
   while (P < kMaxCluster && rows * P < want && vecs / (2 * P) >= min_vecs) P *= 2;
@@ -750,24 +782,18 @@ bool use_row_warps(int64_t rows) {
   static int warps_per_sm = 0;
   if (warps_per_sm == 0) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, display_stats_rows_kernel<T, kRep, kMode>,
-                                                      kRowWarps * 32, 0) != cudaSuccess || n <= 0)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &n, display_stats_rows_kernel<T, kRep, kMode, kUnroll>, kRowWarps * 32, 0) !=
+            cudaSuccess ||
+        n <= 0)
       n = 8;
     warps_per_sm = n * kRowWarps;
   }
   return rows >= 8LL * sm_count() * warps_per_sm;
 }
 
-template <typename T, bool kRep, Mode kMode>
-int launch_stats(const StatsParams& prm, cudaStream_t stream) {
-  if (use_row_warps<T, kRep, kMode>(prm.rows)) {
-    const int64_t blocks = (prm.rows + kRowWarps - 1) / kRowWarps;
-    if (blocks > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
-    display_stats_rows_kernel<T, kRep, kMode>
-        <<<static_cast<unsigned>(blocks), kRowWarps * 32, 0, stream>>>(prm);
-    return launch_result();
-  }
-  const int P = cluster_size<T, kRep, kMode>(prm.rows, prm.vocab);
+template <typename T, bool kRep, Mode kMode, int U>
+int launch_cta_kernel(const StatsParams& prm, int P, cudaStream_t stream) {
   const int64_t blocks = prm.rows * P;
   if (blocks > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
   cudaLaunchConfig_t cfg = {};
@@ -781,8 +807,20 @@ int launch_stats(const StatsParams& prm, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, display_stats_kernel<T, kRep, kMode>, prm);
-  return record_cuda_error(err);
+  return record_cuda_error(cudaLaunchKernelEx(&cfg, display_stats_kernel<T, kRep, kMode, U>, prm));
+}
+
+template <typename T, bool kRep, Mode kMode>
+int launch_stats(const StatsParams& prm, cudaStream_t stream) {
+  if (use_row_warps<T, kRep, kMode>(prm.rows)) {
+    const int64_t blocks = (prm.rows + kRowWarps - 1) / kRowWarps;
+    if (blocks > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+    display_stats_rows_kernel<T, kRep, kMode, kUnroll>
+        <<<static_cast<unsigned>(blocks), kRowWarps * 32, 0, stream>>>(prm);
+    return launch_result();
+  }
+  const int P = cluster_size<T, kRep, kMode>(prm.rows, prm.vocab);
+  return launch_cta_kernel<T, kRep, kMode, kUnroll>(prm, P, stream);
 }
 
 template <bool kRep, Mode kMode>
