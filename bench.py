@@ -50,10 +50,11 @@ REVEAL, REVISION, MARGIN = 0.25, 0.1, 0.05
 CFG2 = dict(B=32, L=1024, V=128256)
 CFG4 = dict(B=64, L=4096, V=152064)
 CFG5 = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64)
-# DRAM bytes (read + write) per row of the statistics kernel, measured by ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum) on a [1, 4096, 128256] bf16
-# launch and divided by its 4096 rows; traffic grows in proportion to rows.
-NCU_TRAFFIC_PER_ROW = (1_051_941_000 + 3_446_016) / 4096
+# DRAM bytes (read + write) per row of the statistics kernel that serves the
+# config-2 shape (warp per row), measured by ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum) on a [1, 10240, 128256] bf16 launch and divided by
+# its 10240 rows; traffic grows in proportion to rows.  None until captured.
+NCU_TRAFFIC_PER_ROW = None
 
 
 def _peaks() -> tuple[float, str]:
@@ -304,7 +305,7 @@ def bench_single(args) -> dict:
                    "l2": "inputs 8.4 GB per step >> 126 MB L2; no flush needed"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "display_stats_kernel<bf16>", "peak_kind": peak_kind,
+                     "kernel": "display_stats_rows_kernel<bf16> (warp per row)", "peak_kind": peak_kind,
                      "kernel_ms": round(kern_ms, 4),
                      "algorithmic_bytes_per_launch": alg_bytes},
         "e2e": e2e,
@@ -428,14 +429,14 @@ def bench_reference(args) -> dict:
 
 
 def profile_case(name: str) -> None:
-    """Small launches for ncu: three statistics launches on a case just large
-    enough to leave L2 (CTA-per-row kernel: [1, 4096, 128256] bf16, 1.05 GB;
-    warp-per-row kernel: [1, 40960, 32000] bf16, 2.6 GB)."""
+    """Small launches for ncu: three statistics launches on the config-2 row
+    shape, large enough to leave L2 (CTA-per-row kernel: [1, 4096, 128256]
+    bf16, 1.05 GB; warp-per-row kernel: [1, 10240, 128256] bf16, 2.6 GB)."""
     import torch
 
     import cid_engine
 
-    shape = {"cta": (1, 4096, 128256), "rows": (1, 40960, 32000)}[name]
+    shape = {"cta": (1, 4096, 128256), "rows": (1, 10240, 128256)}[name]
     g = torch.Generator(device="cuda").manual_seed(1)
     lg = torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) * 2
     ids = torch.randint(0, shape[2], shape[:2], device="cuda")

@@ -31,6 +31,7 @@ CANN_BACKEND_BUILT = bool(_C.cann_backend_built)
 STATUS_TOKEN_ID_OUT_OF_RANGE = 0x1
 STATUS_SEMANTIC_INDEX_OUT_OF_RANGE = 0x2
 STATUS_REPETITION_ID_OUT_OF_RANGE = 0x4
+STATUS_ASSIGNMENT_INVALID = 0x8
 
 
 def device_status(device: int | torch.device = 0, *, reset: bool = False) -> int:

@@ -1,0 +1,144 @@
+// Batched linear assignment (Hungarian method with potentials) for at most 16
+// columns: one warp per batch element, lane j owning column j (lane 0 is the
+// method's virtual column 0).  Semantics of the reference
+// (csrc/ops.cpp:68-175 of fwerkor/cid-engine v1.1.0): costs are read as
+// float32 and every reduced cost, potential and slack is computed in double
+// with the same operations in the same order, so the assignment is
+// bit-identical; among equal slacks the lowest column is taken, as the
+// reference's sequential scan does.
+//
+// The column search of one row ends after at most columns + 1 steps on finite
+// costs; the loop is bounded by that count, and a batch element whose search
+// does not end (non-finite costs) or whose row count lies outside [0, rows]
+// keeps -1 everywhere and sets CID_STATUS_ASSIGNMENT_INVALID.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace cid {
+namespace {
+
+constexpr int kMaxColumns = 16;
+constexpr int kWarpsPerBlock = 4;
+
+struct AssignParams {
+  cid_dtype_t dtype;
+  const void* costs;
+  const int64_t* row_counts;
+  int64_t batch, rows, columns;
+  int64_t* out;
+  uint32_t* status;
+};
+
+__global__ void assignment_kernel(AssignParams p) {
+  __shared__ double u_all[kWarpsPerBlock][kMaxColumns + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t b = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + warp;
+  if (b >= p.batch) return;  // uniform per warp
+  double* u = u_all[warp];
+  const int m = static_cast<int>(p.columns);
+  const int64_t rows = p.rows;
+  for (int64_t r = lane; r < rows; r += 32) p.out[b * rows + r] = -1;
+  __syncwarp();  // the -1 fill is ordered before other lanes' final writes
+  const int64_t active = p.row_counts[b];
+  if (active < 0 || active > rows) {
+    if (lane == 0 && p.status) atomicOr(p.status, CID_STATUS_ASSIGNMENT_INVALID);
+    return;
+  }
+  if (lane <= kMaxColumns) u[lane] = 0.0;
+  __syncwarp();
+  const bool col = lane >= 1 && lane <= m;  // a real column
+  double v = 0.0;                           // potential of column `lane`
+  int pj = 0;                               // row matched to column `lane` (0 = none)
+  int way = 0;
+  const int64_t base = b * rows * m;
+  bool ok = true;
+  for (int row = 1; row <= active && ok; ++row) {
+    if (lane == 0) pj = row;
+    int j0 = 0;
+    double minv = INFINITY;
+    bool used = false;
+    int steps = 0;
+    for (;;) {
+      if (lane == j0) used = true;
+      const int i0 = __shfl_sync(0xffffffffu, pj, j0);
+      // reduced costs of the unused columns, in double: (c - u[i0]) - v[j]
+      if (col && !used) {
+        const double c = static_cast<double>(
+            load_float(p.dtype, p.costs, base + static_cast<int64_t>(i0 - 1) * m + (lane - 1)));
+        const double cur = __dsub_rn(__dsub_rn(c, u[i0]), v);
+        if (cur < minv) {
+          minv = cur;
+          way = j0;
+        }
+      }
+      // delta = smallest slack among unused columns, lowest column on ties;
+      // only values below +inf can be chosen (the reference's strict `<`)
+      double dv = (col && !used && minv < INFINITY) ? minv : INFINITY;
+      int dj = (col && !used && minv < INFINITY) ? lane : 0;
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) {
+        const double ov = __shfl_xor_sync(0xffffffffu, dv, d);
+        const int oj = __shfl_xor_sync(0xffffffffu, dj, d);
+        if (oj != 0 && (dj == 0 || ov < dv || (ov == dv && oj < dj))) {
+          dv = ov;
+          dj = oj;
+        }
+      }
+      const double delta = dv;
+      const int j1 = dj;
+      // potentials: u[p[j]] += delta, v[j] -= delta for used columns (each
+      // used column holds a distinct row); slack -= delta for the others
+      if (lane <= m) {
+        if (used) {
+          u[pj] = __dadd_rn(u[pj], delta);
+          v = __dsub_rn(v, delta);
+        } else {
+          minv = __dsub_rn(minv, delta);
+        }
+      }
+      __syncwarp();
+      j0 = j1;
+      const int pj0 = __shfl_sync(0xffffffffu, pj, j0);
+      if (pj0 == 0) break;
+      if (++steps > m + 1 || j1 == 0) {  // no free column reachable: give up
+        ok = false;
+        break;
+      }
+    }
+    if (!ok) break;
+    // augment along `way` back to the virtual column
+    for (int k = 0; k <= m + 1; ++k) {
+      const int j1 = __shfl_sync(0xffffffffu, way, j0);
+      const int pnew = __shfl_sync(0xffffffffu, pj, j1);
+      if (lane == j0) pj = pnew;
+      j0 = j1;
+      if (j0 == 0) break;
+    }
+  }
+  if (!ok) {
+    if (lane == 0 && p.status) atomicOr(p.status, CID_STATUS_ASSIGNMENT_INVALID);
+    return;
+  }
+  if (col && pj > 0 && pj <= active) p.out[b * rows + (pj - 1)] = lane - 1;
+}
+
+}  // namespace
+}  // namespace cid
+
+using namespace cid;
+
+extern "C" int cid_batched_linear_assignment(cid_dtype_t cost_dtype, const void* costs,
+                                             const int64_t* row_counts, int64_t batch,
+                                             int64_t rows, int64_t columns, int64_t* out,
+                                             uint32_t* status, void* stream) {
+  if (!is_float_dtype(cost_dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || rows < 0 || columns < 0 || rows > columns || columns > kMaxColumns)
+    return CID_ERR_INVALID_ARGUMENT;  // csrc/ops.cpp:71-86
+  if (batch == 0 || rows == 0) return CID_OK;
+  if (!costs || !row_counts || !out) return CID_ERR_INVALID_ARGUMENT;
+  AssignParams p{cost_dtype, costs, row_counts, batch, rows, columns, out, status};
+  const int64_t blocks = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  assignment_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, as_stream(stream)>>>(p);
+  return launch_result();
+}

@@ -334,7 +334,7 @@ at::Tensor prefix_allocation_mask(Backend backend, const at::Tensor& occupancy_i
 }
 
 // ---------------------------------------------------------------------------
-// batched_linear_assignment — csrc/ops.cpp:68-175 (outside the display path)
+// batched_linear_assignment — csrc/ops.cpp:68-175
 // ---------------------------------------------------------------------------
 
 at::Tensor batched_linear_assignment(Backend backend, const at::Tensor& costs,
@@ -346,11 +346,20 @@ at::Tensor batched_linear_assignment(Backend backend, const at::Tensor& costs,
   TORCH_CHECK(row_counts.dim() == 1 && row_counts.size(0) == costs.size(0),
               "row_counts must have shape [batch]");
   TORCH_CHECK(row_counts.scalar_type() == at::kLong, "row_counts must use torch.int64");
+  same_device("batched_linear_assignment", {&costs, &row_counts});
   auto out = at::empty({costs.size(0), costs.size(1)}, costs.options().dtype(at::kLong));
   if (backend == Backend::kMeta) return out;
-  TORCH_CHECK(false,
-              "batched_linear_assignment (slot matching) is not part of the B200 "
-              "display-refinement build");
+  if (backend == Backend::kCpu) detail::no_cpu_backend("batched_linear_assignment");
+  if (out.numel() == 0) return out;
+  const c10::cuda::CUDAGuard guard(costs.device());
+  auto c = costs.contiguous();
+  auto counts = row_counts.contiguous();
+  check_result(cid_batched_linear_assignment(dt(c), c.data_ptr(), counts.data_ptr<std::int64_t>(),
+                                             c.size(0), c.size(1), c.size(2),
+                                             out.data_ptr<std::int64_t>(),
+                                             detail::status_word(c.device()), stream_of(c)),
+               "batched_linear_assignment");
+  return out;
 }
 
 // ---------------------------------------------------------------------------

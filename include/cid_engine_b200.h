@@ -63,6 +63,7 @@ typedef enum cid_result {
 #define CID_STATUS_TOKEN_ID_OUT_OF_RANGE 0x1u
 #define CID_STATUS_SEMANTIC_INDEX_OUT_OF_RANGE 0x2u
 #define CID_STATUS_REPETITION_ID_OUT_OF_RANGE 0x4u
+#define CID_STATUS_ASSIGNMENT_INVALID 0x8u
 
 CID_API int cid_abi_version(void);
 CID_API const char* cid_result_string(int result);
@@ -201,6 +202,21 @@ CID_API int cid_materialize_cell_snapshot(
     int64_t lifecycles, const uint8_t* selected, const int64_t* indices,
     int64_t nindices, int64_t rows, float* out, uint32_t* status,
     void* stream);
+
+/* batched_linear_assignment — replaces csrc/registration.cpp:12-13,
+ * csrc/ops.cpp:68-175, csrc/cuda/linear_assignment.cu.
+ * costs: batch x rows x columns of cost_dtype (read as float32, solved in
+ * double), rows <= columns <= 16; row_counts: batch int64 (active rows);
+ * out: batch x rows int64, the column assigned to each active row, -1
+ * elsewhere.  A row count outside [0, rows], or costs for which the search
+ * cannot complete (non-finite), leave that batch element at -1 and set
+ * CID_STATUS_ASSIGNMENT_INVALID. */
+CID_API int cid_batched_linear_assignment(cid_dtype_t cost_dtype,
+                                          const void* costs,
+                                          const int64_t* row_counts,
+                                          int64_t batch, int64_t rows,
+                                          int64_t columns, int64_t* out,
+                                          uint32_t* status, void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* Training corruption                                                     */

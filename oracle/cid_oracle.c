@@ -896,3 +896,68 @@ int cid_oracle_combine_records(const void* records_in, int world,
   }
   return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* batched_linear_assignment — csrc/ops.cpp:68-175 (Hungarian method with    */
+/* potentials, double precision, first column on ties).                      */
+/* ------------------------------------------------------------------------ */
+
+int cid_oracle_linear_assignment(int dtype, const void* costs,
+                                 const int64_t* row_counts, int64_t batch,
+                                 int64_t rows, int64_t columns, int64_t* out) {
+  if (rows > columns || columns > 16) return -1; /* :73-78 */
+  for (int64_t b = 0; b < batch; ++b) {
+    const int64_t active = row_counts[b];
+    if (active < 0 || active > rows) return -1; /* :104-106 */
+    for (int64_t r = 0; r < rows; ++r) out[b * rows + r] = -1;
+    if (active == 0) continue;
+    double u[17] = {0}, v[17] = {0};
+    int64_t p[17] = {0}, way[17] = {0};
+    const int64_t base = b * rows * columns;
+    for (int64_t row = 1; row <= active; ++row) {
+      p[0] = row;
+      int64_t j0 = 0;
+      double minv[17];
+      int used[17] = {0};
+      for (int64_t j = 0; j <= columns; ++j) minv[j] = INFINITY;
+      int steps = 0;
+      do {
+        used[j0] = 1;
+        const int64_t i0 = p[j0];
+        double delta = INFINITY;
+        int64_t j1 = 0;
+        for (int64_t j = 1; j <= columns; ++j) {
+          if (used[j]) continue;
+          const double c = (double)(float)load(dtype, costs, base + (i0 - 1) * columns + (j - 1));
+          const double cur = c - u[i0] - v[j];
+          if (cur < minv[j]) {
+            minv[j] = cur;
+            way[j] = j0;
+          }
+          if (minv[j] < delta) {
+            delta = minv[j];
+            j1 = j;
+          }
+        }
+        for (int64_t j = 0; j <= columns; ++j) {
+          if (used[j]) {
+            u[p[j]] += delta;
+            v[j] -= delta;
+          } else {
+            minv[j] -= delta;
+          }
+        }
+        j0 = j1;
+        if (++steps > columns + 2) return -3; /* search cannot complete */
+      } while (p[j0] != 0);
+      do {
+        const int64_t j1 = way[j0];
+        p[j0] = p[j1];
+        j0 = j1;
+      } while (j0 != 0);
+    }
+    for (int64_t j = 1; j <= columns; ++j)
+      if (p[j] > 0 && p[j] <= active) out[b * rows + (p[j] - 1)] = j - 1;
+  }
+  return 0;
+}

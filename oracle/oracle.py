@@ -328,3 +328,16 @@ def display_combine_records(records, token_ids, shard_offsets):
             _p(conf), _p(pred), _p(cur),
         )
     return conf, pred, cur
+
+
+def batched_linear_assignment(costs, row_counts):
+    """csrc/ops.cpp:68-175."""
+    c = _host(costs)
+    rc_ = _host(row_counts)
+    b, r, m = c.shape
+    out = torch.empty((b, r), dtype=torch.int64)
+    rc = lib().cid_oracle_linear_assignment(
+        DT[c.dtype], _p(c), _p(rc_), _i(b), _i(r), _i(m), _p(out)
+    )
+    _check(rc, "row_counts values must be in [0, rows]")
+    return out

@@ -683,6 +683,34 @@ def display_corrupt_cases() -> Iterator[Case]:
         yield Case(f"dc/random_{k}", op, [ids, ts, el, torch.rand(b, t, generator=g), rr, ro, 0, eos, v, frac])
 
 
+def assignment_cases() -> Iterator[Case]:
+    op = "batched_linear_assignment"
+    costs = torch.tensor(  # tests/test_engine.py:507-530
+        [[[4.0, 1.0, 3.0, 8.0], [2.0, 0.0, 5.0, 7.0], [3.0, 2.0, 2.0, 6.0], [9.0, 9.0, 9.0, 9.0]],
+         [[1.0, 1.0, 2.0, 3.0], [1.0, 1.0, 2.0, 3.0], [2.0, 2.0, 0.0, 0.0], [4.0, 3.0, 2.0, 1.0]]])
+    yield Case("assign/engine", op, [costs, torch.tensor([3, 4])])
+    yield Case("assign/cpp_kat", op, [costs[:1], torch.tensor([3])])  # tests/cpp/test_ops.cpp:33-53
+    yield Case("assign/first_tie", op, [torch.zeros(2, 8, 8), torch.tensor([4, 8])])  # test_cuda.py:495-502
+    for columns in (4, 8):  # tests/test_cuda.py:427-450 recipe
+        g = _g(1417 + columns)
+        yield Case(
+            f"assign/cuda_{columns}", op,
+            [torch.randn(128, columns, columns, generator=g),
+             torch.randint(0, columns + 1, (128,), generator=g)],
+        )
+    for k in range(24):
+        g = _g(9900 + k)
+        columns = [1, 2, 5, 9, 16, 16][k % 6]
+        rows = max(1, columns - (k % 3))
+        b = 1 + k % 5
+        c = torch.randn(b, rows, columns, generator=g)
+        if k % 4 == 0:
+            c = (c * 2).round()  # many equal costs: tie order matters
+        if k % 4 == 1:
+            c = c.to(torch.float64)
+        yield Case(f"assign/random_{k}", op, [c, torch.randint(0, rows + 1, (b,), generator=g)])
+
+
 ALL: dict[str, Callable[[], Iterator[Case]]] = {
     "stats": stats_cases,
     "repetition": repetition_cases,
@@ -694,6 +722,7 @@ ALL: dict[str, Callable[[], Iterator[Case]]] = {
     "masked_diffusion": masked_diffusion_cases,
     "thought": thought_cases,
     "display_corrupt": display_corrupt_cases,
+    "assignment": assignment_cases,
 }
 
 

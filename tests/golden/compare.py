@@ -26,6 +26,7 @@ TOLERANCES: dict[str, list] = {
     "masked_diffusion_corrupt_from_random": [None, None, None, (1e-6, 0.0)],
     "thought_corrupt_from_epsilon": ["ulp", None, None],
     "display_corrupt_from_random": [None] * 4,
+    "batched_linear_assignment": [None],
 }
 
 

@@ -237,3 +237,39 @@ def test_tensor_device_not_current_device() -> None:
     out = cid_engine.prefix_allocation_mask(occ, lg, threshold=0.5, max_allocations=2)
     assert out.device == dev and torch.cuda.current_device() == cur
     assert torch.equal(out.cpu(), oracle.prefix_allocation_mask(occ, lg, 0.5, 2))
+
+
+def test_assignment_invalid_rows_and_nonfinite_costs_do_not_hang() -> None:
+    """Row counts outside [0, rows] and NaN costs (on which a sequential
+    Hungarian search never ends) leave -1 and set the status bit."""
+    import cid_engine
+
+    cid_engine.device_status(0, reset=True)
+    out = cid_engine.batched_linear_assignment(torch.rand(2, 3, 4, device="cuda"),
+                                               torch.tensor([5, 2], device="cuda"))
+    assert bool((out[0] == -1).all()) and bool((out[1, :2] >= 0).all())
+    assert cid_engine.device_status(0, reset=True) & cid_engine.STATUS_ASSIGNMENT_INVALID
+    nan_costs = torch.full((1, 2, 2), float("nan"), device="cuda")
+    out = cid_engine.batched_linear_assignment(nan_costs, torch.tensor([2], device="cuda"))
+    assert bool((out == -1).all())
+    assert cid_engine.device_status(0, reset=True) & cid_engine.STATUS_ASSIGNMENT_INVALID
+
+
+def test_c_abi_known_answers(tmp_path) -> None:
+    """The reference's C++ KATs through the C ABI from plain C."""
+    import subprocess
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    lib_dir = root / "cid-engine_b200" / "cid_engine"
+    exe = tmp_path / "capi_kats"
+    subprocess.run(
+        ["gcc", "-O1", "-o", str(exe), str(root / "tests" / "cpp" / "capi_kats.c"),
+         f"-I{root / 'include'}", "-I/usr/local/cuda/include", f"-L{lib_dir}",
+         "-l:libcid_engine_b200.so", f"-Wl,-rpath,{lib_dir}", "-L/usr/local/cuda/lib64",
+         "-lcudart", "-Wl,-rpath,/usr/local/cuda/lib64", "-lm"],
+        check=True,
+    )
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stderr
+    assert "passed" in res.stdout
