@@ -53,8 +53,8 @@ CFG5 = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64
 # DRAM bytes (read + write) per row of the statistics kernel that serves the
 # config-2 shape (warp per row), measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on a [1, 10240, 128256] bf16 launch and divided by
-# its 10240 rows; traffic grows in proportion to rows.  None until captured.
-NCU_TRAFFIC_PER_ROW = None
+# its 10240 rows; traffic grows in proportion to rows.
+NCU_TRAFFIC_PER_ROW = (2_631_003_000 + 4_521_216) / 10240
 
 
 def _peaks() -> tuple[float, str]:
@@ -105,13 +105,20 @@ def display_inputs(B, L, V, seed, device, dtype=None):
 
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
+        self.window = None  # (start, end) wall-clock seconds of the timed region
+
+    def mark_start(self) -> None:
+        self.t0 = time.time()
+
+    def mark_end(self) -> None:
+        self.window = (self.t0, time.time())
 
     def __enter__(self):
         try:
@@ -122,6 +129,7 @@ class ClockSampler:
             )
         except OSError:
             self.proc = None
+        time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
         return self
 
     def __exit__(self, *exc):
@@ -137,18 +145,27 @@ class ClockSampler:
             self.lines = []
 
     def summary(self) -> dict:
+        import datetime
+
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
+            if self.window is not None:
+                try:
+                    ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    ts = None
+                if ts is not None and not (self.window[0] - 0.1 <= ts <= self.window[1] + 0.1):
+                    continue
             try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
+                sm.append(float(f[2]))
+                mx = max(mx, float(f[3]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(names, f[6:10]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
@@ -220,12 +237,14 @@ def run_cpu_baseline(sample=(1, 1024, 128256), seconds=10.0) -> dict | None:
 # ---------------------------------------------------------------------------
 
 
-def time_device_steps(step, K, W, stream, kernel_events=None):
+def time_device_steps(step, K, W, stream, clock=None):
     import torch
 
     for _ in range(W):
         step(None)
     torch.cuda.synchronize()
+    if clock is not None:
+        clock.mark_start()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     pairs = []
@@ -236,6 +255,8 @@ def time_device_steps(step, K, W, stream, kernel_events=None):
         step(ev)
     end.record(stream)
     torch.cuda.synchronize()
+    if clock is not None:
+        clock.mark_end()
     total_ms = start.elapsed_time(end)
     kern = [a.elapsed_time(b) for a, b in pairs]
     return total_ms, kern
@@ -264,7 +285,7 @@ def bench_single(args) -> dict:
 
     K, W = args.steps, args.warmup
     with ClockSampler(0) as clk:
-        total_ms, kern = time_device_steps(step, K, W, stream)
+        total_ms, kern = time_device_steps(step, K, W, stream, clk)
     clocks = clk.summary()
     nbytes = logits.numel() * logits.element_size()
     ms = total_ms / K
@@ -449,7 +470,7 @@ def profile_case(name: str) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-e2e", action="store_true")

@@ -123,11 +123,13 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
         pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                  for _ in range(K)]
         with ClockSampler(local) as clk:
+            clk.mark_start()
             a.record()
             for k in range(K):
                 step(pairs[k])
             b.record()
             torch.cuda.synchronize()
+            clk.mark_end()
         dist.barrier()
         torch.cuda.synchronize()
         ms_local = a.elapsed_time(b) / K
@@ -160,7 +162,7 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
                        "l2": f"{shard_bytes / 1e9:.1f} GB per rank per step >> 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "display_stats_kernel<bf16, records> (per rank, max over ranks)",
+                         "kernel": "display_stats_rows_kernel<bf16, records> (per rank, max over ranks)",
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
                          "algorithmic_bytes_per_launch": alg},
             "e2e": None,
