@@ -307,6 +307,7 @@ def bench_single(args) -> dict:
     torch.cuda.empty_cache()
 
     loop = None if args.no_loop else bench_refine_loop(dev)
+    small = None if args.no_loop else bench_small_configs(dev)
     cpu = None if args.no_cpu_baseline else run_cpu_baseline(seconds=args.cpu_seconds)
     line = {
         "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
@@ -334,6 +335,7 @@ def bench_single(args) -> dict:
         "clocks": clocks,
         "cpu_baseline": cpu,
         "refine_loop": loop,
+        "small_configs": small,
     }
     return line
 
@@ -419,6 +421,86 @@ def bench_refine_loop(dev) -> dict:
             "logits_GBps": round(logits_bytes / (ms * 1e-3) / 1e9, 1),
             "roofline_steps_per_s": round(peak * 1e9 / logits_bytes, 1),
             "launches_per_step": 6}
+
+
+def _graph_time_ms(fn, reps: int) -> float:
+    """Per-call device time of `fn` replayed `reps` times inside one CUDA graph."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del graph
+    return a.elapsed_time(b) / reps
+
+
+def bench_small_configs(dev) -> dict:
+    """Config 1 (fp32 [4,256,32000] chain: statistics, refinement, rollout
+    and live occupancy of 32 slots, thought corruption [4,32,512]) and
+    config 3 (masked diffusion [64,2048]); both are launch-bound, so each is
+    timed as CUDA-graph replays (inputs rotate over 8 copies for config 1,
+    1 GB > L2)."""
+    import torch
+
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import cases
+
+    ops = torch.ops.cid_engine
+    ids, logits = cases.cfg1_display()
+    ids, logits = ids.to(dev), logits.to(dev)
+    copies = [logits] + [logits.clone() for _ in range(7)]
+    g = torch.Generator().manual_seed(10)
+    occ = (torch.rand(4, 32, 1, generator=g) < 0.4).float().to(dev)
+    life = torch.zeros(4, 32, 4)
+    life[..., 3] = (torch.rand(4, 32, generator=g) < 0.1).float()
+    life = life.to(dev)
+    al = torch.randn(4, 32, generator=g).to(dev)
+    rv = torch.randn(4, 32, 3, generator=g).to(dev)
+    th = [t.to(dev) for t in cases.cfg1_thought()]
+    state = {"k": 0}
+
+    def cfg1_step():
+        lg = copies[state["k"] % len(copies)]
+        state["k"] += 1
+        c, p, u = ops.display_token_statistics(ids, lg)
+        ops.refine_display_from_statistics(ids, c, p, u, MASK_ID, EOS_ID, REVEAL, REVISION, MARGIN)
+        ops.rollout_slot_transition(occ, al, life, rv, life, 0.5, 8, 3)
+        ops.live_slot_occupancy(occ, life, 3)
+        ops.thought_corrupt_from_epsilon(*th)
+
+    ms1 = _graph_time_ms(cfg1_step, 64)
+    md = [a.to(dev) if isinstance(a, torch.Tensor) else a for a in cases.cfg3_masked_diffusion()]
+
+    def cfg3_call():
+        ops.masked_diffusion_corrupt_from_random(*md)
+
+    ms3 = _graph_time_ms(cfg3_call, 1000)
+    del copies
+    torch.cuda.empty_cache()
+    return {
+        "cfg1_chain": {"workload": "fp32 [4,256,32000] stats+refine, 32 slots rollout+live, "
+                                   "thought [4,32,512]", "us_per_step": round(ms1 * 1e3, 2),
+                       "logits_GBps": round(131_072_000 / (ms1 * 1e-3) / 1e9, 1),
+                       "launches_per_step": 5, "timing": "CUDA graph, 64 steps"},
+        "cfg3_masked_diffusion": {"workload": "ids [64,2048], mask id 50256",
+                                  "us_per_call": round(ms3 * 1e3, 3),
+                                  "GBps": round(2_753_032 / (ms3 * 1e-3) / 1e9, 1),
+                                  "launches_per_call": 2, "timing": "CUDA graph, 1000 calls"},
+    }
 
 
 def bench_reference(args) -> dict:

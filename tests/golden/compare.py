@@ -65,6 +65,8 @@ def assert_matches(op: str, actual, expected, name: str, ambiguous=None) -> None
     shaped like output 0) marks elements where either value is accepted."""
     if isinstance(actual, torch.Tensor):
         actual = (actual,)
+    if isinstance(expected, torch.Tensor):
+        expected = (expected,)
     tols = TOLERANCES[op]
     assert len(actual) == len(expected), name
     for k, (a, e) in enumerate(zip(actual, expected)):

@@ -1,0 +1,192 @@
+"""Property-based differential fuzzing of the CUDA path against the oracle.
+
+The generators follow the reference's fuzz suite (tests/test_fuzz.py of
+fwerkor/cid-engine v1.1.0): random shapes including empty ones, all logit
+dtypes, scales from 0 to 100, strided views, random fractions/margins and EOS
+layouts for the refinement policy, structural insert/delete proposals.  The
+budget is ``CID_ENGINE_FUZZ_EXAMPLES`` (default 60 per test).
+"""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+from hypothesis import HealthCheck, given, settings
+from hypothesis import strategies as st
+
+import cases
+import compare
+from oracle import oracle
+
+pytestmark = [pytest.mark.gpu, pytest.mark.fuzz]
+
+EXAMPLES = int(os.environ.get("CID_ENGINE_FUZZ_EXAMPLES", "60"))
+SETTINGS = settings(max_examples=EXAMPLES, deadline=None, print_blob=True, derandomize=True,
+                    suppress_health_check=[HealthCheck.too_slow])
+DTYPES = st.sampled_from([torch.float16, torch.bfloat16, torch.float32, torch.float64])
+SCALES = st.sampled_from([0.0, 1.0e-4, 0.1, 1.0, 20.0, 100.0])
+UNIT = st.one_of(st.sampled_from([0.0, 1.0, 0.5, 1.0e-7, 1.0 - 1.0e-7]),
+                 st.floats(min_value=0.0, max_value=1.0, allow_nan=False))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _engine():
+    import cid_engine  # noqa: F401
+
+    assert torch.cuda.is_available()
+
+
+def _cuda(t: torch.Tensor) -> torch.Tensor:
+    if t.is_contiguous():
+        return t.cuda()
+    out = torch.empty_strided(t.size(), t.stride(), dtype=t.dtype, device="cuda")
+    out.copy_(t)
+    return out
+
+
+@SETTINGS
+@given(batch=st.integers(0, 4), tokens=st.integers(0, 40), vocab=st.integers(1, 3000),
+       seed=st.integers(0, 2**31 - 1), dtype=DTYPES, scale=SCALES, strided=st.booleans())
+def test_fuzz_display_statistics(batch, tokens, vocab, seed, dtype, scale, strided) -> None:
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(vocab, (batch, tokens), generator=g)
+    lg = (torch.randn(batch, tokens, vocab, generator=g) * scale).to(dtype)
+    if strided:
+        lg = cases._strided_last_dim(lg)
+    out = torch.ops.cid_engine.display_token_statistics(ids.cuda(), _cuda(lg))
+    compare.assert_matches("display_token_statistics", out,
+                           oracle.display_token_statistics(ids, lg), "fuzz stats")
+
+
+@SETTINGS
+@given(batch=st.integers(1, 3), tokens=st.integers(2, 70), vocab=st.integers(4, 300),
+       seed=st.integers(0, 2**31 - 1), dtype=DTYPES, mult=st.floats(0.05, 1.0),
+       with_eos=st.booleans())
+def test_fuzz_repetition(batch, tokens, vocab, seed, dtype, mult, with_eos) -> None:
+    g = torch.Generator().manual_seed(seed)
+    alphabet = torch.tensor([0, 1, 2, 3, vocab - 1])
+    ids = alphabet[torch.randint(len(alphabet), (batch, tokens), generator=g)]
+    lg = (torch.randn(batch, tokens, vocab, generator=g) * 3).to(dtype)
+    eos = 1 if with_eos else None
+    out = torch.ops.cid_engine.display_token_statistics_with_repetition(ids.cuda(), lg.cuda(), 0,
+                                                                        eos, mult)
+    compare.assert_matches("display_token_statistics_with_repetition", out,
+                           oracle.display_token_statistics_with_repetition(ids, lg, 0, eos, mult),
+                           "fuzz repetition")
+
+
+@SETTINGS
+@given(seed=st.integers(0, 2**31 - 1), reveal=UNIT, revision=UNIT,
+       margin=st.one_of(st.sampled_from([0.0, 1.0e-7, 0.01, 0.1, 1.0]),
+                        st.floats(0.0, 1.0, allow_nan=False)),
+       tokens=st.integers(1, 600), batch=st.integers(1, 6), with_eos=st.booleans())
+def test_fuzz_refinement(seed, reveal, revision, margin, tokens, batch, with_eos) -> None:
+    ids, (conf, pred, cur) = cases.refine_inputs_large(seed, batch, tokens)
+    eos = 1 if with_eos else None
+    got = torch.ops.cid_engine.refine_display_from_statistics(
+        ids.cuda(), conf.cuda(), pred.cuda(), cur.cuda(), 0, eos, reveal, revision, margin)
+    exp = oracle.refine_display_from_statistics(ids, conf, pred, cur, 0, eos, reveal, revision,
+                                                margin)
+    assert torch.equal(got.cpu(), exp)
+
+
+@SETTINGS
+@given(seed=st.integers(0, 2**31 - 1), mode=st.sampled_from(["insert", "delete"]))
+def test_fuzz_structural_refinement(seed, mode) -> None:
+    ids, (conf, pred, cur) = cases.refine_inputs_structural(seed, mode)
+    got = torch.ops.cid_engine.refine_display_from_statistics(
+        ids.cuda(), conf.cuda(), pred.cuda(), cur.cuda(), 0, 1, 1.0, 1.0, 0.1)
+    assert torch.equal(got.cpu(), oracle.refine_display_from_statistics(ids, conf, pred, cur, 0,
+                                                                        1, 1.0, 1.0, 0.1))
+
+
+@SETTINGS
+@given(batch=st.integers(0, 6), slots=st.integers(0, 200), seed=st.integers(0, 2**31 - 1),
+       threshold=UNIT, max_extra=st.integers(1, 8), scale=SCALES, rank3=st.booleans(),
+       strided=st.booleans(), dtype=DTYPES)
+def test_fuzz_prefix_allocation(batch, slots, seed, threshold, max_extra, scale, rank3, strided,
+                                dtype) -> None:
+    g = torch.Generator().manual_seed(seed)
+    occ = torch.randint(-1, 2, (batch, slots), generator=g).float()
+    lg = (torch.randn(batch, slots, generator=g) * scale).to(dtype)
+    if rank3:
+        occ = occ.unsqueeze(-1)
+    if strided and slots:
+        lg = cases._strided_last_dim(lg)
+    max_alloc = 1 + (seed % max(1, slots + max_extra))
+    got = torch.ops.cid_engine.prefix_allocation_mask(_cuda(occ), _cuda(lg), threshold, max_alloc)
+    exp = oracle.prefix_allocation_mask(occ, lg, threshold, max_alloc)
+    compare.assert_matches("prefix_allocation_mask", got, exp, "fuzz prefix",
+                           compare.sigmoid_ambiguous(lg, threshold))
+
+
+@SETTINGS
+@given(batch=st.integers(1, 5), slots=st.integers(1, 150), F=st.integers(1, 6),
+       Rv=st.integers(1, 5), seed=st.integers(0, 2**31 - 1), dtype=DTYPES,
+       threshold=UNIT, max_alloc=st.integers(1, 10))
+def test_fuzz_rollout(batch, slots, F, Rv, seed, dtype, threshold, max_alloc) -> None:
+    g = torch.Generator().manual_seed(seed)
+    occ = torch.randint(0, 2, (batch, slots), generator=g).bool()
+    al = torch.randn(batch, slots, generator=g).to(dtype)
+    lc = torch.randint(-2, 3, (batch, slots, F), generator=g).to(dtype)  # ties
+    rv = torch.randn(batch, slots, Rv, generator=g).to(dtype)
+    il = torch.randint(-1, 2, (batch, slots, F), generator=g).to(dtype)
+    r = seed % F
+    got = torch.ops.cid_engine.rollout_slot_transition(occ.cuda(), al.cuda(), lc.cuda(), rv.cuda(),
+                                                       il.cuda(), threshold, max_alloc, r)
+    exp = oracle.rollout_slot_transition(occ, al, lc, rv, il, threshold, max_alloc, r)
+    amb = compare.sigmoid_ambiguous(al, threshold)
+    if bool(amb.any()):
+        return  # the reference's own decision is position-dependent there
+    for a, e in zip(got, exp):
+        assert torch.equal(a.cpu(), e)
+
+
+@SETTINGS
+@given(batch=st.integers(1, 12), tokens=st.integers(1, 3000), seed=st.integers(0, 2**31 - 1),
+       lo=st.floats(1e-6, 1.0), span=st.floats(0.0, 1.0), zero_rows=st.booleans())
+def test_fuzz_masked_diffusion(batch, tokens, seed, lo, span, zero_rows) -> None:
+    hi = min(1.0, lo + span)
+    g = torch.Generator().manual_seed(seed)
+    clean = torch.randint(0, 1000, (batch, tokens), generator=g)
+    rr = torch.rand(batch, 1, generator=g)
+    if zero_rows:
+        rr[::2] = 0.0
+    mr = torch.rand(batch, tokens, generator=g)
+    got = torch.ops.cid_engine.masked_diffusion_corrupt_from_random(clean.cuda(), rr.cuda(),
+                                                                    mr.cuda(), 999, lo, hi)
+    exp = oracle.masked_diffusion_corrupt_from_random(clean, rr, mr, 999, lo, hi)
+    compare.assert_matches("masked_diffusion_corrupt_from_random", got, exp, "fuzz md")
+
+
+@SETTINGS
+@given(batch=st.integers(0, 4), slots=st.integers(0, 40), hidden=st.integers(1, 300),
+       seed=st.integers(0, 2**31 - 1), dtype=st.sampled_from([torch.float32, torch.float64,
+                                                               torch.bfloat16, torch.float16]),
+       tdtype=st.sampled_from([torch.float32, torch.float64, torch.bfloat16]))
+def test_fuzz_thought_corruption(batch, slots, hidden, seed, dtype, tdtype) -> None:
+    g = torch.Generator().manual_seed(seed)
+    sem = torch.randn(batch, slots, hidden, generator=g).to(dtype)
+    eps = torch.randn(batch, slots, hidden, generator=g).to(dtype)
+    ts = (torch.rand(batch, slots, generator=g) * 1.5 - 0.25).to(tdtype)
+    occ = torch.randint(0, 2, (batch, slots, 1), generator=g).to(dtype)
+    got = torch.ops.cid_engine.thought_corrupt_from_epsilon(sem.cuda(), ts.cuda(), occ.cuda(),
+                                                            eps.cuda())
+    compare.assert_matches("thought_corrupt_from_epsilon", got,
+                           oracle.thought_corrupt_from_epsilon(sem, ts, occ, eps), "fuzz thought")
+
+
+@SETTINGS
+@given(batch=st.integers(1, 40), columns=st.integers(1, 16), seed=st.integers(0, 2**31 - 1),
+       integer_costs=st.booleans())
+def test_fuzz_linear_assignment(batch, columns, seed, integer_costs) -> None:
+    g = torch.Generator().manual_seed(seed)
+    rows = 1 + seed % columns
+    costs = torch.randn(batch, rows, columns, generator=g)
+    if integer_costs:
+        costs = (costs * 2).round()
+    counts = torch.randint(0, rows + 1, (batch,), generator=g)
+    got = torch.ops.cid_engine.batched_linear_assignment(costs.cuda(), counts.cuda())
+    assert torch.equal(got.cpu(), oracle.batched_linear_assignment(costs, counts))
