@@ -344,7 +344,8 @@ def bench_refine_loop(dev) -> dict:
     """Config 5: 64 consecutive steps of the fused chain, no host sync."""
     import torch
 
-    from cid_engine.step import SlotInputs, refine_step
+    from cid_engine.loop import DisplayRefineLoop
+    from cid_engine.step import SlotInputs
 
     c = CFG5
     B, L, V, S = c["B"], c["L"], c["V"], c["S"]
@@ -371,56 +372,43 @@ def bench_refine_loop(dev) -> dict:
         semantic_indices=torch.randint(0, c["H"], (c["K"],), generator=g, device=dev),
         threshold=0.5, max_allocations=8, retired_index=3,
     )
-
-    def run(nsteps):
-        ids = ids0
-        for s in range(nsteps):
-            out = refine_step(ids, ring[s % len(ring)], mask_token_id=MASK_ID, eos_token_id=EOS_ID,
-                              reveal_fraction=REVEAL, revision_fraction=REVISION,
-                              revision_margin=MARGIN, slots=slot)
-            ids = out.token_ids
-            slot.occupancy = out.next_occupancy
-        return ids
-
-    occ0 = slot.occupancy.clone()
-    run(3)
-    torch.cuda.synchronize()
+    params = dict(mask_token_id=MASK_ID, eos_token_id=EOS_ID, reveal_fraction=REVEAL,
+                  revision_fraction=REVISION, revision_margin=MARGIN)
+    steps = c["steps"]
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    slot.occupancy = occ0.clone()
-    a.record()
-    run(c["steps"])
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / c["steps"]
-    # the same 64 steps captured once in a CUDA graph and replayed
-    slot.occupancy = occ0.clone()
-    graph = torch.cuda.CUDAGraph()
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        run(2)  # warm-up on the capture stream
-    torch.cuda.current_stream().wait_stream(side)
-    slot.occupancy = occ0.clone()
-    with torch.cuda.graph(graph):
-        run(c["steps"])
-    graph.replay()
-    torch.cuda.synchronize()
-    a.record()
-    graph.replay()
-    b.record()
-    torch.cuda.synchronize()
-    ms_graph = a.elapsed_time(b) / c["steps"]
-    del graph
+    result = {}
+    # eager: every step's operators issued from Python; graph: one replay per
+    # step of the captured chain, with each step's snapshot copied to pinned
+    # host memory on a copy stream (overlapping the next step)
+    for mode, graphs in (("eager", False), ("graph", True)):
+        loop = DisplayRefineLoop(ids0, ring, slots=slot, host_snapshots=4, use_graphs=graphs,
+                                 **params)
+        loop.run(3)
+        loop.drain()
+        loop.reset(ids0, slot.occupancy)
+        torch.cuda.synchronize()
+        a.record()
+        loop.run(steps)
+        b.record()
+        torch.cuda.synchronize()
+        loop.drain()
+        result[mode] = a.elapsed_time(b) / steps
+        snap_bytes = loop.host[0].numel() * 4
+        loop.close()
+    ms, ms_graph = result["eager"], result["graph"]
     logits_bytes = B * L * V * 2
     peak, _ = _peaks()
     del ring
     torch.cuda.empty_cache()
     return {"workload": "refine loop B=256 L=512 V=32000 bf16, S=128, 64 steps",
+            "api": "cid_engine.DisplayRefineLoop",
             "steps_per_s": round(1e3 / ms, 2), "ms_per_step": round(ms, 4),
             "graph_steps_per_s": round(1e3 / ms_graph, 2), "graph_ms_per_step": round(ms_graph, 4),
             "logits_GBps": round(logits_bytes / (ms * 1e-3) / 1e9, 1),
             "roofline_steps_per_s": round(peak * 1e9 / logits_bytes, 1),
-            "launches_per_step": 6}
+            "snapshot_d2h_bytes_per_step": snap_bytes,
+            "launches_per_step": 5,
+            "torch_copies_per_step": 3}
 
 
 def _graph_time_ms(fn, reps: int) -> float:

@@ -260,10 +260,12 @@ def display_combine_records(
 
 
 from cid_engine.step import refine_step  # noqa: E402
+from cid_engine.loop import DisplayRefineLoop  # noqa: E402
 
 __all__ = [
     "CANN_BACKEND_BUILT",
     "CUDA_BACKEND_BUILT",
+    "DisplayRefineLoop",
     "ROCM_BACKEND_BUILT",
     "batched_linear_assignment",
     "device_status",

@@ -17,10 +17,16 @@ from torch import Tensor
 
 class HostStatisticsPipeline:
     """Reusable device buffers + copy stream for host-resident logits of a
-    fixed shape [B, L, V] (any float dtype)."""
+    fixed shape [B, L, V] (any float dtype).
+
+    ``reduce(ids_chunk, logits_chunk)`` is the per-chunk operator, by default
+    ``display_token_statistics``; ``display_shard_records`` of a vocabulary
+    shard fits the same slot.  Its outputs are concatenated along dim 0."""
 
     def __init__(self, batch: int, tokens: int, vocab: int, dtype: torch.dtype,
-                 device: torch.device | int = 0, chunk: int | None = None, buffers: int = 2):
+                 device: torch.device | int = 0, chunk: int | None = None, buffers: int = 2,
+                 reduce=None):
+        self.reduce = reduce or torch.ops.cid_engine.display_token_statistics
         self.device = torch.device("cuda", device) if isinstance(device, int) else device
         self.shape = (batch, tokens, vocab)
         row_bytes = tokens * vocab * torch.empty((), dtype=dtype).element_size()
@@ -38,7 +44,6 @@ class HostStatisticsPipeline:
         assert tuple(logits.shape) == self.shape, "logits shape differs from the pipeline's"
         compute = torch.cuda.current_stream(self.device)
         ids = token_ids.to(self.device, non_blocking=True)
-        ops = torch.ops.cid_engine
         outs = []
         start = torch.cuda.Event()
         start.record(compute)
@@ -54,13 +59,16 @@ class HostStatisticsPipeline:
                 ready = torch.cuda.Event()
                 ready.record(self.copy_stream)
             compute.wait_event(ready)
-            outs.append(ops.display_token_statistics(ids[b0:b1], buf))
+            out = self.reduce(ids[b0:b1], buf)
+            outs.append(out if isinstance(out, tuple) else (out,))
             done = torch.cuda.Event()
             done.record(compute)
             self.free[k] = done
         if len(outs) == 1:
-            return outs[0]
-        return tuple(torch.cat([o[j] for o in outs]) for j in range(3))
+            res = outs[0]
+        else:
+            res = tuple(torch.cat([o[j] for o in outs]) for j in range(len(outs[0])))
+        return res if len(res) > 1 else res[0]
 
 
 def display_token_statistics_from_host(token_ids: Tensor, logits: Tensor, *,

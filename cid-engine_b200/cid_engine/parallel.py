@@ -90,6 +90,62 @@ def sharded_display_inputs(B, L, V, rank, world, seed, device):
     return ids, logits, offs
 
 
+def e2e_vocab_parallel(ids: Tensor, logits: Tensor, offs: list[int], rank: int, *, batch: int,
+                       steps: int, warmup: int) -> dict:
+    """End-to-end vocabulary-parallel step through the public API from pinned
+    host memory on every rank: per step the ids and this rank's logits shard
+    (the first ``batch`` sequences) go host->device, overlapped in chunks with
+    the record kernel (``HostStatisticsPipeline``), the records are
+    all-gathered and combined, the rows refined and the refined ids read
+    back.  Device time, max over ranks."""
+    from cid_engine.host_pipeline import HostStatisticsPipeline
+
+    dev = logits.device
+    V, lo = offs[-1], offs[rank]
+    world = dist.get_world_size()
+    sub = logits[:batch]
+    logits_h = torch.empty(sub.shape, dtype=sub.dtype, pin_memory=True)
+    logits_h.copy_(sub)
+    ids_h = torch.empty(ids[:batch].shape, dtype=ids.dtype, pin_memory=True)
+    ids_h.copy_(ids[:batch])
+    out_h = torch.empty_like(ids_h, pin_memory=True)
+    ops = torch.ops.cid_engine
+    pipe = HostStatisticsPipeline(*sub.shape, dtype=sub.dtype, device=dev,
+                                  reduce=lambda i, x: ops.display_shard_records(i, x, lo, V))
+
+    def step():
+        i = ids_h.to(dev, non_blocking=True)
+        rec = pipe.statistics(i, logits_h)
+        c, p, u = ops.display_combine_records(gather_records(rec), i, offs)
+        refined = ops.refine_display_from_statistics(i, c, p, u, 0, 1, 0.25, 0.1, 0.05)
+        out_h.copy_(refined, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    total = batch * ids.shape[1] * V * logits.element_size()
+    ids_bytes = ids_h.numel() * ids_h.element_size()
+    del pipe, logits_h
+    return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": total + world * ids_bytes,
+            "d2h_bytes_per_step": world * ids_bytes,
+            "ms_per_step": round(ms, 3), "steps": steps,
+            "sample": f"first {batch} of {ids.shape[0]} sequences on every rank (bytes: all ranks)",
+            "api": "cid_engine.host_pipeline (display_shard_records) + parallel.gather_records + "
+                   "display_combine_records + refine_display_from_statistics"}
+
+
 def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_baseline) -> dict:
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -137,6 +193,10 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
         t = torch.tensor([ms_local, kern_local], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, kern_ms = float(t[0]), float(t[1])
+        e2e = None
+        if not args.no_e2e:
+            e2e = e2e_vocab_parallel(ids, logits, offs, rank, batch=4,
+                                     steps=max(3, min(K, args.e2e_steps)), warmup=2)
         total_bytes = B * L * V * 2
         shard_bytes = logits.numel() * 2
         peak, peak_kind = peaks()
@@ -165,7 +225,7 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
                          "kernel": "display_stats_rows_kernel<bf16, records> (per rank, max over ranks)",
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
                          "algorithmic_bytes_per_launch": alg},
-            "e2e": None,
+            "e2e": e2e,
             "gpu_launches": 3 * K,
             "clocks": clk.summary(),
         }
