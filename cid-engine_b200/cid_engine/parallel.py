@@ -60,6 +60,33 @@ def vocab_parallel_statistics(token_ids: Tensor, logits_shard: Tensor, *, total_
     return ops.display_combine_records(gathered, token_ids, offs)
 
 
+def vocab_parallel_refine(token_ids: Tensor, logits_shard: Tensor, *, total_vocab: int,
+                          mask_token_id: int, eos_token_id: int | None, reveal_fraction: float,
+                          revision_fraction: float, revision_margin: float, group=None,
+                          timing: tuple | None = None) -> Tensor:
+    """One vocabulary-parallel decode step: this rank's shard records, the
+    NCCL all-gather, the combine and the refinement, enqueued on the current
+    stream without host synchronisation.  Every rank returns the same refined
+    ids [B, L].  ``timing`` = (start, end) CUDA events recorded around the
+    record kernel.  (Splitting the step into chunks of sequences so that the
+    exchange of one chunk overlaps the streaming of the next measured slower
+    on B200: the step's exposed exchange is ~2% of it.)"""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    offs = shard_offsets(total_vocab, world)
+    assert logits_shard.shape[-1] == offs[rank + 1] - offs[rank], "shard width mismatch"
+    ops = torch.ops.cid_engine
+    stream = torch.cuda.current_stream(logits_shard.device)
+    if timing is not None:
+        timing[0].record(stream)
+    rec = ops.display_shard_records(token_ids, logits_shard, offs[rank], total_vocab)
+    if timing is not None:
+        timing[1].record(stream)
+    c, p, u = ops.display_combine_records(gather_records(rec, group), token_ids, offs)
+    return ops.refine_display_from_statistics(token_ids, c, p, u, mask_token_id, eos_token_id,
+                                              reveal_fraction, revision_fraction, revision_margin)
+
+
 # ---------------------------------------------------------------------------
 # multi-GPU bench arm (launched by bench.py under torchrun)
 # ---------------------------------------------------------------------------
@@ -156,18 +183,11 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
     try:
         B, L, V = 64, 4096, 152064
         ids, logits, offs = sharded_display_inputs(B, L, V, rank, world, 3, dev)
-        ops = torch.ops.cid_engine
-        stream = torch.cuda.current_stream()
 
         def step(ev):
-            if ev is not None:
-                ev[0].record(stream)
-            rec = ops.display_shard_records(ids, logits, offs[rank], V)
-            if ev is not None:
-                ev[1].record(stream)
-            gathered = gather_records(rec)
-            c, p, u = ops.display_combine_records(gathered, ids, offs)
-            ops.refine_display_from_statistics(ids, c, p, u, 0, 1, 0.25, 0.1, 0.05)
+            vocab_parallel_refine(ids, logits, total_vocab=V, mask_token_id=0, eos_token_id=1,
+                                  reveal_fraction=0.25, revision_fraction=0.1,
+                                  revision_margin=0.05, timing=ev)
 
         K, W = args.steps, args.warmup
         for _ in range(W):

@@ -90,3 +90,4 @@ def refine_step(
     out.snapshot = snap
     out.rollout = roll
     return out
+

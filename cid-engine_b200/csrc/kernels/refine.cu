@@ -26,8 +26,10 @@
 namespace cid {
 namespace {
 
-constexpr int kT = 256;
-constexpr int kWarps = kT / 32;
+// Block size: 256 threads, or 512 for long rows when the batch leaves most
+// SMs idle (one CTA per row is then latency-bound; twice the warps hide more
+// of it, and 512 threads still leave 128 registers per thread).
+constexpr int kMaxWarps = 512 / 32;
 constexpr int64_t kSmemLimit = 160 * 1024;
 
 __device__ __forceinline__ int64_t imin(int64_t a, int64_t b) { return a < b ? a : b; }
@@ -59,14 +61,15 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 }
 
 struct Scratch {
-  int64_t i64[kWarps];
-  uint32_t u32[kWarps];
-  int hist[256];       // radix-select histogram
-  uint32_t sel_digit;  // radix-select result of the current pass
-  int64_t sel_above;
+  int64_t i64[kMaxWarps];
+  int hist[2][2][256];       // radix-select histograms [buffer][class][digit]
+  uint32_t sel_digit[2][2];  // radix-select result per [buffer][class]
+  int64_t sel_above[2][2];
 };
 
+template <int kT>
 __device__ __forceinline__ int64_t block_sum(int64_t v, Scratch& s) {
+  constexpr int kWarps = kT / 32;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) v += __shfl_down_sync(0xffffffffu, v, d);
   if ((threadIdx.x & 31) == 0) s.i64[threadIdx.x >> 5] = v;
@@ -78,7 +81,9 @@ __device__ __forceinline__ int64_t block_sum(int64_t v, Scratch& s) {
   return r;
 }
 
+template <int kT>
 __device__ __forceinline__ int64_t block_min(int64_t v, Scratch& s) {
+  constexpr int kWarps = kT / 32;
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) v = min(v, __shfl_down_sync(0xffffffffu, v, d));
   if ((threadIdx.x & 31) == 0) s.i64[threadIdx.x >> 5] = v;
@@ -91,6 +96,7 @@ __device__ __forceinline__ int64_t block_min(int64_t v, Scratch& s) {
 }
 
 // Exclusive prefix sum over threads (in thread order) of v.
+template <int kT>
 __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, Scratch& s) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int64_t inc = v;
@@ -107,37 +113,60 @@ __device__ __forceinline__ int64_t block_exclusive_scan(int64_t v, Scratch& s) {
   return base + inc - v;
 }
 
-// Selects the k positions of [0, L) with elig(i) that come first in a stable
-// descending sort by key(i); calls take(i) for each (from any thread).
-// The k-th largest order key T is found by a 4-pass radix select (8 bits per
-// pass, most significant first, shared-memory histogram); every position with
-// a key above T is taken, and of those equal to T the first `need` in index
-// order.
-template <typename Elig, typename Key, typename Take>
-__device__ void select_top_k(int64_t L, int64_t k, Elig elig, Key key, Take take, Scratch& s) {
-  if (k <= 0) return;
+// Two independent stable top-k selections over [0, L) in one radix pass
+// sequence.  Position i belongs to class cls(i) (0, 1, or -1 for neither)
+// with key key(i, c); class c takes the k[c] positions that come first in a
+// stable descending sort of its members by key, i.e. std::stable_sort(>)
+// order.  The k[c]-th largest order key T[c] is found by a 4-pass radix
+// select (8 bits per pass, most significant first, shared-memory histograms,
+// double-buffered so a pass needs two barriers); every member with a key
+// above T[c] is taken, and of those equal to T[c] the first `need` in index
+// order.  take(i, c) is called once per selected position, from any thread.
+template <int kT, typename Cls, typename Key, typename Take>
+__device__ void select_top_k2(int64_t L, int64_t k0, int64_t k1, Cls cls, Key key, Take take,
+                              Scratch& s) {
+  if (k0 <= 0 && k1 <= 0) return;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t prefix = 0u;  // decided high bits of T
-  int64_t above = 0;     // eligible keys strictly above the prefix range
+  // per-class state in scalars (a runtime-indexed array would live on the stack)
+  uint32_t prefix0 = 0u, prefix1 = 0u;  // decided high bits of T[c]
+  int64_t above0 = 0, above1 = 0;       // members strictly above the prefix range
+  auto k_of = [&](int c) { return c == 0 ? k0 : k1; };
+  auto prefix_of = [&](int c) { return c == 0 ? prefix0 : prefix1; };
+  for (int i = threadIdx.x; i < 2 * 2 * 256; i += kT) (&s.hist[0][0][0])[i] = 0;
+  __syncthreads();
   for (int pass = 0; pass < 4; ++pass) {
+    const int buf = pass & 1;
     const int shift = 24 - 8 * pass;
     const uint32_t hi_mask = pass == 0 ? 0u : (0xffffffffu << (shift + 8));
-    for (int i = threadIdx.x; i < 256; i += kT) s.hist[i] = 0;
-    __syncthreads();
-    for (int64_t i = threadIdx.x; i < L; i += kT) {
-      if (!elig(i)) continue;
-      const uint32_t u = order_key(key(i));
-      if ((u & hi_mask) == prefix) atomicAdd(&s.hist[(u >> shift) & 255u], 1);
+    // warp-uniform trip count; lanes with the same (class, digit) add once
+    // (keys of similar magnitude share their top byte, so per-lane atomics
+    // would collide)
+    for (int64_t i0 = threadIdx.x - lane; i0 < L; i0 += kT) {
+      const int64_t i = i0 + lane;
+      int bin = -1;
+      if (i < L) {
+        const int c = cls(i);
+        if (c >= 0 && k_of(c) > 0) {
+          const uint32_t u = order_key(key(i, c));
+          if ((u & hi_mask) == prefix_of(c)) bin = c * 256 + static_cast<int>((u >> shift) & 255u);
+        }
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (bin >= 0 && lane == __ffs(peers) - 1)
+        atomicAdd(&s.hist[buf][bin >> 8][bin & 255], __popc(peers));
     }
+    // the other buffer was last read before the previous pass's barrier
+    for (int i = threadIdx.x; i < 2 * 256; i += kT) (&s.hist[buf ^ 1][0][0])[i] = 0;
     __syncthreads();
-    if (warp == 0) {
-      // lane l owns digits 255-8l .. 248-8l (descending); find the digit where
-      // the count from the top first reaches k
+    if (warp < 2 && k_of(warp) > 0) {
+      // warp c, lane l owns digits 255-8l .. 248-8l (descending) of class c;
+      // find the digit where the count from the top first reaches k[c]
+      const int c = warp;
       int h[8];
       int sum = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        h[j] = s.hist[255 - (lane * 8 + j)];
+        h[j] = s.hist[buf][c][255 - (lane * 8 + j)];
         sum += h[j];
       }
       int incl = sum;
@@ -146,14 +175,14 @@ __device__ void select_top_k(int64_t L, int64_t k, Elig elig, Key key, Take take
         const int o = __shfl_up_sync(0xffffffffu, incl, d);
         if (lane >= d) incl += o;
       }
-      int64_t running = above + (incl - sum);
-      const bool mine = running < k && running + sum >= k;
-      if (mine) {
+      const int64_t kc = k_of(c);
+      int64_t running = (c == 0 ? above0 : above1) + (incl - sum);
+      if (running < kc && running + sum >= kc) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          if (running + h[j] >= k) {
-            s.sel_digit = static_cast<uint32_t>(255 - (lane * 8 + j));
-            s.sel_above = running;
+          if (running + h[j] >= kc) {
+            s.sel_digit[buf][c] = static_cast<uint32_t>(255 - (lane * 8 + j));
+            s.sel_above[buf][c] = running;
             break;
           }
           running += h[j];
@@ -161,25 +190,45 @@ __device__ void select_top_k(int64_t L, int64_t k, Elig elig, Key key, Take take
       }
     }
     __syncthreads();
-    prefix |= s.sel_digit << shift;
-    above = s.sel_above;
-    __syncthreads();
+    if (k0 > 0) {
+      prefix0 |= s.sel_digit[buf][0] << shift;
+      above0 = s.sel_above[buf][0];
+    }
+    if (k1 > 0) {
+      prefix1 |= s.sel_digit[buf][1] << shift;
+      above1 = s.sel_above[buf][1];
+    }
   }
-  const uint32_t T = prefix;
-  const int64_t need = k - above;  // ties at T to take, by index
-  for (int64_t i = threadIdx.x; i < L; i += kT)
-    if (elig(i) && order_key(key(i)) > T) take(i);
-  // ties: contiguous ownership so that the scan follows index order
+  for (int64_t i = threadIdx.x; i < L; i += kT) {
+    const int c = cls(i);
+    if (c >= 0 && k_of(c) > 0 && order_key(key(i, c)) > prefix_of(c)) take(i, c);
+  }
+  // ties: contiguous ownership so that the scan follows index order; both
+  // classes' tie counts (each < 2^31) packed in one scan
+  const int64_t need0 = k0 - above0, need1 = k1 - above1;
   const int64_t per = (L + kT - 1) / kT;
   const int64_t lo = min(L, per * threadIdx.x), hi = min(L, lo + per);
+  auto tie = [&](int64_t i) -> int {
+    const int c = cls(i);
+    return (c >= 0 && k_of(c) > 0 && order_key(key(i, c)) == prefix_of(c)) ? c : -1;
+  };
   int64_t mine = 0;
-  for (int64_t i = lo; i < hi; ++i) mine += (elig(i) && order_key(key(i)) == T) ? 1 : 0;
-  int64_t rank = block_exclusive_scan(mine, s);
-  for (int64_t i = lo; i < hi && rank < need; ++i)
-    if (elig(i) && order_key(key(i)) == T) {
-      take(i);
-      ++rank;
+  for (int64_t i = lo; i < hi; ++i) {
+    const int c = tie(i);
+    if (c >= 0) mine += c == 0 ? 1 : (int64_t{1} << 32);
+  }
+  const int64_t before = block_exclusive_scan<kT>(mine, s);
+  int64_t rank0 = before & 0xffffffffLL, rank1 = before >> 32;
+  for (int64_t i = lo; i < hi && (rank0 < need0 || rank1 < need1); ++i) {
+    const int c = tie(i);
+    if (c == 0 && rank0 < need0) {
+      take(i, 0);
+      ++rank0;
+    } else if (c == 1 && rank1 < need1) {
+      take(i, 1);
+      ++rank1;
     }
+  }
 }
 
 struct Candidate {
@@ -205,10 +254,13 @@ __device__ __forceinline__ bool cand_better(const Candidate& a, const Candidate&
   return a.kind > b.kind;
 }
 
+template <int kT>
 __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
+  constexpr int kWarps = kT / 32;
+  constexpr int kChunk = 8;
   extern __shared__ __align__(16) unsigned char dyn[];
   __shared__ Scratch scratch;
-  __shared__ Candidate cand_smem[kWarps];
+  __shared__ Candidate cand_smem[kMaxWarps];
   __shared__ Candidate best_smem;
 
   const int64_t L = p.tokens;
@@ -232,14 +284,33 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
     int64_t* s_res = s_pred + L;
     float* s_conf = reinterpret_cast<float*>(s_res + L);
     float* s_gain = s_conf + L;
-    for (int64_t i = threadIdx.x; i < L; i += kT) {
-      const int64_t t = g_tok[i];
-      const float c = g_conf[i];
-      s_tok[i] = t;
-      s_res[i] = t;
-      s_pred[i] = g_pred[i];
-      s_conf[i] = c;
-      s_gain[i] = __fsub_rn(c, g_cur[i]);  // refine.cpp:277
+    // kStage iterations' loads in flight per thread before any store: one
+    // HBM latency per kStage * kT positions instead of per kT
+    constexpr int kStage = 4;
+    for (int64_t i0 = threadIdx.x; i0 < L; i0 += kT * kStage) {
+      int64_t t[kStage], pr[kStage];
+      float c[kStage], u[kStage];
+#pragma unroll
+      for (int j = 0; j < kStage; ++j) {
+        const int64_t i = i0 + static_cast<int64_t>(j) * kT;
+        if (i < L) {
+          t[j] = __ldg(g_tok + i);
+          pr[j] = __ldg(g_pred + i);
+          c[j] = __ldg(g_conf + i);
+          u[j] = __ldg(g_cur + i);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kStage; ++j) {
+        const int64_t i = i0 + static_cast<int64_t>(j) * kT;
+        if (i < L) {
+          s_tok[i] = t[j];
+          s_res[i] = t[j];
+          s_pred[i] = pr[j];
+          s_conf[i] = c[j];
+          s_gain[i] = __fsub_rn(c[j], u[j]);  // refine.cpp:277
+        }
+      }
     }
     tok = s_tok;
     pred = s_pred;
@@ -265,12 +336,16 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
     int64_t first = LLONG_MAX;
     for (int64_t i = threadIdx.x; i < L; i += kT)
       if (tok[i] == eos) { first = i; break; }
-    first = block_min(first, scratch);
+    first = block_min<kT>(first, scratch);
     eos_pos = first == LLONG_MAX ? -1 : first;
   }
 
   bool structural_done = false;
-  // 2. structural edit (refine.cpp:290-319, 93-218)
+  // 2. structural edit (refine.cpp:290-319, 93-218).  One start per thread;
+  // the offsets 1..budget (<= 32) of a start are scanned in chunks of kChunk
+  // with all loads of a chunk issued before any compare (the first-element
+  // tests of the insertion and the deletion share the chunk), so a start
+  // costs budget/kChunk shared-memory round trips instead of one per offset.
   if (eos_pos > 0 && p.revision != 0.0) {
     int64_t budget = static_cast<int64_t>(ceil(static_cast<double>(eos_pos) * p.revision));
     budget = imax(1, imin(32, budget));
@@ -279,46 +354,70 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
     best.valid = 0;
     for (int64_t s = threadIdx.x; s < eos_pos; s += kT) {
       const float gs = gain(s);
-      if (pred[s] == tok[s] || static_cast<double>(gs) < p.margin) continue;
-      // insertion: nearest q in (s, s+budget] with pred[q, q+klen) == tok[s, s+klen)
+      const int64_t ts = tok[s], ps = pred[s];
+      if (ps == ts || static_cast<double>(gs) < p.margin) continue;
+      // insertion: nearest q in (s, qlast] with pred[q, q+klen) == tok[s, s+klen);
+      // deletion: nearest r in (s, rlast] with tok[r, r+dlen) == pred[s, s+dlen)
       const int64_t klen = imin(3, alen - s);
       const int64_t qlast = imin(s + budget, L - klen);
-      for (int64_t q = s + 1; q <= qlast; ++q) {
-        bool eq = true;
-        for (int64_t k = 0; k < klen && eq; ++k) eq = pred[q + k] == tok[s + k];
-        if (!eq) continue;
-        bool ok = true;
-        for (int64_t k = s; k < q && ok; ++k) ok = pred[k] != mask && pred[k] != eos;
+      const int64_t dlen = imin(3, L - s);
+      const int64_t rlast = dlen < 2 ? s : imin(imin(eos_pos - 1, s + budget), alen - dlen);
+      int64_t q_hit = -1, r_hit = -1;
+      for (int64_t o0 = 1; o0 <= budget && (q_hit < 0 || r_hit < 0); o0 += kChunk) {
+        int64_t pv[kChunk], tv[kChunk];
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) {
+          const int64_t o = s + o0 + j;
+          pv[j] = (q_hit < 0 && o <= qlast) ? pred[o] : ~ts;  // ~x never equals x
+          tv[j] = (r_hit < 0 && o <= rlast) ? tok[o] : ~ps;
+        }
+        unsigned qm = 0, rm = 0;
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) {
+          qm |= static_cast<unsigned>(pv[j] == ts) << j;
+          rm |= static_cast<unsigned>(tv[j] == ps) << j;
+        }
+        while (qm && q_hit < 0) {  // full k-gram check of the first-element hits
+          const int64_t q = s + o0 + (__ffs(qm) - 1);
+          bool eq = true;
+          for (int64_t k = 1; k < klen && eq; ++k) eq = pred[q + k] == tok[s + k];
+          if (eq) q_hit = q;
+          qm &= qm - 1;
+        }
+        while (rm && r_hit < 0) {
+          const int64_t r = s + o0 + (__ffs(rm) - 1);
+          bool eq = true;
+          for (int64_t k = 1; k < dlen && eq; ++k) eq = tok[r + k] == pred[s + k];
+          if (eq) r_hit = r;
+          rm &= rm - 1;
+        }
+      }
+      if (q_hit >= 0) {
+        bool ok = true;  // pred[s, q) must hold neither mask nor EOS
+        for (int64_t k = s; k < q_hit && ok; ++k) ok = pred[k] != mask && pred[k] != eos;
         if (ok) {
           int64_t anchor = 0;
-          while (q + anchor < L && s + anchor < alen && pred[q + anchor] == tok[s + anchor]) ++anchor;
-          const int64_t growth = q - s;
+          while (q_hit + anchor < L && s + anchor < alen && pred[q_hit + anchor] == tok[s + anchor])
+            ++anchor;
+          const int64_t growth = q_hit - s;
           if (anchor >= 2 && static_cast<double>(gs) >= p.margin && eos_pos + 1 + growth <= L) {
-            Candidate c{anchor, gs, -growth, s, 1, 0, growth, 1};
+            const Candidate c{anchor, gs, -growth, s, 1, 0, growth, 1};
             if (cand_better(c, best)) best = c;
           }
         }
-        break;  // only the nearest match is considered
       }
-      // deletion: nearest r in (s, min(eos-1, s+budget)] with tok[r, r+dlen) == pred[s, s+dlen)
-      const int64_t dlen = imin(3, L - s);
-      if (dlen < 2) continue;
-      const int64_t rlast = imin(imin(eos_pos - 1, s + budget), alen - dlen);
-      for (int64_t r = s + 1; r <= rlast; ++r) {
-        bool eq = true;
-        for (int64_t k = 0; k < dlen && eq; ++k) eq = tok[r + k] == pred[s + k];
-        if (!eq) continue;
+      if (r_hit >= 0) {
         int64_t anchor = 0;
-        while (s + anchor < L && r + anchor < alen && pred[s + anchor] == tok[r + anchor]) ++anchor;
-        const int64_t del = r - s;
+        while (s + anchor < L && r_hit + anchor < alen && pred[s + anchor] == tok[r_hit + anchor])
+          ++anchor;
+        const int64_t del = r_hit - s;
         if (anchor >= 2 && static_cast<double>(gs) >= p.margin && eos_pos + 1 - del <= L) {
-          Candidate c{anchor, gs, -del, s, 0, del, 0, 1};
+          const Candidate c{anchor, gs, -del, s, 0, del, 0, 1};
           if (cand_better(c, best)) best = c;
         }
-        break;
       }
     }
-    // block arg-best
+    // block arg-best: warp shuffles, then warp 0 over the warps' candidates
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (int d = 1; d < 32; d <<= 1) {
       Candidate o;
@@ -334,11 +433,23 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
     }
     if (lane == 0) cand_smem[warp] = best;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      Candidate b = cand_smem[0];
-      for (int w = 1; w < kWarps; ++w)
-        if (cand_better(cand_smem[w], b)) b = cand_smem[w];
-      best_smem = b;
+    if (warp == 0) {
+      Candidate b{};
+      b.valid = 0;
+      if (lane < kWarps) b = cand_smem[lane];
+      for (int d = 1; d < kWarps; d <<= 1) {
+        Candidate o;
+        o.anchor = __shfl_xor_sync(0xffffffffu, b.anchor, d);
+        o.gain = __shfl_xor_sync(0xffffffffu, b.gain, d);
+        o.neg_growth = __shfl_xor_sync(0xffffffffu, b.neg_growth, d);
+        o.start = __shfl_xor_sync(0xffffffffu, b.start, d);
+        o.kind = __shfl_xor_sync(0xffffffffu, b.kind, d);
+        o.del = __shfl_xor_sync(0xffffffffu, b.del, d);
+        o.ins = __shfl_xor_sync(0xffffffffu, b.ins, d);
+        o.valid = __shfl_xor_sync(0xffffffffu, b.valid, d);
+        if (cand_better(o, b)) b = o;
+      }
+      if (lane == 0) best_smem = b;
     }
     __syncthreads();
     const Candidate b = best_smem;
@@ -361,46 +472,47 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
 
   if (!structural_done) {
     const int64_t stop = eos_pos >= 0 ? eos_pos : L;  // refine.cpp:321
-    // 3a. reveal (refine.cpp:322-342)
-    int64_t nm = 0;
-    for (int64_t i = threadIdx.x; i < stop; i += kT) nm += tok[i] == mask ? 1 : 0;
-    nm = block_sum(nm, scratch);
-    if (nm > 0 && p.reveal != 0.0) {
-      const int64_t k = static_cast<int64_t>(ceil(static_cast<double>(nm) * p.reveal));
-      select_top_k(
-          stop, k, [&](int64_t i) { return tok[i] == mask; }, [&](int64_t i) { return conf[i]; },
-          [&](int64_t i) { res[i] = pred[i]; }, scratch);
+    // 3a/3b. reveal (refine.cpp:322-342) and revision (refine.cpp:344-379):
+    // disjoint member sets (masked / visible positions) and independent
+    // counts, so both selections share one radix pass sequence.  The
+    // revision margin is compared in float32.
+    const float margin_f = static_cast<float>(p.margin);
+    const bool revise = p.revision != 0.0;
+    auto cls = [&](int64_t i) -> int {
+      const int64_t t = tok[i];
+      if (t == mask) return 0;
+      return (revise && pred[i] != t && gain(i) >= margin_f) ? 1 : -1;
+    };
+    int64_t counts = 0;  // masked | candidates << 32 (each < 2^31)
+    for (int64_t i = threadIdx.x; i < stop; i += kT) {
+      const int c = cls(i);
+      counts += c == 0 ? 1 : c == 1 ? (int64_t{1} << 32) : 0;
     }
-    if (p.revision != 0.0) {
-      // 3b. revision (refine.cpp:344-379); the margin is compared in float32
-      const float margin_f = static_cast<float>(p.margin);
-      const int64_t visible = stop - nm;
-      auto is_cand = [&](int64_t i) {
-        return tok[i] != mask && pred[i] != tok[i] && gain(i) >= margin_f;
-      };
-      int64_t nc = 0;
-      for (int64_t i = threadIdx.x; i < stop; i += kT) nc += is_cand(i) ? 1 : 0;
-      nc = block_sum(nc, scratch);
-      if (nc > 0) {
-        int64_t k = static_cast<int64_t>(ceil(static_cast<double>(visible) * p.revision));
-        k = min(k, nc);
-        select_top_k(stop, k, is_cand, gain, [&](int64_t i) { res[i] = pred[i]; }, scratch);
-      }
-      // 3c. EOS expansion (refine.cpp:381-406), double margin
-      if (eos_pos >= 0 && eos_pos + 1 < L && pred[eos_pos] != eos &&
-          static_cast<double>(gain(eos_pos)) >= p.margin) {
-        const int64_t basec = imax(1, eos_pos + 1);
-        const int64_t budget =
-            imax(1, static_cast<int64_t>(ceil(static_cast<double>(basec) * p.reveal)));
-        int64_t new_eos = imin(L - 1, eos_pos + budget);
-        int64_t first = LLONG_MAX;
-        for (int64_t t = eos_pos + 1 + threadIdx.x; t <= new_eos; t += kT)
-          if (pred[t] == eos) { first = t; break; }
-        first = block_min(first, scratch);
-        if (first != LLONG_MAX) new_eos = first;
-        for (int64_t t = eos_pos + threadIdx.x; t < new_eos; t += kT) res[t] = pred[t];
-        if (threadIdx.x == 0) res[new_eos] = eos;
-      }
+    counts = block_sum<kT>(counts, scratch);
+    const int64_t nm = counts & 0xffffffffLL, nc = counts >> 32;
+    int64_t k0 = 0, k1 = 0;
+    if (nm > 0 && p.reveal != 0.0)
+      k0 = static_cast<int64_t>(ceil(static_cast<double>(nm) * p.reveal));
+    if (revise && nc > 0)
+      k1 = imin(static_cast<int64_t>(ceil(static_cast<double>(stop - nm) * p.revision)), nc);
+    select_top_k2<kT>(
+        stop, k0, k1, cls, [&](int64_t i, int c) { return c == 0 ? conf[i] : gain(i); },
+        [&](int64_t i, int) { res[i] = pred[i]; }, scratch);
+    // 3c. EOS expansion (refine.cpp:381-406), double margin; writes only
+    // positions >= eos_pos, disjoint from the selections above
+    if (revise && eos_pos >= 0 && eos_pos + 1 < L && pred[eos_pos] != eos &&
+        static_cast<double>(gain(eos_pos)) >= p.margin) {
+      const int64_t basec = imax(1, eos_pos + 1);
+      const int64_t ebudget =
+          imax(1, static_cast<int64_t>(ceil(static_cast<double>(basec) * p.reveal)));
+      int64_t new_eos = imin(L - 1, eos_pos + ebudget);
+      int64_t first = LLONG_MAX;
+      for (int64_t t = eos_pos + 1 + threadIdx.x; t <= new_eos; t += kT)
+        if (pred[t] == eos) { first = t; break; }
+      first = block_min<kT>(first, scratch);
+      if (first != LLONG_MAX) new_eos = first;
+      for (int64_t t = eos_pos + threadIdx.x; t < new_eos; t += kT) res[t] = pred[t];
+      if (threadIdx.x == 0) res[new_eos] = eos;
     }
     __syncthreads();
   }
@@ -410,7 +522,7 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
   if (p.has_eos) {
     for (int64_t i = threadIdx.x; i < L; i += kT)
       if (res[i] == eos) { cut = i; break; }
-    cut = block_min(cut, scratch);
+    cut = block_min<kT>(cut, scratch);
   }
   if (p.use_smem) {
     for (int64_t i = threadIdx.x; i < L; i += kT) g_out[i] = i > cut ? mask : res[i];
@@ -455,11 +567,20 @@ extern "C" int cid_refine_display(const int64_t* token_ids, const float* confide
   const int64_t smem = tokens * (3 * 8 + 2 * 4);
   p.use_smem = smem <= kSmemLimit;
   const size_t dyn = p.use_smem ? static_cast<size_t>(smem) : 0;
-  if (dyn > 48 * 1024) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
+  // 512 threads per row when rows are long and too few to fill the SMs
+  const bool wide = tokens >= 1024 && batch < 2LL * sm_count();
+  if (dyn > 48 * 1024) {  // per device, so set on every launch (cheap)
+    const cudaError_t e = wide ? cudaFuncSetAttribute(refine_kernel<512>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      static_cast<int>(kSmemLimit))
+                               : cudaFuncSetAttribute(refine_kernel<256>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                      static_cast<int>(kSmemLimit));
     if (e != cudaSuccess) return record_cuda_error(e);
   }
-  refine_kernel<<<static_cast<unsigned>(batch), kT, dyn, as_stream(stream)>>>(p);
+  if (wide)
+    refine_kernel<512><<<static_cast<unsigned>(batch), 512, dyn, as_stream(stream)>>>(p);
+  else
+    refine_kernel<256><<<static_cast<unsigned>(batch), 256, dyn, as_stream(stream)>>>(p);
   return launch_result();
 }

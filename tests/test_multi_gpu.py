@@ -58,6 +58,21 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
             assert torch.equal(pred, e_pred)
             torch.testing.assert_close(conf, e_conf, rtol=2e-5, atol=2e-6, equal_nan=True)
             torch.testing.assert_close(cur, e_cur, rtol=2e-5, atol=2e-6, equal_nan=True)
+        # the fused vocabulary-parallel step == statistics then refinement
+        V = 50021
+        g = torch.Generator(device=dev).manual_seed(7)
+        logits = (torch.randn(5, 64, V, generator=g, device=dev) * 3).to(torch.bfloat16)
+        ids = torch.randint(2, V, (5, 64), generator=g, device=dev)
+        ids[torch.rand((5, 64), generator=g, device=dev) < 0.6] = 0
+        ids[:, 40] = 1
+        offs = parallel.shard_offsets(V, world)
+        shard = logits[..., offs[rank]:offs[rank + 1]].contiguous()
+        kw = dict(mask_token_id=0, eos_token_id=1, reveal_fraction=0.25, revision_fraction=0.1,
+                  revision_margin=0.05)
+        c, p, u = parallel.vocab_parallel_statistics(ids, shard, total_vocab=V)
+        expected = cid_engine.refine_display_from_statistics(ids, c, p, u, **kw)
+        got = parallel.vocab_parallel_refine(ids, shard, total_vocab=V, **kw)
+        assert torch.equal(got, expected)
         torch.cuda.synchronize()
         Path(result_dir, f"ok{rank}").write_text("ok")
     finally:
