@@ -32,6 +32,7 @@ STATUS_TOKEN_ID_OUT_OF_RANGE = 0x1
 STATUS_SEMANTIC_INDEX_OUT_OF_RANGE = 0x2
 STATUS_REPETITION_ID_OUT_OF_RANGE = 0x4
 STATUS_ASSIGNMENT_INVALID = 0x8
+STATUS_LM_HEAD_TIMEOUT = 0x10
 
 
 def device_status(device: int | torch.device = 0, *, reset: bool = False) -> int:
@@ -259,6 +260,22 @@ def display_combine_records(
     return torch.ops.cid_engine.display_combine_records(records, token_ids, list(shard_offsets))
 
 
+
+def lm_head_display_statistics(
+    token_ids: Tensor,
+    hidden: Tensor,
+    weight: Tensor,
+    *,
+    round_bf16: bool = True,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """``display_token_statistics(token_ids, hidden @ weight.T)`` without
+    writing the ``[*, vocab]`` logits: bf16 ``hidden [*token_ids.shape, H]``
+    and ``weight [vocab, H]`` (H % 8 == 0) multiplied on the tcgen05 tensor
+    cores with f32 accumulation, each logit rounded to bf16 first when
+    ``round_bf16`` (the statistics of a bf16 LM head's stored output)."""
+    return torch.ops.cid_engine.lm_head_display_statistics(token_ids, hidden, weight, round_bf16)
+
+
 from cid_engine.step import refine_step  # noqa: E402
 from cid_engine.loop import DisplayRefineLoop  # noqa: E402
 
@@ -275,6 +292,7 @@ __all__ = [
     "display_token_statistics",
     "display_token_statistics_with_repetition",
     "live_slot_occupancy",
+    "lm_head_display_statistics",
     "materialize_cell_snapshot",
     "masked_diffusion_corrupt_from_random",
     "prefix_allocation_mask",

@@ -91,6 +91,13 @@ at::Tensor display_shard_records(Backend backend, const at::Tensor& token_ids,
 Tensor3 display_combine_records(Backend backend, const at::Tensor& records,
                                 const at::Tensor& token_ids, at::IntArrayRef shard_offsets);
 
+// LM head fused with the display statistics (additive operator of this
+// build): display_token_statistics(token_ids, hidden @ weight^T) without
+// writing the logits.
+Tensor3 lm_head_display_statistics(Backend backend, const at::Tensor& token_ids,
+                                   const at::Tensor& hidden, const at::Tensor& weight,
+                                   bool round_bf16);
+
 // Device status word (CID_STATUS_* bits) of `device`; read() synchronises.
 std::int64_t read_device_status(std::int64_t device, bool reset);
 

@@ -1,0 +1,593 @@
+// LM head fused with the display statistics: the statistics of
+// logits = hidden @ weight^T (bf16 operands, f32 accumulation, optionally
+// rounded to bf16 as a bf16 LM head would store them) without writing the
+// [rows, vocab] logits to memory.
+//
+// The reference has no LM head (its statistics operator takes materialised
+// logits); this is the producer side of the display path on B200:
+//
+// * one persistent CTA per SM, warp-specialised: warp 0 issues TMA loads of
+//   128 x 64 hidden tiles and 256 x 64 weight tiles (128-byte swizzle) into a
+//   4-stage shared-memory ring; warp 1 issues tcgen05.mma (M=128, N=256,
+//   K=16, kind::f16 with bf16 A and B) into one of two 256-column TMEM
+//   accumulators; warps 2-5 read the finished accumulator with tcgen05.ld
+//   (thread = row, TMEM lane = row) and fold its 256 columns into the row's
+//   online (max, sum of exp, first argmax, current-token logit) state while
+//   the other accumulator fills;
+// * a work unit is (block of 128 rows, group of G consecutive 256-column
+//   vocabulary tiles); each unit ends in one 16-byte shard record per row
+//   (the same record as the vocabulary-parallel statistics), and the record
+//   combine kernel merges the groups of a row into its statistics;
+// * units are ordered in groups of 16 row blocks, so the CTAs running at a
+//   time share their hidden blocks and weight tiles in L2;
+// * every mbarrier wait is bounded (2 s of %globaltimer); a wait that runs
+//   out sets CID_STATUS_LM_HEAD_TIMEOUT and a shared abort flag, every role
+//   leaves its loop, in-flight TMA copies and MMAs are waited for (bounded)
+//   and the TMEM is freed before the CTA exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <climits>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace cid {
+namespace {
+
+constexpr int kBM = 128;  // rows per tile (UMMA M)
+constexpr int kBN = 256;  // vocabulary columns per tile (UMMA N)
+constexpr int kBK = 64;   // hidden elements per stage: one 128-byte swizzle row
+constexpr int kUmmaK = 16;
+constexpr int kStages = 4;
+constexpr int kAccBufs = 2;
+constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 512: all of TMEM
+constexpr int kRowGroup = 16;                   // row blocks per raster group
+constexpr int kMaxGroups = 64;                  // record combine limit
+constexpr int kThreads = 192;                   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr uint32_t kStageA = kBM * kBK * 2;     // 16 KiB
+constexpr uint32_t kStageB = kBN * kBK * 2;     // 32 KiB
+constexpr uint32_t kStageBytes = kStageA + kStageB;
+constexpr size_t kSmemBytes = kStages * size_t{kStageBytes} + 1024 /* align */ + 256 /* barriers */;
+constexpr unsigned long long kWaitNs = 2000000000ull;  // bounded waits: 2 s
+constexpr unsigned long long kDrainNs = 200000000ull;  // drain after an abort: 0.2 s
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kGap = 5.0f;  // offset re-set threshold (natural units), as the stats kernels
+
+// Instruction descriptor of tcgen05.mma kind::f16: D f32 (bits 4-5 = 1),
+// A and B bf16 (bits 7-9 = 1, 10-12 = 1), both K-major, N >> 3 at bit 17,
+// M >> 4 at bit 24.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
+                            (uint32_t(kBM >> 4) << 24);
+
+struct LmParams {
+  int64_t rows;         // hidden rows
+  int64_t vocab;        // weight rows (columns of the logits)
+  int64_t vocab_offset; // global column of weight row 0
+  int64_t ktiles;       // ceil(hidden / kBK)
+  int64_t tiles;        // ceil(vocab / kBN)
+  int64_t group_tiles;  // vocabulary tiles per work unit
+  int64_t groups;       // ceil(tiles / group_tiles)
+  int64_t row_blocks;   // ceil(rows / kBM)
+  int64_t units;        // row_blocks * groups
+  const int64_t* ids;
+  cid_shard_record_t* records;  // [groups][rows]
+  uint32_t* status;
+  int round_bf16;
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the phase of `bar` with the given parity; false when `abort` is
+// raised or `limit_ns` passes first.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          unsigned long long limit_ns) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (global_ns() - t0 > limit_ns) return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle
+// layout TMA writes: rows of 128 bytes, 8-row atoms 1024 bytes apart
+// (stride byte offset), version 1, layout type 2 (128-byte swizzle).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3fffu) | (uint64_t{1} << 16) |
+         (uint64_t{1024 >> 4} << 32) | (uint64_t{1} << 46) | (uint64_t{2} << 61);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once all tcgen05.mma issued so far by this thread are done.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive f32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// ---------------------------------------------------------------------------
+// Work units
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void unit_coords(const LmParams& p, int64_t u, int64_t& rb,
+                                            int64_t& vg) {
+  const int64_t per_group = int64_t{kRowGroup} * p.groups;
+  const int64_t gi = u / per_group;
+  const int64_t first = gi * kRowGroup;
+  const int64_t rows_in = p.row_blocks - first < kRowGroup ? p.row_blocks - first : kRowGroup;
+  const int64_t local = u - gi * per_group;
+  rb = first + local % rows_in;
+  vg = local / rows_in;
+}
+
+__device__ __forceinline__ void raise_abort(volatile int* abort, uint32_t* status) {
+  *abort = 1;
+  if (status) atomicOr(status, CID_STATUS_LM_HEAD_TIMEOUT);
+}
+
+// Per-row online state over the columns of one work unit.
+struct RowState {
+  float m, om, off, s;
+  int64_t where;      // weight column of the first maximum, -1 before any
+  int64_t first_nan;  // weight column of the first NaN, -1 if none
+  float cur;          // logit at the row's token id (when in the unit)
+};
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// Folds 32 consecutive columns (weight columns c0..c0+31) into the state.
+__device__ __forceinline__ void fold32(RowState& st, float (&x)[32], int64_t c0, int64_t vocab,
+                                       int64_t local_id, int round_bf16) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float v = round_bf16 ? bf16_round(x[j]) : x[j];
+    if (c0 + j >= vocab) v = -INFINITY;  // padding columns of the last tile
+    x[j] = v;
+  }
+  const int64_t rel = local_id - c0;
+  if (rel >= 0 && rel < 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j == rel) st.cur = x[j];
+  }
+  float cm = x[0];
+#pragma unroll
+  for (int j = 1; j < 32; ++j) cm = fmaxf(cm, x[j]);  // NaN ignored
+  if (cm > st.m) {
+    int jj = 0;
+#pragma unroll
+    for (int j = 31; j >= 0; --j)
+      if (x[j] == cm) jj = j;
+    st.m = cm;
+    st.where = c0 + jj;
+    if (st.m > st.om + kGap) {
+      const float noff = st.m * kLog2e;
+      st.s = st.om == -INFINITY ? (st.s != st.s ? st.s : 0.0f) : st.s * exp2f(st.off - noff);
+      st.om = st.m;
+      st.off = noff;
+    }
+  }
+  float a = 0.0f, b = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    a += ex2(fmaf(x[j], kLog2e, -st.off));
+    b += ex2(fmaf(x[j + 1], kLog2e, -st.off));
+  }
+  const float cs = a + b;
+  if (cs != cs && st.first_nan < 0) {  // a NaN column (or inf - inf) in the chunk
+    int jn = -1;
+#pragma unroll
+    for (int j = 31; j >= 0; --j)
+      if (x[j] != x[j]) jn = j;
+    if (jn >= 0) st.first_nan = c0 + jn;
+  }
+  st.s += cs;
+}
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads, 1)
+    lm_head_stats_kernel(const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_b, LmParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-byte aligned
+  unsigned char* stage_a = smem;
+  unsigned char* stage_b = smem + kStages * kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + kAccBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kAccBufs);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kAccBufs; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0, issue_par = 0;  // per-stage bits: ever issued, parity of last issue
+      bool ok = true;
+      for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        int64_t rb, vg;
+        unit_coords(p, u, rb, vg);
+        const int64_t t0 = vg * p.group_tiles;
+        const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
+        for (int64_t t = t0; ok && t < t1; ++t) {
+          for (int64_t kt = 0; kt < p.ktiles; ++kt) {
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort, kWaitNs)) {
+              if (!*abort) raise_abort(abort, p.status);
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&full[s], kStageBytes);
+            tma_load_2d(stage_a + s * kStageA, &map_a, static_cast<int32_t>(kt * kBK),
+                        static_cast<int32_t>(rb * kBM), &full[s]);
+            tma_load_2d(stage_b + s * kStageB, &map_b, static_cast<int32_t>(kt * kBK),
+                        static_cast<int32_t>(t * kBN), &full[s]);
+            issued |= 1u << s;
+            issue_par = (issue_par & ~(1u << s)) | (ph << s);
+            if (++s == kStages) {
+              s = 0;
+              ph ^= 1u;
+            }
+          }
+        }
+      }
+      // copies in flight land before the CTA exits (immediate unless aborted)
+      for (int i = 0; i < kStages; ++i)
+        if (issued & (1u << i)) mbar_wait(&full[i], (issue_par >> i) & 1u, nullptr, kDrainNs);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int s = 0, buf = 0;
+      uint32_t ph = 0, aph = 0;
+      uint64_t* last_bar = nullptr;  // barrier of the last commit and its phase parity
+      uint32_t last_par = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        int64_t rb, vg;
+        unit_coords(p, u, rb, vg);
+        const int64_t t0 = vg * p.group_tiles;
+        const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
+        for (int64_t t = t0; ok && t < t1; ++t) {
+          if (!mbar_wait(&acc_empty[buf], aph ^ 1u, abort, kWaitNs)) {
+            if (!*abort) raise_abort(abort, p.status);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kBN);
+          for (int64_t kt = 0; kt < p.ktiles; ++kt) {
+            if (!mbar_wait(&full[s], ph, abort, kWaitNs)) {
+              if (!*abort) raise_abort(abort, p.status);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(stage_a + s * kStageA);
+            const uint32_t b0 = smem_u32(stage_b + s * kStageB);
+#pragma unroll
+            for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+              // K advance inside the 128-byte swizzle atom: +32 bytes per 16 elements
+              umma_bf16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32),
+                        (kt | kk) != 0 ? 1u : 0u);
+            }
+            umma_commit(&empty[s]);  // frees the stage once these MMAs are done
+            last_bar = &empty[s];
+            last_par = ph;
+            if (++s == kStages) {
+              s = 0;
+              ph ^= 1u;
+            }
+          }
+          if (!ok) break;
+          umma_commit(&acc_full[buf]);  // the accumulator is complete
+          last_bar = &acc_full[buf];
+          last_par = aph;
+          if (++buf == kAccBufs) {
+            buf = 0;
+            aph ^= 1u;
+          }
+        }
+      }
+      // MMAs in flight finish before the TMEM is freed (immediate unless aborted)
+      if (last_bar != nullptr) mbar_wait(last_bar, last_par, nullptr, kDrainNs);
+    }
+  } else {
+    // ---------------- epilogue: thread = row, TMEM lane = row ----------------
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31 for this warp
+    const int row_in_block = quarter * 32 + lane;
+    int buf = 0;
+    uint32_t aph = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+      int64_t rb, vg;
+      unit_coords(p, u, rb, vg);
+      const int64_t t0 = vg * p.group_tiles;
+      const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
+      const int64_t row = rb * kBM + row_in_block;
+      const bool valid = row < p.rows;
+      const int64_t c_lo = t0 * kBN;                                        // weight columns
+      const int64_t c_hi = t1 * kBN < p.vocab ? t1 * kBN : p.vocab;          // of this unit
+      const int64_t id = valid ? p.ids[row] - p.vocab_offset : -1;
+      const int64_t local_id = (id >= c_lo && id < c_hi) ? id : INT64_MIN / 2;
+      RowState st{-INFINITY, -INFINITY, 0.0f, 0.0f, -1, -1, 0.0f};
+      for (int64_t t = t0; t < t1; ++t) {
+        bool got = mbar_wait(&acc_full[buf], aph, abort, kWaitNs);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          if (lane == 0 && !*abort) raise_abort(abort, p.status);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr =
+            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * kBN);
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float x[32];
+          tmem_ld32(taddr + static_cast<uint32_t>(c * 32), x);
+          fold32(st, x, t * kBN + c * 32, p.vocab, local_id, p.round_bf16);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        if (++buf == kAccBufs) {
+          buf = 0;
+          aph ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (valid) {
+        cid_shard_record_t rec;
+        rec.max_logit = st.m;
+        const bool special = !(st.m > -INFINITY && st.m < INFINITY) || st.s != st.s;
+        if (special) {
+          const int64_t local = st.first_nan >= 0 ? st.first_nan : (st.where >= 0 ? st.where : c_lo);
+          rec.sum_exp = st.m == -INFINITY ? 0.0f : __int_as_float(0x7fffffff);
+          rec.index = static_cast<int32_t>(p.vocab_offset + local) |
+                      (st.first_nan >= 0 ? static_cast<int32_t>(0x80000000u) : 0);
+        } else {
+          const float top = ex2(fmaf(st.m, kLog2e, -st.off));
+          rec.sum_exp = __fdiv_rn(st.s, top);
+          rec.index = static_cast<int32_t>(p.vocab_offset + st.where);
+        }
+        rec.current = local_id >= 0 ? st.cur : 0.0f;
+        p.records[vg * p.rows + row] = rec;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [outer, inner] matrix, box
+// [box_outer, 64] with the 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_outer) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct Plan {
+  int64_t tiles, group_tiles, groups, row_blocks, units;
+};
+
+Plan plan(int64_t rows, int64_t vocab) {
+  Plan pl;
+  pl.tiles = (vocab + kBN - 1) / kBN;
+  pl.group_tiles = (pl.tiles + kMaxGroups - 1) / kMaxGroups;
+  if (pl.group_tiles < 4) pl.group_tiles = 4;
+  pl.groups = (pl.tiles + pl.group_tiles - 1) / pl.group_tiles;
+  pl.row_blocks = (rows + kBM - 1) / kBM;
+  pl.units = pl.row_blocks * pl.groups;
+  return pl;
+}
+
+}  // namespace
+}  // namespace cid
+
+using namespace cid;
+
+extern "C" size_t cid_lm_head_workspace_bytes(int64_t rows, int64_t vocab) {
+  if (rows <= 0 || vocab <= 0) return 0;
+  const Plan pl = plan(rows, vocab);
+  return static_cast<size_t>(pl.groups) * static_cast<size_t>(rows) * sizeof(cid_shard_record_t);
+}
+
+extern "C" int cid_lm_head_display_statistics(const void* hidden, int64_t rows, int64_t hidden_dim,
+                                              const void* weight, int64_t vocab,
+                                              const int64_t* token_ids, int round_bf16,
+                                              float* confidence, int64_t* predicted,
+                                              float* current_confidence, void* workspace,
+                                              size_t workspace_bytes, uint32_t* status,
+                                              void* stream) {
+  if (rows < 0 || hidden_dim <= 0 || vocab <= 0 || vocab > INT32_MAX) return CID_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return CID_OK;
+  if (!hidden || !weight || !token_ids || !confidence || !predicted || !current_confidence ||
+      !workspace)
+    return CID_ERR_INVALID_ARGUMENT;
+  // TMA: row strides and base addresses 16-byte aligned
+  if (hidden_dim % 8 != 0 || (reinterpret_cast<uintptr_t>(hidden) & 15u) ||
+      (reinterpret_cast<uintptr_t>(weight) & 15u))
+    return CID_ERR_INVALID_ARGUMENT;
+  if (rows > INT32_MAX - kBM) return CID_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < cid_lm_head_workspace_bytes(rows, vocab)) return CID_ERR_SCRATCH_LIMIT;
+  const Plan pl = plan(rows, vocab);
+  CUtensorMap map_a, map_b;
+  if (!make_map(&map_a, hidden, hidden_dim, rows, kBM) ||
+      !make_map(&map_b, weight, hidden_dim, vocab, kBN))
+    return CID_ERR_INVALID_ARGUMENT;
+  LmParams p = {};
+  p.rows = rows;
+  p.vocab = vocab;
+  p.vocab_offset = 0;
+  p.ktiles = (hidden_dim + kBK - 1) / kBK;
+  p.tiles = pl.tiles;
+  p.group_tiles = pl.group_tiles;
+  p.groups = pl.groups;
+  p.row_blocks = pl.row_blocks;
+  p.units = pl.units;
+  p.ids = token_ids;
+  p.records = static_cast<cid_shard_record_t*>(workspace);
+  p.status = status;
+  p.round_bf16 = round_bf16 ? 1 : 0;
+  cudaError_t e = cudaFuncSetAttribute(lm_head_stats_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kSmemBytes));
+  if (e != cudaSuccess) return record_cuda_error(e);
+  const int64_t grid = pl.units < sm_count() ? pl.units : sm_count();
+  lm_head_stats_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, as_stream(stream)>>>(
+      map_a, map_b, p);
+  int rc = launch_result();
+  if (rc != CID_OK) return rc;
+  // merge the groups of every row (ascending column ranges) into its statistics
+  int64_t offsets[kMaxGroups + 1];
+  for (int64_t g = 0; g < pl.groups; ++g) offsets[g] = g * pl.group_tiles * kBN;
+  offsets[pl.groups] = vocab;
+  return cid_display_combine_records(p.records, static_cast<int>(pl.groups), offsets, token_ids,
+                                     rows, confidence, predicted, current_confidence, status,
+                                     stream);
+}

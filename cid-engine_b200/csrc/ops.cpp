@@ -261,6 +261,45 @@ Tensor3 display_combine_records(Backend backend, const at::Tensor& records,
   return {confidence, predicted, current};
 }
 
+Tensor3 lm_head_display_statistics(Backend backend, const at::Tensor& token_ids,
+                                   const at::Tensor& hidden, const at::Tensor& weight,
+                                   bool round_bf16) {
+  TORCH_CHECK(token_ids.scalar_type() == at::kLong, "token_ids must use torch.int64");
+  TORCH_CHECK(hidden.dim() >= 1 && hidden.dim() - 1 == token_ids.dim() &&
+                  hidden.sizes().slice(0, hidden.dim() - 1) == token_ids.sizes(),
+              "hidden must have shape [*token_ids.shape, hidden_dim]");
+  TORCH_CHECK(weight.dim() == 2 && weight.size(1) == hidden.size(-1),
+              "weight must have shape [vocab, hidden_dim]");
+  TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 && weight.scalar_type() == at::kBFloat16,
+              "hidden and weight must use torch.bfloat16");
+  TORCH_CHECK(weight.size(0) > 0, "weight vocabulary dimension must be non-empty");
+  TORCH_CHECK(hidden.size(-1) % 8 == 0, "hidden_dim must be a multiple of 8");
+  same_device("lm_head_display_statistics", {&token_ids, &hidden, &weight});
+  const auto f32 = token_ids.options().dtype(at::kFloat);
+  auto confidence = at::empty(token_ids.sizes(), f32);
+  auto predicted = at::empty(token_ids.sizes(), token_ids.options().dtype(at::kLong));
+  auto current = at::empty(token_ids.sizes(), f32);
+  if (backend == Backend::kMeta) return {confidence, predicted, current};
+  if (backend == Backend::kCpu) detail::no_cpu_backend("lm_head_display_statistics");
+  if (token_ids.numel() == 0) return {confidence, predicted, current};
+  const c10::cuda::CUDAGuard guard(hidden.device());
+  auto h = hidden.contiguous();
+  auto w = weight.contiguous();
+  auto ids = token_ids.contiguous();
+  const auto rows = ids.numel();
+  const size_t ws_bytes = cid_lm_head_workspace_bytes(rows, w.size(0));
+  auto workspace = at::empty({static_cast<std::int64_t>(ws_bytes)},
+                             hidden.options().dtype(at::kByte));
+  check_result(cid_lm_head_display_statistics(
+                   h.data_ptr(), rows, h.size(-1), w.data_ptr(), w.size(0),
+                   ids.data_ptr<std::int64_t>(), round_bf16 ? 1 : 0,
+                   confidence.data_ptr<float>(), predicted.data_ptr<std::int64_t>(),
+                   current.data_ptr<float>(), workspace.data_ptr(), ws_bytes,
+                   detail::status_word(h.device()), stream_of(h)),
+               "lm_head_display_statistics");
+  return {confidence, predicted, current};
+}
+
 // ---------------------------------------------------------------------------
 // live_slot_occupancy — csrc/ops.cpp:12-39
 // ---------------------------------------------------------------------------

@@ -83,6 +83,12 @@ Tensor3 combine_records_impl(const at::Tensor& rec, const at::Tensor& ids, at::I
 }
 
 template <Backend B>
+Tensor3 lm_head_impl(const at::Tensor& ids, const at::Tensor& hidden, const at::Tensor& weight,
+                     bool round_bf16) {
+  return lm_head_display_statistics(B, ids, hidden, weight, round_bf16);
+}
+
+template <Backend B>
 void register_all(torch::Library& m) {
   m.impl("live_slot_occupancy", TORCH_FN(live_impl<B>));
   m.impl("prefix_allocation_mask", TORCH_FN(prefix_impl<B>));
@@ -97,6 +103,7 @@ void register_all(torch::Library& m) {
   m.impl("materialize_cell_snapshot", TORCH_FN(snapshot_impl<B>));
   m.impl("display_shard_records", TORCH_FN(shard_records_impl<B>));
   m.impl("display_combine_records", TORCH_FN(combine_records_impl<B>));
+  m.impl("lm_head_display_statistics", TORCH_FN(lm_head_impl<B>));
 }
 
 }  // namespace
@@ -152,6 +159,10 @@ TORCH_LIBRARY(cid_engine, m) {
   m.def(
       "display_combine_records(Tensor records, Tensor token_ids, int[] shard_offsets) "
       "-> (Tensor, Tensor, Tensor)");
+  // additive: LM head fused with the display statistics
+  m.def(
+      "lm_head_display_statistics(Tensor token_ids, Tensor hidden, Tensor weight, "
+      "bool round_bf16=True) -> (Tensor, Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(cid_engine, CUDA, m) {

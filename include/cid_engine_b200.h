@@ -64,6 +64,8 @@ typedef enum cid_result {
 #define CID_STATUS_SEMANTIC_INDEX_OUT_OF_RANGE 0x2u
 #define CID_STATUS_REPETITION_ID_OUT_OF_RANGE 0x4u
 #define CID_STATUS_ASSIGNMENT_INVALID 0x8u
+/* A bounded wait of the LM-head kernel ran out (its outputs are invalid). */
+#define CID_STATUS_LM_HEAD_TIMEOUT 0x10u
 
 CID_API int cid_abi_version(void);
 CID_API const char* cid_result_string(int result);
@@ -297,6 +299,29 @@ CID_API int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype,
                         double replacement_fraction, int64_t* corrupted,
                         int64_t* labels, uint8_t* masked, uint8_t* replaced,
                         void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* LM head fused with the display statistics (no reference counterpart:   */
+/* the reference's statistics take materialised logits, csrc/ops.cpp:446). */
+/* ---------------------------------------------------------------------- */
+
+/* Workspace bytes cid_lm_head_display_statistics needs for rows x vocab. */
+CID_API size_t cid_lm_head_workspace_bytes(int64_t rows, int64_t vocab);
+
+/* display_token_statistics(token_ids, logits) of logits = hidden @ weight^T
+ * without writing the logits: hidden rows x hidden_dim bf16 and weight
+ * vocab x hidden_dim bf16, both row-major with hidden_dim % 8 == 0 and
+ * 16-byte aligned bases; f32 accumulation on the tcgen05 tensor cores,
+ * each logit rounded to bf16 first when round_bf16 != 0 (the statistics of
+ * a bf16 LM head's stored output).  token_ids rows int64; outputs as
+ * cid_display_token_statistics.  workspace: device memory of at least
+ * cid_lm_head_workspace_bytes(rows, vocab) bytes.  Waits inside the kernel
+ * are bounded; one that runs out sets CID_STATUS_LM_HEAD_TIMEOUT. */
+CID_API int cid_lm_head_display_statistics(const void* hidden, int64_t rows, int64_t hidden_dim,
+                        const void* weight, int64_t vocab, const int64_t* token_ids,
+                        int round_bf16, float* confidence, int64_t* predicted,
+                        float* current_confidence, void* workspace,
+                        size_t workspace_bytes, uint32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,138 @@
+"""The LM head fused with the display statistics
+(``cid_engine.lm_head_display_statistics``) against the statistics of the
+materialised logits.
+
+References: logits = hidden.float() @ weight.float().T from torch in f32
+(no TF32), then the (separately oracle-checked) statistics kernel on those
+logits — as f32 for ``round_bf16=False``, rounded to bf16 for
+``round_bf16=True``.  The tensor-core accumulation order differs from the
+reference GEMM's, so: confidences within rtol 1e-4 (f32) / 1e-2 (bf16: a
+logit can round to the neighbouring bf16 value); the predicted column must
+hold the row maximum of the reference logits within the accumulation error
+(f32: 1e-3 absolute; bf16: one bf16 ulp of the maximum).  Exact structure
+is checked exactly: duplicated weight rows give bit-identical columns, and
+the lower column must win.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _engine():
+    import cid_engine  # noqa: F401
+
+    assert torch.cuda.is_available()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.cuda.empty_cache()
+
+
+def _inputs(rows, vocab, hidden, seed, scale=0.5):
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    h = (torch.randn(rows, hidden, generator=g, device=dev) * scale).to(torch.bfloat16)
+    w = (torch.randn(vocab, hidden, generator=g, device=dev) * scale).to(torch.bfloat16)
+    ids = torch.randint(0, vocab, (rows,), generator=g, device=dev)
+    return ids, h, w
+
+
+def _check(ids, h, w, round_bf16):
+    import cid_engine
+
+    conf, pred, cur = cid_engine.lm_head_display_statistics(ids, h, w, round_bf16=round_bf16)
+    logits = h.float() @ w.float().T
+    if round_bf16:
+        logits = logits.to(torch.bfloat16)
+    e_conf, e_pred, e_cur = cid_engine.display_token_statistics(ids.view(1, -1),
+                                                                logits.unsqueeze(0))
+    e_conf, e_pred, e_cur = e_conf[0], e_pred[0], e_cur[0]
+    rtol = 1e-2 if round_bf16 else 1e-4
+    torch.testing.assert_close(conf, e_conf, rtol=rtol, atol=1e-7)
+    torch.testing.assert_close(cur, e_cur, rtol=rtol, atol=1e-7)
+    lf = logits.float()
+    rowmax = lf.max(dim=1).values
+    got = lf.gather(1, pred.view(-1, 1)).view(-1)
+    tol = (rowmax.abs() * 2.0**-7 + 1e-6) if round_bf16 else torch.full_like(rowmax, 1e-3)
+    assert bool(((rowmax - got) <= tol).all()), "predicted column does not hold the row maximum"
+    agree = (pred == e_pred).float().mean().item()
+    assert agree > 0.95, f"argmax agreement {agree}"
+    return conf, pred, cur
+
+
+@pytest.mark.parametrize("round_bf16", [False, True])
+@pytest.mark.parametrize("rows,vocab,hidden", [
+    (5, 300, 64),        # one row block, two tiles, the last partial
+    (300, 1000, 128),    # partial row block, 4 tiles
+    (256, 5000, 72),     # hidden not a multiple of 64 (zero-filled K tail)
+    (1100, 32000, 256),  # many work units and vocabulary groups
+    (130, 70001, 64),    # groups of more than 4 tiles, odd vocabulary
+])
+def test_lm_head_matches_materialised_logits(rows, vocab, hidden, round_bf16) -> None:
+    import cid_engine
+
+    cid_engine.device_status(0, reset=True)
+    ids, h, w = _inputs(rows, vocab, hidden, seed=rows + vocab)
+    _check(ids, h, w, round_bf16)
+    assert cid_engine.device_status(0) == 0
+
+
+def test_lm_head_exact_ties_take_the_lower_column() -> None:
+    import cid_engine
+
+    ids, h, w = _inputs(200, 3000, 128, seed=4)
+    # rows of the weight duplicated across tiles and groups: identical columns
+    w[2900] = w[17]
+    w[1500] = w[17]
+    w[600] = w[599]
+    conf, pred, cur = cid_engine.lm_head_display_statistics(ids, h, w, round_bf16=False)
+    logits = h.float() @ w.float().T
+    top = logits.argmax(dim=1)
+    for dup, base in ((2900, 17), (1500, 17), (600, 599)):
+        rows_dup = (pred == dup).nonzero().flatten()
+        assert rows_dup.numel() == 0, f"column {dup} chosen over its duplicate {base}"
+    # rows whose maximum sits on a duplicated column report the lower one
+    hits = (top == 17) | (top == 1500) | (top == 2900)
+    assert bool((pred[hits] == 17).all())
+
+
+def test_lm_head_peaks_and_batch_shape() -> None:
+    import cid_engine
+
+    B, L, V, H = 3, 50, 4096, 64
+    ids, h, w = _inputs(B * L, V, H, seed=9)
+    # a planted dominant logit per row: hidden aligned with one weight row
+    cols = torch.randint(0, V, (B * L,), device=h.device)
+    h = (w[cols].float() * 4).to(torch.bfloat16)
+    conf, pred, cur = cid_engine.lm_head_display_statistics(ids.view(B, L), h.view(B, L, H), w)
+    assert conf.shape == (B, L) and pred.dtype == torch.int64
+    logits = (h.float() @ w.float().T).to(torch.bfloat16).float()
+    assert bool((logits.gather(1, pred.view(-1, 1)).view(-1) >= logits.max(1).values).all())
+
+
+def test_lm_head_out_of_range_id_sets_status() -> None:
+    import cid_engine
+
+    ids, h, w = _inputs(64, 512, 64, seed=2)
+    ids[3] = 512
+    ids[5] = -1
+    cid_engine.device_status(0, reset=True)
+    conf, pred, cur = cid_engine.lm_head_display_statistics(ids, h, w)
+    assert bool(cur[3].isnan()) and bool(cur[5].isnan())
+    assert cid_engine.device_status(0) & cid_engine.STATUS_TOKEN_ID_OUT_OF_RANGE
+
+
+def test_lm_head_validation() -> None:
+    import cid_engine
+
+    ids, h, w = _inputs(8, 256, 64, seed=1)
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        cid_engine.lm_head_display_statistics(ids, h.float(), w)
+    with pytest.raises(RuntimeError, match="multiple of 8"):
+        cid_engine.lm_head_display_statistics(ids, h[:, :60].contiguous(), w[:, :60].contiguous())
+    with pytest.raises(RuntimeError, match="shape"):
+        cid_engine.lm_head_display_statistics(ids[:4], h, w)
