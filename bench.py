@@ -308,6 +308,7 @@ def bench_single(args) -> dict:
 
     loop = None if args.no_loop else bench_refine_loop(dev)
     small = None if args.no_loop else bench_small_configs(dev)
+    lm_head = None if args.no_loop else bench_lm_head(dev)
     cpu = None if args.no_cpu_baseline else run_cpu_baseline(seconds=args.cpu_seconds)
     line = {
         "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
@@ -336,6 +337,7 @@ def bench_single(args) -> dict:
         "cpu_baseline": cpu,
         "refine_loop": loop,
         "small_configs": small,
+        "lm_head": lm_head,
     }
     return line
 
@@ -491,6 +493,66 @@ def bench_small_configs(dev) -> dict:
     }
 
 
+def bench_lm_head(dev) -> dict:
+    """LM head fused with the display statistics on the config-2 rows:
+    hidden bf16 [32*1024, 4096] x weight bf16 [128256, 4096] (the display
+    logits of config 2 produced by a 4096-wide LM head), statistics of the
+    bf16-rounded logits; against cuBLAS writing the bf16 logits and the
+    statistics kernel reading them back, timed in the same run."""
+    import torch
+
+    import cid_engine
+
+    R, H, V = CFG2["B"] * CFG2["L"], 4096, CFG2["V"]
+    g = torch.Generator(device=dev).manual_seed(5)
+    h = (torch.randn(R, H, generator=g, device=dev) * 0.05).to(torch.bfloat16)
+    w = (torch.randn(V, H, generator=g, device=dev) * 0.05).to(torch.bfloat16)
+    ids = torch.randint(0, V, (R,), generator=g, device=dev)
+    flop = 2.0 * R * V * H
+
+    def timed(fn, reps=4):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    def unfused():
+        logits = h @ w.T
+        return cid_engine.display_token_statistics(ids.view(1, -1), logits.view(1, R, V))
+
+    ms_fused = timed(lambda: cid_engine.lm_head_display_statistics(ids, h, w))
+    ms_gemm = timed(lambda: h @ w.T)
+    ms_unfused = timed(unfused)
+    c, p, u = cid_engine.lm_head_display_statistics(ids, h, w)
+    e_c, e_p, e_u = unfused()
+    agree = float((p == e_p[0]).float().mean())
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak_burst = float(peaks.get("bf16_tflops", 1590.0))
+    peak_sust = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    tflops = flop / (ms_fused * 1e-3) / 1e12
+    del h, w
+    torch.cuda.empty_cache()
+    return {"workload": f"LM head + display statistics, hidden bf16 [{R},{H}] x weight bf16 [{V},{H}]",
+            "api": "cid_engine.lm_head_display_statistics",
+            "fused_ms": round(ms_fused, 3), "fused_tflops": round(tflops, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "unit": "TFLOP/s",
+                         "peak_burst": peak_burst, "frac_burst": round(tflops / peak_burst, 4),
+                         "peak_sustained": peak_sust, "frac_sustained": round(tflops / peak_sust, 4),
+                         "peak_kind": "measured" if peaks else "fallback"},
+            "cublas_gemm_ms": round(ms_gemm, 3),
+            "cublas_gemm_tflops": round(flop / (ms_gemm * 1e-3) / 1e12, 1),
+            "unfused_ms": round(ms_unfused, 3),
+            "logits_bytes_not_written": R * V * 2,
+            "argmax_agreement_with_unfused": agree,
+            "launches_per_call": 2}
+
+
 def bench_reference(args, world: int = 1) -> dict:
     """Reference CPU backend on the host cores, on the B200 arm's workload,
     metric and unit: config 2 at N=1, the vocabulary-parallel config 4 under
@@ -537,6 +599,16 @@ def profile_case(name: str) -> None:
 
     import cid_engine
 
+    if name == "lm_head":  # fused LM head + statistics: rows 8192, vocab 128256, hidden 4096
+        g = torch.Generator(device="cuda").manual_seed(1)
+        h = (torch.randn(8192, 4096, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+        w = (torch.randn(128256, 4096, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+        ids = torch.randint(0, 128256, (8192,), generator=g, device="cuda")
+        for _ in range(3):
+            c, p, u = cid_engine.lm_head_display_statistics(ids, h, w)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "mean_conf": float(c.mean())}))
+        return
     shape = {"cta": (1, 4096, 128256), "rows": (1, 10240, 128256)}[name]
     g = torch.Generator(device="cuda").manual_seed(1)
     lg = torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) * 2
@@ -560,7 +632,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-min-reps", type=int, default=3)
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
-    ap.add_argument("--profile-case", choices=("cta", "rows"), default=None,
+    ap.add_argument("--profile-case", choices=("cta", "rows", "lm_head"), default=None,
                     help="run a small statistics case for ncu and exit")
     ap.add_argument("--sample-b", type=int, default=1)
     ap.add_argument("--sample-l", type=int, default=1024)
