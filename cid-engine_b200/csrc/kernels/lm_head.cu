@@ -171,9 +171,9 @@ __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 
-// 32 consecutive f32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// Issues the load of 32 consecutive f32 columns of this thread's TMEM lane
+// without waiting; the registers are valid after tmem_wait32 on them.
+__device__ __forceinline__ void tmem_issue32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
       "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -183,9 +183,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// Waits for this thread's outstanding TMEM loads; the registers are in-out
+// operands so that no use of them is scheduled before the wait.
+__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// Packed f32 pair arithmetic (sm_100): {a0,a1} * {b,b} + {c,c} and {s0,s1} += {a0,a1}.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %4};\n"
+      " mov.b64 rc, {%5, %5};\n fma.rn.f32x2 ra, ra, rb, rc;\n mov.b64 {%0, %1}, ra;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n .reg .b64 ra, rb;\n mov.b64 ra, {%0, %1};\n mov.b64 rb, {%2, %3};\n"
+      " add.rn.f32x2 ra, ra, rb;\n mov.b64 {%0, %1}, ra;\n}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
 }
 
 // ---------------------------------------------------------------------------
@@ -216,18 +241,30 @@ struct RowState {
   float cur;          // logit at the row's token id (when in the unit)
 };
 
-__device__ __forceinline__ float bf16_round(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
-}
-
-// Folds 32 consecutive columns (weight columns c0..c0+31) into the state.
-__device__ __forceinline__ void fold32(RowState& st, float (&x)[32], int64_t c0, int64_t vocab,
-                                       int64_t local_id, int round_bf16) {
+// Folds 32 consecutive columns (weight columns c0..c0+31, raw f32 bits from
+// TMEM) into the state: logits rounded to bf16 in pairs (one cvt per two),
+// exponent arguments and sums in packed f32 pairs.
+__device__ __forceinline__ void fold32(RowState& st, const uint32_t (&r)[32], int64_t c0,
+                                       int64_t vocab, int64_t local_id, int round_bf16) {
+  float x[32];
+  if (round_bf16) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    float v = round_bf16 ? bf16_round(x[j]) : x[j];
-    if (c0 + j >= vocab) v = -INFINITY;  // padding columns of the last tile
-    x[j] = v;
+    for (int j = 0; j < 32; j += 2) {
+      uint32_t pk;  // upper half: column j + 1, lower half: column j
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+          : "=r"(pk)
+          : "f"(__uint_as_float(r[j + 1])), "f"(__uint_as_float(r[j])));
+      x[j] = __uint_as_float(pk << 16);
+      x[j + 1] = __uint_as_float(pk & 0xffff0000u);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r[j]);
+  }
+  if (c0 + 32 > vocab) {  // padding columns of the last tile
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (c0 + j >= vocab) x[j] = -INFINITY;
   }
   const int64_t rel = local_id - c0;
   if (rel >= 0 && rel < 32) {
@@ -252,13 +289,17 @@ __device__ __forceinline__ void fold32(RowState& st, float (&x)[32], int64_t c0,
       st.off = noff;
     }
   }
-  float a = 0.0f, b = 0.0f;
+  float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+  const float moff = -st.off;
 #pragma unroll
-  for (int j = 0; j < 32; j += 2) {
-    a += ex2(fmaf(x[j], kLog2e, -st.off));
-    b += ex2(fmaf(x[j + 1], kLog2e, -st.off));
+  for (int j = 0; j < 32; j += 4) {
+    float e0, e1, e2, e3;
+    fma2(e0, e1, x[j], x[j + 1], kLog2e, moff);
+    fma2(e2, e3, x[j + 2], x[j + 3], kLog2e, moff);
+    add2(a0, a1, ex2(e0), ex2(e1));
+    add2(b0, b1, ex2(e2), ex2(e3));
   }
-  const float cs = a + b;
+  const float cs = (a0 + a1) + (b0 + b1);
   if (cs != cs && st.first_nan < 0) {  // a NaN column (or inf - inf) in the chunk
     int jn = -1;
 #pragma unroll
@@ -439,11 +480,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t taddr =
             tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * kBN);
-#pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          float x[32];
-          tmem_ld32(taddr + static_cast<uint32_t>(c * 32), x);
-          fold32(st, x, t * kBN + c * 32, p.vocab, local_id, p.round_bf16);
+        // each chunk's TMEM load is in flight while the previous chunk folds
+        uint32_t ra[32], rb[32];
+        tmem_issue32(taddr, ra);
+        tmem_wait32(ra);
+#pragma unroll
+        for (int c = 0; c < kBN / 32; c += 2) {
+          tmem_issue32(taddr + static_cast<uint32_t>((c + 1) * 32), rb);
+          fold32(st, ra, t * kBN + c * 32, p.vocab, local_id, p.round_bf16);
+          tmem_wait32(rb);
+          if (c + 2 < kBN / 32) tmem_issue32(taddr + static_cast<uint32_t>((c + 2) * 32), ra);
+          fold32(st, rb, t * kBN + (c + 1) * 32, p.vocab, local_id, p.round_bf16);
+          if (c + 2 < kBN / 32) tmem_wait32(ra);
         }
         tc_fence_before();
         __syncwarp();
