@@ -276,6 +276,25 @@ def lm_head_display_statistics(
     return torch.ops.cid_engine.lm_head_display_statistics(token_ids, hidden, weight, round_bf16)
 
 
+
+def lm_head_shard_records(
+    token_ids: Tensor,
+    hidden: Tensor,
+    weight_shard: Tensor,
+    *,
+    vocab_offset: int,
+    total_vocab: int,
+    round_bf16: bool = True,
+) -> Tensor:
+    """The per-rank half of a vocabulary-parallel LM head: the 16-byte shard
+    record of every row (as ``display_shard_records``) over
+    ``hidden @ weight_shard.T``, whose columns are the global vocabulary ids
+    ``[vocab_offset, vocab_offset + weight_shard.shape[0])``, without writing
+    those logits."""
+    return torch.ops.cid_engine.lm_head_shard_records(token_ids, hidden, weight_shard,
+                                                      vocab_offset, total_vocab, round_bf16)
+
+
 from cid_engine.step import refine_step  # noqa: E402
 from cid_engine.loop import DisplayRefineLoop  # noqa: E402
 
@@ -293,6 +312,7 @@ __all__ = [
     "display_token_statistics_with_repetition",
     "live_slot_occupancy",
     "lm_head_display_statistics",
+    "lm_head_shard_records",
     "materialize_cell_snapshot",
     "masked_diffusion_corrupt_from_random",
     "prefix_allocation_mask",

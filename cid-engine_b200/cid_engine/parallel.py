@@ -60,6 +60,28 @@ def vocab_parallel_statistics(token_ids: Tensor, logits_shard: Tensor, *, total_
     return ops.display_combine_records(gathered, token_ids, offs)
 
 
+def vocab_parallel_lm_head_statistics(token_ids: Tensor, hidden: Tensor, weight_shard: Tensor, *,
+                                      total_vocab: int, round_bf16: bool = True,
+                                      group=None) -> tuple[Tensor, Tensor, Tensor]:
+    """``display_token_statistics`` of the logits of a vocabulary-parallel LM
+    head: this rank holds ``weight_shard`` = the rows
+    ``shard_offsets(total_vocab, world)[rank:rank+2]`` of the output
+    embedding and the full ``hidden`` states.  Each rank reduces its logits
+    to 16-byte row records inside the GEMM (the logits never reach memory),
+    the records are all-gathered over NCCL and combined; every rank returns
+    the unsharded statistics."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    offs = shard_offsets(total_vocab, world)
+    assert weight_shard.shape[0] == offs[rank + 1] - offs[rank], "shard height mismatch"
+    ops = torch.ops.cid_engine
+    records = ops.lm_head_shard_records(token_ids, hidden, weight_shard, offs[rank], total_vocab,
+                                        round_bf16)
+    ids = token_ids.reshape(1, -1)
+    c, p, u = ops.display_combine_records(gather_records(records, group), ids, offs)
+    return c.view(token_ids.shape), p.view(token_ids.shape), u.view(token_ids.shape)
+
+
 def vocab_parallel_refine(token_ids: Tensor, logits_shard: Tensor, *, total_vocab: int,
                           mask_token_id: int, eos_token_id: int | None, reveal_fraction: float,
                           revision_fraction: float, revision_margin: float, group=None,

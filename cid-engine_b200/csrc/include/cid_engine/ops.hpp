@@ -97,6 +97,12 @@ Tensor3 display_combine_records(Backend backend, const at::Tensor& records,
 Tensor3 lm_head_display_statistics(Backend backend, const at::Tensor& token_ids,
                                    const at::Tensor& hidden, const at::Tensor& weight,
                                    bool round_bf16);
+// The per-rank half of a vocabulary-parallel LM head: shard records [rows, 4]
+// (int32) of hidden @ weight_shard^T for global columns starting at vocab_offset.
+at::Tensor lm_head_shard_records(Backend backend, const at::Tensor& token_ids,
+                                 const at::Tensor& hidden, const at::Tensor& weight_shard,
+                                 std::int64_t vocab_offset, std::int64_t total_vocab,
+                                 bool round_bf16);
 
 // Device status word (CID_STATUS_* bits) of `device`; read() synchronises.
 std::int64_t read_device_status(std::int64_t device, bool reset);

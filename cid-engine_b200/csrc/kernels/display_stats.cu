@@ -741,6 +741,56 @@ __global__ void combine_records_kernel(CombineParams p) {
   p.current[row] = cur;
 }
 
+// Merges the records of W ascending column ranges of each row into the one
+// record of their union (the record of the concatenated shard): lowest range
+// wins max ties, a NaN flag wins over everything (first range holding one),
+// sums re-expressed relative to the merged maximum, the current logit taken
+// from the range that holds the row's token id (0 when none does).
+__global__ void merge_records_kernel(CombineParams p, cid_shard_record_t* out) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= p.rows) return;
+  const int64_t id = p.ids[row];
+  float cur = 0.0f;
+  for (int r = 0; r < p.world; ++r)
+    if (id >= p.offsets[r] && id < p.offsets[r + 1])
+      cur = p.records[static_cast<int64_t>(r) * p.rows + row].current;
+  cid_shard_record_t m;
+  m.current = cur;
+  for (int r = 0; r < p.world; ++r) {
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+    if (rec.index < 0) {
+      m.max_logit = rec.max_logit;
+      m.sum_exp = __int_as_float(0x7fffffff);
+      m.index = rec.index;
+      out[row] = m;
+      return;
+    }
+  }
+  float M = -INFINITY;
+  int32_t idx = p.records[row].index;
+  for (int r = 0; r < p.world; ++r) {
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+    if (rec.max_logit > M) {
+      M = rec.max_logit;
+      idx = rec.index;
+    }
+  }
+  m.max_logit = M;
+  m.index = idx;
+  if (!isfinite(M)) {
+    m.sum_exp = M == -INFINITY ? 0.0f : __int_as_float(0x7fffffff);
+  } else {
+    float S = 0.0f;
+    for (int r = 0; r < p.world; ++r) {
+      const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+      if (rec.max_logit == -INFINITY) continue;
+      S += rec.sum_exp * ex2((rec.max_logit - M) * kLog2e);
+    }
+    m.sum_exp = S;
+  }
+  out[row] = m;
+}
+
 // ---------------------------------------------------------------------------
 // Launch helpers
 // ---------------------------------------------------------------------------
@@ -930,6 +980,30 @@ extern "C" int cid_display_shard_records(cid_dtype_t dtype, const void* logits,
   prm.vocab_offset = vocab_offset;
   prm.total_vocab = total_vocab;
   return dispatch_stats<false, Mode::kRecord>(dtype, prm, as_stream(stream));
+}
+
+extern "C" int cid_display_merge_records(const cid_shard_record_t* records, int world,
+                                         const int64_t* shard_offsets_host,
+                                         const int64_t* token_ids, int64_t rows,
+                                         cid_shard_record_t* merged, void* stream) {
+  if (world < 1 || world > kMaxWorld || rows < 0 || !shard_offsets_host)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return CID_OK;
+  if (!records || !token_ids || !merged) return CID_ERR_INVALID_ARGUMENT;
+  CombineParams prm = {};
+  prm.records = records;
+  prm.world = world;
+  for (int r = 0; r <= world; ++r) {
+    prm.offsets[r] = shard_offsets_host[r];
+    if (r > 0 && prm.offsets[r] < prm.offsets[r - 1]) return CID_ERR_INVALID_ARGUMENT;
+  }
+  prm.ids = token_ids;
+  prm.rows = rows;
+  const int threads = 256;
+  const int64_t blocks = (rows + threads - 1) / threads;
+  merge_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(prm,
+                                                                                         merged);
+  return launch_result();
 }
 
 extern "C" int cid_display_combine_records(const cid_shard_record_t* records, int world,

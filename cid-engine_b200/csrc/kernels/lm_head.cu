@@ -585,18 +585,15 @@ extern "C" size_t cid_lm_head_workspace_bytes(int64_t rows, int64_t vocab) {
   return static_cast<size_t>(pl.groups) * static_cast<size_t>(rows) * sizeof(cid_shard_record_t);
 }
 
-extern "C" int cid_lm_head_display_statistics(const void* hidden, int64_t rows, int64_t hidden_dim,
-                                              const void* weight, int64_t vocab,
-                                              const int64_t* token_ids, int round_bf16,
-                                              float* confidence, int64_t* predicted,
-                                              float* current_confidence, void* workspace,
-                                              size_t workspace_bytes, uint32_t* status,
-                                              void* stream) {
-  if (rows < 0 || hidden_dim <= 0 || vocab <= 0 || vocab > INT32_MAX) return CID_ERR_INVALID_ARGUMENT;
-  if (rows == 0) return CID_OK;
-  if (!hidden || !weight || !token_ids || !confidence || !predicted || !current_confidence ||
-      !workspace)
-    return CID_ERR_INVALID_ARGUMENT;
+namespace {
+
+// Validates, launches the fused kernel (records of every row and vocabulary
+// group into `workspace`) and fills the groups' global column offsets.
+int launch_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const void* weight,
+                   int64_t vocab, int64_t vocab_offset, const int64_t* token_ids, int round_bf16,
+                   void* workspace, size_t workspace_bytes, uint32_t* status, void* stream,
+                   int64_t (&offsets)[kMaxGroups + 1], int& groups) {
+  if (!hidden || !weight || !token_ids || !workspace) return CID_ERR_INVALID_ARGUMENT;
   // TMA: row strides and base addresses 16-byte aligned
   if (hidden_dim % 8 != 0 || (reinterpret_cast<uintptr_t>(hidden) & 15u) ||
       (reinterpret_cast<uintptr_t>(weight) & 15u))
@@ -611,7 +608,7 @@ extern "C" int cid_lm_head_display_statistics(const void* hidden, int64_t rows, 
   LmParams p = {};
   p.rows = rows;
   p.vocab = vocab;
-  p.vocab_offset = 0;
+  p.vocab_offset = vocab_offset;
   p.ktiles = (hidden_dim + kBK - 1) / kBK;
   p.tiles = pl.tiles;
   p.group_tiles = pl.group_tiles;
@@ -629,13 +626,55 @@ extern "C" int cid_lm_head_display_statistics(const void* hidden, int64_t rows, 
   const int64_t grid = pl.units < sm_count() ? pl.units : sm_count();
   lm_head_stats_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, as_stream(stream)>>>(
       map_a, map_b, p);
-  int rc = launch_result();
+  const int rc = launch_result();
+  if (rc != CID_OK) return rc;
+  groups = static_cast<int>(pl.groups);
+  for (int64_t g = 0; g < pl.groups; ++g) offsets[g] = vocab_offset + g * pl.group_tiles * kBN;
+  offsets[pl.groups] = vocab_offset + vocab;
+  return CID_OK;
+}
+
+}  // namespace
+
+extern "C" int cid_lm_head_display_statistics(const void* hidden, int64_t rows, int64_t hidden_dim,
+                                              const void* weight, int64_t vocab,
+                                              const int64_t* token_ids, int round_bf16,
+                                              float* confidence, int64_t* predicted,
+                                              float* current_confidence, void* workspace,
+                                              size_t workspace_bytes, uint32_t* status,
+                                              void* stream) {
+  if (rows < 0 || hidden_dim <= 0 || vocab <= 0 || vocab > INT32_MAX) return CID_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return CID_OK;
+  if (!confidence || !predicted || !current_confidence) return CID_ERR_INVALID_ARGUMENT;
+  int64_t offsets[kMaxGroups + 1];
+  int groups = 0;
+  int rc = launch_lm_head(hidden, rows, hidden_dim, weight, vocab, 0, token_ids, round_bf16,
+                          workspace, workspace_bytes, status, stream, offsets, groups);
   if (rc != CID_OK) return rc;
   // merge the groups of every row (ascending column ranges) into its statistics
+  return cid_display_combine_records(static_cast<const cid_shard_record_t*>(workspace), groups,
+                                     offsets, token_ids, rows, confidence, predicted,
+                                     current_confidence, status, stream);
+}
+
+extern "C" int cid_lm_head_shard_records(const void* hidden, int64_t rows, int64_t hidden_dim,
+                                         const void* weight_shard, int64_t vocab_shard,
+                                         int64_t vocab_offset, int64_t total_vocab,
+                                         const int64_t* token_ids, int round_bf16,
+                                         cid_shard_record_t* records, void* workspace,
+                                         size_t workspace_bytes, uint32_t* status, void* stream) {
+  if (rows < 0 || hidden_dim <= 0 || vocab_shard <= 0 || vocab_offset < 0 ||
+      total_vocab > INT32_MAX || vocab_offset + vocab_shard > total_vocab)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return CID_OK;
+  if (!records) return CID_ERR_INVALID_ARGUMENT;
   int64_t offsets[kMaxGroups + 1];
-  for (int64_t g = 0; g < pl.groups; ++g) offsets[g] = g * pl.group_tiles * kBN;
-  offsets[pl.groups] = vocab;
-  return cid_display_combine_records(p.records, static_cast<int>(pl.groups), offsets, token_ids,
-                                     rows, confidence, predicted, current_confidence, status,
-                                     stream);
+  int groups = 0;
+  int rc = launch_lm_head(hidden, rows, hidden_dim, weight_shard, vocab_shard, vocab_offset,
+                          token_ids, round_bf16, workspace, workspace_bytes, status, stream,
+                          offsets, groups);
+  if (rc != CID_OK) return rc;
+  // one record per row over the whole shard
+  return cid_display_merge_records(static_cast<const cid_shard_record_t*>(workspace), groups,
+                                   offsets, token_ids, rows, records, stream);
 }

@@ -300,6 +300,45 @@ Tensor3 lm_head_display_statistics(Backend backend, const at::Tensor& token_ids,
   return {confidence, predicted, current};
 }
 
+at::Tensor lm_head_shard_records(Backend backend, const at::Tensor& token_ids,
+                                 const at::Tensor& hidden, const at::Tensor& weight_shard,
+                                 std::int64_t vocab_offset, std::int64_t total_vocab,
+                                 bool round_bf16) {
+  TORCH_CHECK(token_ids.scalar_type() == at::kLong, "token_ids must use torch.int64");
+  TORCH_CHECK(hidden.dim() >= 1 && hidden.dim() - 1 == token_ids.dim() &&
+                  hidden.sizes().slice(0, hidden.dim() - 1) == token_ids.sizes(),
+              "hidden must have shape [*token_ids.shape, hidden_dim]");
+  TORCH_CHECK(weight_shard.dim() == 2 && weight_shard.size(1) == hidden.size(-1),
+              "weight must have shape [vocab, hidden_dim]");
+  TORCH_CHECK(hidden.scalar_type() == at::kBFloat16 && weight_shard.scalar_type() == at::kBFloat16,
+              "hidden and weight must use torch.bfloat16");
+  TORCH_CHECK(weight_shard.size(0) > 0, "weight vocabulary dimension must be non-empty");
+  TORCH_CHECK(hidden.size(-1) % 8 == 0, "hidden_dim must be a multiple of 8");
+  TORCH_CHECK(vocab_offset >= 0 && vocab_offset + weight_shard.size(0) <= total_vocab,
+              "vocabulary shard must lie inside [0, total_vocab)");
+  same_device("lm_head_shard_records", {&token_ids, &hidden, &weight_shard});
+  auto records = at::empty({token_ids.numel(), 4}, token_ids.options().dtype(at::kInt));
+  if (backend == Backend::kMeta) return records;
+  if (backend == Backend::kCpu) detail::no_cpu_backend("lm_head_shard_records");
+  if (token_ids.numel() == 0) return records;
+  const c10::cuda::CUDAGuard guard(hidden.device());
+  auto h = hidden.contiguous();
+  auto w = weight_shard.contiguous();
+  auto ids = token_ids.contiguous();
+  const auto rows = ids.numel();
+  const size_t ws_bytes = cid_lm_head_workspace_bytes(rows, w.size(0));
+  auto workspace = at::empty({static_cast<std::int64_t>(ws_bytes)},
+                             hidden.options().dtype(at::kByte));
+  check_result(cid_lm_head_shard_records(
+                   h.data_ptr(), rows, h.size(-1), w.data_ptr(), w.size(0), vocab_offset,
+                   total_vocab, ids.data_ptr<std::int64_t>(), round_bf16 ? 1 : 0,
+                   reinterpret_cast<cid_shard_record_t*>(records.data_ptr<int>()),
+                   workspace.data_ptr(), ws_bytes, detail::status_word(h.device()),
+                   stream_of(h)),
+               "lm_head_shard_records");
+  return records;
+}
+
 // ---------------------------------------------------------------------------
 // live_slot_occupancy — csrc/ops.cpp:12-39
 // ---------------------------------------------------------------------------

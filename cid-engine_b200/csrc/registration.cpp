@@ -89,6 +89,13 @@ Tensor3 lm_head_impl(const at::Tensor& ids, const at::Tensor& hidden, const at::
 }
 
 template <Backend B>
+at::Tensor lm_head_shard_impl(const at::Tensor& ids, const at::Tensor& hidden,
+                              const at::Tensor& weight, std::int64_t off, std::int64_t total,
+                              bool round_bf16) {
+  return lm_head_shard_records(B, ids, hidden, weight, off, total, round_bf16);
+}
+
+template <Backend B>
 void register_all(torch::Library& m) {
   m.impl("live_slot_occupancy", TORCH_FN(live_impl<B>));
   m.impl("prefix_allocation_mask", TORCH_FN(prefix_impl<B>));
@@ -104,6 +111,7 @@ void register_all(torch::Library& m) {
   m.impl("display_shard_records", TORCH_FN(shard_records_impl<B>));
   m.impl("display_combine_records", TORCH_FN(combine_records_impl<B>));
   m.impl("lm_head_display_statistics", TORCH_FN(lm_head_impl<B>));
+  m.impl("lm_head_shard_records", TORCH_FN(lm_head_shard_impl<B>));
 }
 
 }  // namespace
@@ -163,6 +171,9 @@ TORCH_LIBRARY(cid_engine, m) {
   m.def(
       "lm_head_display_statistics(Tensor token_ids, Tensor hidden, Tensor weight, "
       "bool round_bf16=True) -> (Tensor, Tensor, Tensor)");
+  m.def(
+      "lm_head_shard_records(Tensor token_ids, Tensor hidden, Tensor weight_shard, "
+      "int vocab_offset, int total_vocab, bool round_bf16=True) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(cid_engine, CUDA, m) {

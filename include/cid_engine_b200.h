@@ -127,6 +127,15 @@ CID_API int cid_display_shard_records(cid_dtype_t dtype, const void* logits,
 
 /* records: world x rows (rank-major).  shard_offsets: world+1 ascending
  * column offsets on the HOST (shard r owns [offsets[r], offsets[r+1])). */
+/* Merges records [world][rows] of ascending column ranges shard_offsets_host
+ * (world + 1 host values) into one record per row of their union, as
+ * cid_display_shard_records would produce for the concatenated range (no
+ * reference counterpart: the merge inside one GPU of the vocabulary-parallel
+ * statistics, used by cid_lm_head_shard_records). */
+CID_API int cid_display_merge_records(const cid_shard_record_t* records, int world,
+                        const int64_t* shard_offsets_host, const int64_t* token_ids,
+                        int64_t rows, cid_shard_record_t* merged, void* stream);
+
 CID_API int cid_display_combine_records(const cid_shard_record_t* records, int world,
                                 const int64_t* shard_offsets_host,
                                 const int64_t* token_ids, int64_t rows,
@@ -322,6 +331,19 @@ CID_API int cid_lm_head_display_statistics(const void* hidden, int64_t rows, int
                         int round_bf16, float* confidence, int64_t* predicted,
                         float* current_confidence, void* workspace,
                         size_t workspace_bytes, uint32_t* status, void* stream);
+
+/* The shard record (cid_display_shard_records) of every row over the logits
+ * hidden @ weight_shard^T, whose rows are the global columns [vocab_offset,
+ * vocab_offset + vocab_shard) of total_vocab, without writing those logits:
+ * the per-rank half of a vocabulary-parallel LM head (the records of all
+ * ranks then go through cid_display_combine_records).  Operands, rounding
+ * and workspace (cid_lm_head_workspace_bytes(rows, vocab_shard)) as
+ * cid_lm_head_display_statistics; records: rows x 16 bytes of device memory. */
+CID_API int cid_lm_head_shard_records(const void* hidden, int64_t rows, int64_t hidden_dim,
+                        const void* weight_shard, int64_t vocab_shard, int64_t vocab_offset,
+                        int64_t total_vocab, const int64_t* token_ids, int round_bf16,
+                        cid_shard_record_t* records, void* workspace, size_t workspace_bytes,
+                        uint32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -136,3 +136,34 @@ def test_lm_head_validation() -> None:
         cid_engine.lm_head_display_statistics(ids, h[:, :60].contiguous(), w[:, :60].contiguous())
     with pytest.raises(RuntimeError, match="shape"):
         cid_engine.lm_head_display_statistics(ids[:4], h, w)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_lm_head_shard_records_combine_to_unsharded(world) -> None:
+    """Vocabulary shards of the weight (as a vocabulary-parallel LM head holds
+    them), reduced to records and combined, give the unsharded statistics:
+    every column's logit is accumulated in the same order, so the argmax is
+    exact; the sums are regrouped (rtol 1e-5)."""
+    import cid_engine
+    from cid_engine import parallel
+
+    rows, V, H = 300, 20011, 128
+    ids, h, w = _inputs(rows, V, H, seed=world)
+    conf, pred, cur = cid_engine.lm_head_display_statistics(ids, h, w)
+    offs = parallel.shard_offsets(V, world)
+    recs = torch.stack([
+        cid_engine.lm_head_shard_records(ids, h, w[offs[r]:offs[r + 1]].contiguous(),
+                                         vocab_offset=offs[r], total_vocab=V)
+        for r in range(world)])
+    c, p, u = cid_engine.display_combine_records(recs, ids.view(1, -1), offs)
+    assert torch.equal(p.view(-1), pred)
+    torch.testing.assert_close(c.view(-1), conf, rtol=1e-5, atol=1e-8)
+    torch.testing.assert_close(u.view(-1), cur, rtol=1e-5, atol=1e-8)
+
+
+def test_lm_head_shard_records_validation() -> None:
+    import cid_engine
+
+    ids, h, w = _inputs(8, 256, 64, seed=1)
+    with pytest.raises(RuntimeError, match="inside"):
+        cid_engine.lm_head_shard_records(ids, h, w, vocab_offset=10, total_vocab=256)

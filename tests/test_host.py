@@ -143,3 +143,22 @@ def test_meta_shapes() -> None:
     assert th[0].dtype == torch.bfloat16 and th[1].shape == (2, 3, 1)
     rec = ops.display_shard_records(*_meta(ids, torch.zeros(3, 5, 7)), 7, 21)
     assert rec.shape == (15, 4) and rec.dtype == torch.int32
+    hid = torch.zeros(3, 5, 64, dtype=torch.bfloat16)
+    wgt = torch.zeros(100, 64, dtype=torch.bfloat16)
+    lc, lp, lu = ops.lm_head_display_statistics(*_meta(ids, hid, wgt))
+    assert lc.shape == (3, 5) and lp.dtype == torch.int64 and lu.dtype == torch.float32
+    lr = ops.lm_head_shard_records(*_meta(ids, hid, wgt), 50, 150)
+    assert lr.shape == (15, 4) and lr.dtype == torch.int32
+
+
+def test_lm_head_validation_on_host() -> None:
+    ops = torch.ops.cid_engine
+    ids = torch.zeros(3, 5, dtype=torch.long)
+    hid = torch.zeros(3, 5, 64, dtype=torch.bfloat16)
+    wgt = torch.zeros(100, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.lm_head_display_statistics(ids, hid, wgt)
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        ops.lm_head_display_statistics(ids, hid.float(), wgt)
+    with pytest.raises(RuntimeError, match="inside"):
+        ops.lm_head_shard_records(ids, hid, wgt, 60, 150)

@@ -73,6 +73,19 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
         expected = cid_engine.refine_display_from_statistics(ids, c, p, u, **kw)
         got = parallel.vocab_parallel_refine(ids, shard, total_vocab=V, **kw)
         assert torch.equal(got, expected)
+        # vocabulary-parallel LM head: weight rows sharded, logits never written
+        V, H = 32003, 128
+        g = torch.Generator(device=dev).manual_seed(11)
+        hid = (torch.randn(3, 40, H, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        wgt = (torch.randn(V, H, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        lids = torch.randint(0, V, (3, 40), generator=g, device=dev)
+        offs = parallel.shard_offsets(V, world)
+        w_shard = wgt[offs[rank]:offs[rank + 1]].contiguous()
+        c, p, u = parallel.vocab_parallel_lm_head_statistics(lids, hid, w_shard, total_vocab=V)
+        e_c, e_p, e_u = cid_engine.lm_head_display_statistics(lids, hid, wgt)
+        assert torch.equal(p, e_p)
+        torch.testing.assert_close(c, e_c, rtol=1e-5, atol=1e-8)
+        torch.testing.assert_close(u, e_u, rtol=1e-5, atol=1e-8)
         torch.cuda.synchronize()
         Path(result_dir, f"ok{rank}").write_text("ok")
     finally:
