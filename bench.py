@@ -599,6 +599,22 @@ def profile_case(name: str) -> None:
 
     import cid_engine
 
+    if name == "refine":  # refinement alone on config-2 and config-4 row shapes
+        g = torch.Generator(device="cuda").manual_seed(1)
+        for B, L in ((32, 1024), (64, 4096)):
+            ids = torch.randint(2, 32000, (B, L), generator=g, device="cuda")
+            ids[torch.rand((B, L), generator=g, device="cuda") < 0.6] = MASK_ID
+            ids[:, L // 2 + 7] = EOS_ID
+            conf = torch.rand((B, L), generator=g, device="cuda")
+            cur = torch.rand((B, L), generator=g, device="cuda") * conf
+            pred = torch.randint(2, 32000, (B, L), generator=g, device="cuda")
+            for _ in range(3):
+                out = cid_engine.refine_display_from_statistics(
+                    ids, conf, pred, cur, mask_token_id=MASK_ID, eos_token_id=EOS_ID,
+                    reveal_fraction=REVEAL, revision_fraction=REVISION, revision_margin=MARGIN)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "checksum": int(out.sum())}))
+        return
     if name == "lm_head":  # fused LM head + statistics: rows 8192, vocab 128256, hidden 4096
         g = torch.Generator(device="cuda").manual_seed(1)
         h = (torch.randn(8192, 4096, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
@@ -632,7 +648,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-min-reps", type=int, default=3)
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
-    ap.add_argument("--profile-case", choices=("cta", "rows", "lm_head"), default=None,
+    ap.add_argument("--profile-case", choices=("cta", "rows", "lm_head", "refine"), default=None,
                     help="run a small statistics case for ncu and exit")
     ap.add_argument("--sample-b", type=int, default=1)
     ap.add_argument("--sample-l", type=int, default=1024)
