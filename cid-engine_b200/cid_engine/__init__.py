@@ -295,7 +295,7 @@ def lm_head_shard_records(
                                                       vocab_offset, total_vocab, round_bf16)
 
 
-from cid_engine.step import refine_step  # noqa: E402
+from cid_engine.step import refine_step, refine_step_from_hidden  # noqa: E402
 from cid_engine.loop import DisplayRefineLoop  # noqa: E402
 
 __all__ = [
@@ -318,6 +318,7 @@ __all__ = [
     "prefix_allocation_mask",
     "refine_display_from_statistics",
     "refine_step",
+    "refine_step_from_hidden",
     "rollout_slot_transition",
     "thought_corrupt_from_epsilon",
 ]

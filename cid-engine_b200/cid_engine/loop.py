@@ -22,7 +22,10 @@ for the device-resident chain:
   statistics and fills the ring position's logits buffer from the current ids.
 
 Without a producer the caller owns the logits ring: step ``s`` reads
-``logits_buffers[s % len(logits_buffers)]``.
+``logits_buffers[s % len(logits_buffers)]``.  With ``lm_head_weight`` the ring
+holds the display positions' hidden states ``[B, L, H]`` instead, and each
+step runs the LM head fused with the statistics
+(``refine_step_from_hidden``): no ``[B, L, V]`` logits are written at all.
 """
 
 from __future__ import annotations
@@ -34,7 +37,7 @@ from collections.abc import Callable, Sequence
 import torch
 from torch import Tensor
 
-from cid_engine.step import SlotInputs, StepOutputs, refine_step
+from cid_engine.step import SlotInputs, StepOutputs, refine_step, refine_step_from_hidden
 
 Producer = Callable[[int, Tensor, Tensor], None]
 
@@ -64,6 +67,7 @@ class DisplayRefineLoop:
         producer: Producer | None = None,
         host_snapshots: int = 4,
         use_graphs: bool = True,
+        lm_head_weight: Tensor | None = None,
     ) -> None:
         if token_ids.device.type != "cuda":
             raise RuntimeError("DisplayRefineLoop runs on CUDA devices only")
@@ -71,11 +75,13 @@ class DisplayRefineLoop:
             raise ValueError("logits_buffers must hold at least one buffer")
         for lg in logits_buffers:
             if lg.device != token_ids.device or tuple(lg.shape[:2]) != tuple(token_ids.shape):
-                raise ValueError("every logits buffer must be [B, L, V] on the ids' device")
+                raise ValueError("every buffer must be [B, L, V] logits (or [B, L, H] hidden "
+                                 "states with lm_head_weight) on the ids' device")
         if host_snapshots < 0:
             raise ValueError("host_snapshots must be >= 0")
         self.device = token_ids.device
         self.logits = list(logits_buffers)
+        self.lm_head_weight = lm_head_weight
         self.params = dict(mask_token_id=mask_token_id, eos_token_id=eos_token_id,
                            reveal_fraction=reveal_fraction, revision_fraction=revision_fraction,
                            revision_margin=revision_margin)
@@ -110,7 +116,11 @@ class DisplayRefineLoop:
         slots = None
         if self.slots is not None:
             slots = dataclasses.replace(self.slots, occupancy=self.occ)
-        out = refine_step(self.ids, lg, slots=slots, **self.params)
+        if self.lm_head_weight is not None:
+            out = refine_step_from_hidden(self.ids, lg, self.lm_head_weight, slots=slots,
+                                          **self.params)
+        else:
+            out = refine_step(self.ids, lg, slots=slots, **self.params)
         self.ids.copy_(out.token_ids)
         if slots is not None:
             self.occ.copy_(out.next_occupancy)

@@ -60,8 +60,53 @@ def refine_step(
 ) -> StepOutputs:
     """stats -> refine (-> rollout -> live occupancy -> snapshot), enqueued
     on the current stream without any host synchronisation."""
+    conf, pred, cur = torch.ops.cid_engine.display_token_statistics(token_ids, logits)
+    return step_from_statistics(token_ids, conf, pred, cur, mask_token_id=mask_token_id,
+                                eos_token_id=eos_token_id, reveal_fraction=reveal_fraction,
+                                revision_fraction=revision_fraction,
+                                revision_margin=revision_margin, slots=slots)
+
+
+def refine_step_from_hidden(
+    token_ids: Tensor,
+    hidden: Tensor,
+    lm_head_weight: Tensor,
+    *,
+    mask_token_id: int,
+    eos_token_id: int | None,
+    reveal_fraction: float,
+    revision_fraction: float,
+    revision_margin: float,
+    slots: SlotInputs | None = None,
+    round_bf16: bool = True,
+) -> StepOutputs:
+    """The same step from the display positions' hidden states: the LM head
+    and the statistics in one kernel (``lm_head_display_statistics``), so no
+    ``[B, L, V]`` logits are written, then the chain of ``refine_step``."""
+    conf, pred, cur = torch.ops.cid_engine.lm_head_display_statistics(
+        token_ids, hidden, lm_head_weight, round_bf16)
+    return step_from_statistics(token_ids, conf, pred, cur, mask_token_id=mask_token_id,
+                                eos_token_id=eos_token_id, reveal_fraction=reveal_fraction,
+                                revision_fraction=revision_fraction,
+                                revision_margin=revision_margin, slots=slots)
+
+
+def step_from_statistics(
+    token_ids: Tensor,
+    conf: Tensor,
+    pred: Tensor,
+    cur: Tensor,
+    *,
+    mask_token_id: int,
+    eos_token_id: int | None,
+    reveal_fraction: float,
+    revision_fraction: float,
+    revision_margin: float,
+    slots: SlotInputs | None = None,
+) -> StepOutputs:
+    """refine (-> rollout -> live occupancy -> snapshot) from the step's
+    display statistics."""
     ops = torch.ops.cid_engine
-    conf, pred, cur = ops.display_token_statistics(token_ids, logits)
     refined = ops.refine_display_from_statistics(
         token_ids, conf, pred, cur, mask_token_id, eos_token_id,
         reveal_fraction, revision_fraction, revision_margin,
@@ -90,4 +135,3 @@ def refine_step(
     out.snapshot = snap
     out.rollout = roll
     return out
-

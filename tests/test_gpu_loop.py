@@ -185,3 +185,37 @@ def test_loop_reset_and_display_only() -> None:
     with pytest.raises(RuntimeError):
         loop.snapshot(0)
     loop.close()
+
+
+def test_loop_from_hidden_states_matches_eager() -> None:
+    """The loop over hidden-state buffers (LM head fused with the statistics)
+    equals the eager chain of refine_step_from_hidden, and each step's
+    statistics are the fused LM head's."""
+    import dataclasses
+
+    import cid_engine
+    from cid_engine.loop import DisplayRefineLoop
+    from cid_engine.step import refine_step_from_hidden
+
+    ids, _, slots = _inputs(B=3, L=64, V=512, S=8, ring=2, seed=21)
+    dev = ids.device
+    g = torch.Generator(device=dev).manual_seed(3)
+    H, V = 64, 3000
+    hidden = [(torch.randn(3, 64, H, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+              for _ in range(2)]
+    weight = (torch.randn(V, H, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    ids = ids.clamp(max=V - 1)
+    loop = DisplayRefineLoop(ids, hidden, slots=slots, lm_head_weight=weight, **PARAMS)
+    occ = slots.occupancy.reshape(3, 8) != 0
+    cur = ids
+    for s in range(5):
+        loop.step()
+        out = refine_step_from_hidden(cur, hidden[s % 2], weight,
+                                      slots=dataclasses.replace(slots, occupancy=occ), **PARAMS)
+        torch.cuda.synchronize()
+        c, p, u = cid_engine.lm_head_display_statistics(cur, hidden[s % 2], weight)
+        assert torch.equal(out.predicted, p) and torch.equal(out.confidence, c)
+        assert torch.equal(loop.last_outputs.token_ids, out.token_ids), f"step {s}"
+        assert torch.equal(loop.last_outputs.snapshot, out.snapshot)
+        cur, occ = out.token_ids, out.next_occupancy
+    loop.close()
