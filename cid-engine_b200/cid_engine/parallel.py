@@ -60,6 +60,144 @@ def vocab_parallel_statistics(token_ids: Tensor, logits_shard: Tensor, *, total_
     return ops.display_combine_records(gathered, token_ids, offs)
 
 
+_DTYPE_CODES = {torch.float32: 0, torch.float64: 1, torch.float16: 2, torch.bfloat16: 3}
+
+
+def _capi():
+    """The C ABI library (loaded already by the torch extension), with the
+    signatures of the peer-exchange entry points."""
+    import ctypes
+    from pathlib import Path
+
+    lib = ctypes.CDLL(str(Path(__file__).resolve().parent / "libcid_engine_b200.so"))
+    if not getattr(lib, "_peer_signatures", False):
+        P, I64, I, U32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint32
+        lib.cid_peer_inbox_bytes.restype = ctypes.c_size_t
+        lib.cid_peer_inbox_bytes.argtypes = [I, I64]
+        lib.cid_peer_inbox_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(P)]
+        lib.cid_peer_inbox_free.argtypes = [P]
+        lib.cid_peer_inbox_export.argtypes = [P, ctypes.c_char_p]
+        lib.cid_peer_inbox_import.argtypes = [ctypes.c_char_p, ctypes.POINTER(P)]
+        lib.cid_peer_inbox_release.argtypes = [P]
+        lib.cid_display_shard_records_to_peers.argtypes = [
+            I, P, I64, P, I64, I64, I64, I64, I, I, ctypes.POINTER(P), I64, U32, P, P]
+        lib.cid_display_combine_inbox.argtypes = [
+            P, I, ctypes.POINTER(I64), P, I64, I64, U32, ctypes.c_double, P, P, P, P, P]
+        lib.cid_result_string.restype = ctypes.c_char_p
+        lib.cid_last_cuda_error.restype = ctypes.c_char_p
+        lib._peer_signatures = True
+    return lib
+
+
+def _check(lib, rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"cid_engine.{what}: {lib.cid_result_string(rc).decode()} "
+                           f"({lib.cid_last_cuda_error().decode()})")
+
+
+class PeerRecordExchange:
+    """Vocabulary-parallel statistics whose record exchange is fused into the
+    statistics kernel over peer memory: no collective in the step.
+
+    At set-up every rank allocates one inbox (``rows_capacity`` rows, two
+    epoch parities), exports its CUDA IPC handle, receives the others' (one
+    ``all_gather_object`` on the process group) and maps them (peer access
+    over NVLink).  A step is two launches on the current stream: the record
+    kernel stores each row's 16-byte record into every rank's inbox and
+    publishes the step's epoch in every rank's flag word, and the combine
+    kernel waits (bounded by ``wait_seconds``) until every rank has published
+    the epoch in this rank's inbox, then merges.  Two parities make reuse
+    safe: a rank starts step k+2 only after every rank's step-k combine.  A
+    wait that runs out sets ``cid_engine.STATUS_PEER_TIMEOUT`` in the device
+    status word and leaves NaN statistics.  Every rank must call
+    ``statistics`` the same number of times."""
+
+    def __init__(self, rows_capacity: int, *, group=None, wait_seconds: float = 5.0) -> None:
+        import ctypes
+
+        self.lib = _capi()
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.capacity = int(rows_capacity)
+        self.wait_seconds = float(wait_seconds)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        nbytes = self.lib.cid_peer_inbox_bytes(self.world, self.capacity)
+        if nbytes == 0:
+            raise ValueError("a peer exchange spans 1..8 ranks and a non-negative capacity")
+        own = ctypes.c_void_p()
+        _check(self.lib, self.lib.cid_peer_inbox_alloc(nbytes, ctypes.byref(own)), "peer_inbox")
+        self.own = own.value
+        handle = ctypes.create_string_buffer(64)
+        _check(self.lib, self.lib.cid_peer_inbox_export(self.own, handle), "peer_inbox")
+        handles = [handle.raw]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+        self.mapped = []
+        ptrs = []
+        for q in range(self.world):
+            if q == self.rank:
+                ptrs.append(self.own)
+                continue
+            peer = ctypes.c_void_p()
+            _check(self.lib, self.lib.cid_peer_inbox_import(handles[q], ctypes.byref(peer)),
+                   "peer_inbox")
+            self.mapped.append(peer.value)
+            ptrs.append(peer.value)
+        self.inboxes = (ctypes.c_void_p * self.world)(*ptrs)
+        self.epoch = 0
+        if self.world > 1:
+            dist.barrier(group=group)  # every inbox zeroed and mapped before any store
+
+    def statistics(self, token_ids: Tensor, logits_shard: Tensor, *, vocab_offset: int,
+                   total_vocab: int, shard_offsets: list[int]):
+        """(confidence, predicted, current) of ``display_token_statistics`` on
+        the unsharded logits, from this rank's shard ``logits_shard`` [B, L, V_r]
+        (columns from ``vocab_offset``) and the ranks' ``shard_offsets``."""
+        import ctypes
+
+        import cid_engine
+
+        ids = token_ids.contiguous()
+        lg = logits_shard.contiguous()
+        rows = ids.numel()
+        if rows > self.capacity:
+            raise ValueError(f"{rows} rows exceed the exchange's capacity {self.capacity}")
+        conf = torch.empty(ids.shape, dtype=torch.float32, device=ids.device)
+        pred = torch.empty(ids.shape, dtype=torch.int64, device=ids.device)
+        cur = torch.empty(ids.shape, dtype=torch.float32, device=ids.device)
+        if rows == 0:
+            return conf, pred, cur
+        self.epoch += 1
+        stream = torch.cuda.current_stream(ids.device).cuda_stream
+        status = cid_engine._C.status_word_ptr(ids.device.index)
+        _check(self.lib, self.lib.cid_display_shard_records_to_peers(
+            _DTYPE_CODES[lg.dtype], lg.data_ptr(), lg.shape[-1], ids.data_ptr(), rows,
+            lg.shape[-1], vocab_offset, total_vocab, self.rank, self.world, self.inboxes,
+            self.capacity, self.epoch & 0xffffffff, status, stream), "shard_records_to_peers")
+        offs = (ctypes.c_int64 * (self.world + 1))(*shard_offsets)
+        _check(self.lib, self.lib.cid_display_combine_inbox(
+            self.own, self.world, offs, ids.data_ptr(), rows, self.capacity,
+            self.epoch & 0xffffffff, self.wait_seconds, conf.data_ptr(), pred.data_ptr(),
+            cur.data_ptr(), status, stream), "combine_inbox")
+        return conf, pred, cur
+
+    def close(self) -> None:
+        """Unmaps the peers' inboxes and frees this rank's (after every rank
+        has finished its steps)."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for ptr in self.mapped:
+            self.lib.cid_peer_inbox_release(ptr)
+        self.mapped = []
+        self.lib.cid_peer_inbox_free(self.own)
+        self.own = None
+
+
 def vocab_parallel_lm_head_statistics(token_ids: Tensor, hidden: Tensor, weight_shard: Tensor, *,
                                       total_vocab: int, round_bf16: bool = True,
                                       group=None) -> tuple[Tensor, Tensor, Tensor]:

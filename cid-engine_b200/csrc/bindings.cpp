@@ -16,4 +16,12 @@ PYBIND11_MODULE(_C, m) {
       [](std::int64_t device, bool reset) { return cid::engine::read_device_status(device, reset); },
       pybind11::arg("device"), pybind11::arg("reset") = false,
       "CID_STATUS_* bits raised by kernels on `device` since the last reset (synchronises).");
+  m.def(
+      "status_word_ptr",
+      [](std::int64_t device) {
+        return reinterpret_cast<std::uintptr_t>(
+            cid::engine::detail::status_word(at::Device(at::kCUDA, static_cast<int>(device))));
+      },
+      pybind11::arg("device"),
+      "Device address of `device`'s status word, for kernels launched through the C ABI.");
 }

@@ -33,6 +33,7 @@
 
 #include <climits>
 #include <cmath>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -48,6 +49,7 @@ constexpr int kThreads = CID_STATS_THREADS;  // threads per CTA
 constexpr int kMaxCluster = 8;
 constexpr float kGap = 5.0f;  // natural-log units; terms stay <= e^5
 constexpr int64_t kNone = LLONG_MAX;
+constexpr int kMaxPeers = 8;  // ranks of a peer record exchange
 
 // packed float32 pair ops (sm_100)
 __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
@@ -229,9 +231,37 @@ struct StatsParams {
   cid_shard_record_t* records;
   int64_t vocab_offset;
   int64_t total_vocab;
+  // peer-exchange variant: this rank's record slot in every rank's inbox and
+  // this rank's flag word there; `counter` (local) counts the rows written
+  cid_shard_record_t* peer_records[kMaxPeers];
+  uint32_t* peer_flags[kMaxPeers];
+  int peers;
+  uint32_t epoch;
+  uint32_t* counter;
 };
 
-enum class Mode { kFinal, kRecord };
+// kFinal: statistics; kRecord: one shard record per row; kPeers: the record
+// stored into every rank's inbox over peer memory, then the epoch published.
+enum class Mode { kFinal, kRecord, kPeers };
+
+// Stores a row's record into every rank's inbox (peer memory over NVLink for
+// the other ranks), and, from the writer of the last row, publishes the
+// epoch in every rank's flag word.  Called by the single writer thread of
+// each row: its stores are fenced at system scope before the row is counted,
+// so a rank that reads a published flag (acquire, system scope) sees every
+// record of that epoch.
+__device__ __forceinline__ void publish_record(const StatsParams& p, int64_t row,
+                                               const cid_shard_record_t& rec) {
+  for (int q = 0; q < p.peers; ++q) p.peer_records[q][row] = rec;
+  __threadfence_system();
+  if (atomicAdd(p.counter, 1u) == static_cast<uint32_t>(p.rows - 1)) {
+    *p.counter = 0;  // the next call counts from zero (stream order)
+    __threadfence_system();
+    for (int q = 0; q < p.peers; ++q)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q]), "r"(p.epoch)
+                   : "memory");
+  }
+}
 
 // Adjacent-run repetition patch of one row: up to two columns whose logit is
 // raised by count*log(multiplier) (csrc/ops.cpp:505-551).
@@ -496,7 +526,8 @@ __device__ void write_special(const StatsParams& p, int64_t row, const T* rowp, 
                 (first_nan != kNone ? static_cast<int32_t>(0x80000000u) : 0);
     const int64_t id = p.ids[row] - p.vocab_offset;
     rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
-    p.records[row] = rec;
+    if (kMode == Mode::kPeers) publish_record(p, row, rec);
+    else p.records[row] = rec;
   }
 }
 
@@ -527,7 +558,8 @@ __device__ void write_normal(const StatsParams& p, int64_t row, const T* rowp, i
     rec.index = static_cast<int32_t>(p.vocab_offset + col);
     const int64_t id = p.ids[row] - p.vocab_offset;
     rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
-    p.records[row] = rec;
+    if (kMode == Mode::kPeers) publish_record(p, row, rec);
+    else p.records[row] = rec;
   }
 }
 
@@ -681,6 +713,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(Stat
 constexpr int kMaxWorld = 64;
 struct CombineParams {
   const cid_shard_record_t* records;
+  int64_t stride;  // records between ranks (rows, or an inbox's capacity)
   int world;
   int64_t offsets[kMaxWorld + 1];
   const int64_t* ids;
@@ -691,13 +724,12 @@ struct CombineParams {
   uint32_t* status;
 };
 
-__global__ void combine_records_kernel(CombineParams p) {
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (row >= p.rows) return;
+// The statistics of one row from its ranks' records.
+__device__ __forceinline__ void combine_row(const CombineParams& p, int64_t row) {
   const float qnan = __int_as_float(0x7fffffff);
   // NaN anywhere: the lowest rank's first NaN (ranks hold ascending columns)
   for (int r = 0; r < p.world; ++r) {
-    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
     if (rec.index < 0) {
       p.predicted[row] = rec.index & 0x7fffffff;
       p.confidence[row] = qnan;
@@ -708,7 +740,7 @@ __global__ void combine_records_kernel(CombineParams p) {
   float M = -INFINITY;
   int32_t idx = p.records[row].index;
   for (int r = 0; r < p.world; ++r) {
-    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
     if (rec.max_logit > M) {
       M = rec.max_logit;
       idx = rec.index;
@@ -722,7 +754,7 @@ __global__ void combine_records_kernel(CombineParams p) {
   }
   float S = 0.0f;
   for (int r = 0; r < p.world; ++r) {
-    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
     if (rec.max_logit == -INFINITY) continue;
     S += rec.sum_exp * ex2((rec.max_logit - M) * kLog2e);
   }
@@ -732,13 +764,59 @@ __global__ void combine_records_kernel(CombineParams p) {
     if (id >= p.offsets[r] && id < p.offsets[r + 1]) owner = r;
   float cur = qnan;
   if (owner >= 0) {
-    const float x = p.records[static_cast<int64_t>(owner) * p.rows + row].current;
+    const float x = p.records[static_cast<int64_t>(owner) * p.stride + row].current;
     cur = __fdiv_rn(ex2((x - M) * kLog2e), S);
   } else if (p.status) {
     atomicOr(p.status, CID_STATUS_TOKEN_ID_OUT_OF_RANGE);
   }
   p.confidence[row] = __fdiv_rn(1.0f, S);
   p.current[row] = cur;
+}
+
+__global__ void combine_records_kernel(CombineParams p) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= p.rows) return;
+  combine_row(p, row);
+}
+
+// Combine from this rank's inbox once every rank has published `epoch` in
+// its flag word there (thread 0 of each CTA waits, acquire at system scope,
+// bounded by wait_ns; a wait that runs out sets CID_STATUS_PEER_TIMEOUT and
+// the CTA writes NaN statistics with predicted 0).
+__global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uint32_t epoch,
+                                     unsigned long long wait_ns) {
+  __shared__ int ready;
+  if (threadIdx.x == 0) {
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    bool ok = true;
+    for (int q = 0; q < p.world && ok; ++q) {
+      for (;;) {
+        uint32_t f;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + q) : "memory");
+        if (static_cast<int32_t>(f - epoch) >= 0) break;
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > wait_ns) {
+          ok = false;
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+    if (!ok && p.status) atomicOr(p.status, CID_STATUS_PEER_TIMEOUT);
+    ready = ok ? 1 : 0;
+  }
+  __syncthreads();
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= p.rows) return;
+  if (!ready) {
+    p.predicted[row] = 0;
+    p.confidence[row] = __int_as_float(0x7fffffff);
+    p.current[row] = __int_as_float(0x7fffffff);
+    return;
+  }
+  combine_row(p, row);
 }
 
 // Merges the records of W ascending column ranges of each row into the one
@@ -753,11 +831,11 @@ __global__ void merge_records_kernel(CombineParams p, cid_shard_record_t* out) {
   float cur = 0.0f;
   for (int r = 0; r < p.world; ++r)
     if (id >= p.offsets[r] && id < p.offsets[r + 1])
-      cur = p.records[static_cast<int64_t>(r) * p.rows + row].current;
+      cur = p.records[static_cast<int64_t>(r) * p.stride + row].current;
   cid_shard_record_t m;
   m.current = cur;
   for (int r = 0; r < p.world; ++r) {
-    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
     if (rec.index < 0) {
       m.max_logit = rec.max_logit;
       m.sum_exp = __int_as_float(0x7fffffff);
@@ -769,7 +847,7 @@ __global__ void merge_records_kernel(CombineParams p, cid_shard_record_t* out) {
   float M = -INFINITY;
   int32_t idx = p.records[row].index;
   for (int r = 0; r < p.world; ++r) {
-    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
     if (rec.max_logit > M) {
       M = rec.max_logit;
       idx = rec.index;
@@ -782,7 +860,7 @@ __global__ void merge_records_kernel(CombineParams p, cid_shard_record_t* out) {
   } else {
     float S = 0.0f;
     for (int r = 0; r < p.world; ++r) {
-      const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.rows + row];
+      const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
       if (rec.max_logit == -INFINITY) continue;
       S += rec.sum_exp * ex2((rec.max_logit - M) * kLog2e);
     }
@@ -999,6 +1077,7 @@ extern "C" int cid_display_merge_records(const cid_shard_record_t* records, int 
   }
   prm.ids = token_ids;
   prm.rows = rows;
+  prm.stride = rows;
   const int threads = 256;
   const int64_t blocks = (rows + threads - 1) / threads;
   merge_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(prm,
@@ -1026,6 +1105,7 @@ extern "C" int cid_display_combine_records(const cid_shard_record_t* records, in
   }
   prm.ids = token_ids;
   prm.rows = rows;
+  prm.stride = rows;
   prm.confidence = confidence;
   prm.predicted = predicted;
   prm.current = current_confidence;
@@ -1033,5 +1113,158 @@ extern "C" int cid_display_combine_records(const cid_shard_record_t* records, in
   const int threads = 256;
   const int64_t blocks = (rows + threads - 1) / threads;
   combine_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(prm);
+  return launch_result();
+}
+
+// ---------------------------------------------------------------------------
+// Peer record exchange: the vocabulary-parallel records stored by the
+// statistics kernel straight into every rank's inbox, instead of a
+// collective after it.
+//
+// Inbox layout (one cudaMalloc per rank, mapped into the other ranks with
+// CUDA IPC): records [2 parities][world][rows_capacity] (16 B each), then a
+// 256-byte tail: flag words [world] (uint32, rank q's last published epoch)
+// at offset 0 and the local row counter at offset 128.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr size_t kInboxTail = 256;
+constexpr size_t kCounterOffset = 128;
+
+size_t inbox_record_bytes(int world, int64_t capacity) {
+  return 2 * static_cast<size_t>(world) * static_cast<size_t>(capacity) *
+         sizeof(cid_shard_record_t);
+}
+cid_shard_record_t* inbox_records(void* inbox, int world, int64_t capacity, uint32_t parity,
+                                  int src) {
+  return static_cast<cid_shard_record_t*>(inbox) +
+         (static_cast<int64_t>(parity) * world + src) * capacity;
+}
+uint32_t* inbox_flags(void* inbox, int world, int64_t capacity) {
+  return reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(inbox) +
+                                     inbox_record_bytes(world, capacity));
+}
+
+}  // namespace
+
+extern "C" size_t cid_peer_inbox_bytes(int world, int64_t rows_capacity) {
+  if (world < 1 || world > kMaxPeers || rows_capacity < 0) return 0;
+  return inbox_record_bytes(world, rows_capacity) + kInboxTail;
+}
+
+extern "C" int cid_peer_inbox_alloc(size_t bytes, void** inbox) {
+  if (!inbox || bytes == 0) return CID_ERR_INVALID_ARGUMENT;
+  *inbox = nullptr;
+  cudaError_t e = cudaMalloc(inbox, bytes);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  e = cudaMemset(*inbox, 0, bytes);  // flags 0 (no epoch yet), counter 0
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(*inbox);
+    *inbox = nullptr;
+    return record_cuda_error(e);
+  }
+  return CID_OK;
+}
+
+extern "C" int cid_peer_inbox_free(void* inbox) {
+  if (!inbox) return CID_OK;
+  return record_cuda_error(cudaFree(inbox));
+}
+
+extern "C" int cid_peer_inbox_export(void* inbox, unsigned char handle[64]) {
+  if (!inbox || !handle) return CID_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, inbox);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(handle, &h, sizeof(h));
+  return CID_OK;
+}
+
+extern "C" int cid_peer_inbox_import(const unsigned char handle[64], void** peer_inbox) {
+  if (!handle || !peer_inbox) return CID_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *peer_inbox = nullptr;
+  return record_cuda_error(
+      cudaIpcOpenMemHandle(peer_inbox, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+extern "C" int cid_peer_inbox_release(void* peer_inbox) {
+  if (!peer_inbox) return CID_OK;
+  return record_cuda_error(cudaIpcCloseMemHandle(peer_inbox));
+}
+
+extern "C" int cid_display_shard_records_to_peers(
+    cid_dtype_t dtype, const void* logits, int64_t row_stride, const int64_t* token_ids,
+    int64_t rows, int64_t shard_vocab, int64_t vocab_offset, int64_t total_vocab, int rank,
+    int world, void* const* inboxes, int64_t rows_capacity, uint32_t epoch, uint32_t* status,
+    void* stream) {
+  int rc = check_logits(dtype, logits, row_stride, rows, shard_vocab);
+  if (rc != CID_OK) return rc;
+  if (vocab_offset < 0 || vocab_offset + shard_vocab > total_vocab || total_vocab > INT_MAX)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !inboxes)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (rows < 1 || rows > rows_capacity || rows > UINT32_MAX || !token_ids)
+    return CID_ERR_INVALID_ARGUMENT;  // every rank publishes, so rows == 0 is not a call
+  for (int q = 0; q < world; ++q)
+    if (!inboxes[q]) return CID_ERR_INVALID_ARGUMENT;
+  StatsParams prm = {};
+  prm.logits = logits;
+  prm.row_stride = row_stride;
+  prm.ids = token_ids;
+  prm.rows = rows;
+  prm.vocab = shard_vocab;
+  prm.status = status;
+  prm.tokens = 1;
+  prm.vocab_offset = vocab_offset;
+  prm.total_vocab = total_vocab;
+  prm.peers = world;
+  prm.epoch = epoch;
+  for (int q = 0; q < world; ++q) {
+    prm.peer_records[q] = inbox_records(inboxes[q], world, rows_capacity, epoch & 1u, rank);
+    prm.peer_flags[q] = inbox_flags(inboxes[q], world, rows_capacity) + rank;
+  }
+  prm.counter = reinterpret_cast<uint32_t*>(
+      reinterpret_cast<unsigned char*>(inbox_flags(inboxes[rank], world, rows_capacity)) +
+      kCounterOffset);
+  return dispatch_stats<false, Mode::kPeers>(dtype, prm, as_stream(stream));
+}
+
+extern "C" int cid_display_combine_inbox(void* inbox, int world,
+                                         const int64_t* shard_offsets_host,
+                                         const int64_t* token_ids, int64_t rows,
+                                         int64_t rows_capacity, uint32_t epoch,
+                                         double wait_seconds, float* confidence,
+                                         int64_t* predicted, float* current_confidence,
+                                         uint32_t* status, void* stream) {
+  if (world < 1 || world > kMaxPeers || !shard_offsets_host || !inbox)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (rows < 1 || rows > rows_capacity || !(wait_seconds > 0.0 && wait_seconds < 3600.0))
+    return CID_ERR_INVALID_ARGUMENT;
+  if (!token_ids || !confidence || !predicted || !current_confidence)
+    return CID_ERR_INVALID_ARGUMENT;
+  CombineParams prm = {};
+  prm.records = inbox_records(inbox, world, rows_capacity, epoch & 1u, 0);
+  prm.stride = rows_capacity;
+  prm.world = world;
+  for (int r = 0; r <= world; ++r) {
+    prm.offsets[r] = shard_offsets_host[r];
+    if (r > 0 && prm.offsets[r] < prm.offsets[r - 1]) return CID_ERR_INVALID_ARGUMENT;
+  }
+  prm.ids = token_ids;
+  prm.rows = rows;
+  prm.confidence = confidence;
+  prm.predicted = predicted;
+  prm.current = current_confidence;
+  prm.status = status;
+  const int threads = 256;
+  const int64_t blocks = (rows + threads - 1) / threads;
+  combine_inbox_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(
+      prm, inbox_flags(inbox, world, rows_capacity), epoch,
+      static_cast<unsigned long long>(wait_seconds * 1e9));
   return launch_result();
 }

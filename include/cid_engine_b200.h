@@ -66,6 +66,9 @@ typedef enum cid_result {
 #define CID_STATUS_ASSIGNMENT_INVALID 0x8u
 /* A bounded wait of the LM-head kernel ran out (its outputs are invalid). */
 #define CID_STATUS_LM_HEAD_TIMEOUT 0x10u
+/* A rank's records of this epoch did not arrive in a peer exchange's wait
+ * (its statistics are NaN). */
+#define CID_STATUS_PEER_TIMEOUT 0x20u
 
 CID_API int cid_abi_version(void);
 CID_API const char* cid_result_string(int result);
@@ -344,6 +347,45 @@ CID_API int cid_lm_head_shard_records(const void* hidden, int64_t rows, int64_t 
                         int64_t total_vocab, const int64_t* token_ids, int round_bf16,
                         cid_shard_record_t* records, void* workspace, size_t workspace_bytes,
                         uint32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Peer record exchange (no reference counterpart: the multi-GPU form of   */
+/* the vocabulary-parallel statistics, csrc/ops.cpp:446-474 sharded).      */
+/* ---------------------------------------------------------------------- */
+
+/* Bytes of one rank's inbox for `world` ranks (<= 8) and up to rows_capacity
+ * rows: records [2][world][rows_capacity] then a 256-byte tail (flag words,
+ * row counter). */
+CID_API size_t cid_peer_inbox_bytes(int world, int64_t rows_capacity);
+/* cudaMalloc'd, zeroed inbox on the current device (set-up, not per step). */
+CID_API int cid_peer_inbox_alloc(size_t bytes, void** inbox);
+CID_API int cid_peer_inbox_free(void* inbox);
+/* CUDA IPC handle of an inbox (64 bytes), and its mapping in another process
+ * of the same node (peer access over NVLink); release unmaps it. */
+CID_API int cid_peer_inbox_export(void* inbox, unsigned char handle[64]);
+CID_API int cid_peer_inbox_import(const unsigned char handle[64], void** peer_inbox);
+CID_API int cid_peer_inbox_release(void* peer_inbox);
+
+/* The shard records of cid_display_shard_records, stored by the statistics
+ * kernel into every rank's inbox (inboxes: `world` device pointers as this
+ * process maps them, inboxes[rank] its own) in the slot of this rank and
+ * epoch parity; the writer of the last row then publishes `epoch` in every
+ * inbox's flag word of this rank (release, system scope).  1 <= rows <=
+ * rows_capacity; `epoch` increases by one per step on every rank. */
+CID_API int cid_display_shard_records_to_peers(cid_dtype_t dtype, const void* logits,
+                        int64_t row_stride, const int64_t* token_ids, int64_t rows,
+                        int64_t shard_vocab, int64_t vocab_offset, int64_t total_vocab,
+                        int rank, int world, void* const* inboxes, int64_t rows_capacity,
+                        uint32_t epoch, uint32_t* status, void* stream);
+
+/* cid_display_combine_records over this rank's inbox once every rank has
+ * published `epoch` there; the wait is bounded by wait_seconds, after which
+ * the statistics are NaN (predicted 0) and CID_STATUS_PEER_TIMEOUT is set. */
+CID_API int cid_display_combine_inbox(void* inbox, int world, const int64_t* shard_offsets_host,
+                        const int64_t* token_ids, int64_t rows, int64_t rows_capacity,
+                        uint32_t epoch, double wait_seconds, float* confidence,
+                        int64_t* predicted, float* current_confidence, uint32_t* status,
+                        void* stream);
 
 #ifdef __cplusplus
 }

@@ -109,3 +109,15 @@ def test_host_validation_rejects_without_a_device(lib: ctypes.CDLL) -> None:
     assert rc == CID_OK
     lib.cid_masked_diffusion_workspace_bytes.restype = ctypes.c_size_t
     assert lib.cid_masked_diffusion_workspace_bytes(i64(64)) == 64 * 8
+
+
+def test_peer_inbox_layout_sizes() -> None:
+    """Inbox bytes: records [2][world][capacity] x 16 B + a 256-byte tail."""
+    import ctypes
+
+    lib = ctypes.CDLL(str(LIB))
+    lib.cid_peer_inbox_bytes.restype = ctypes.c_size_t
+    lib.cid_peer_inbox_bytes.argtypes = [ctypes.c_int, ctypes.c_int64]
+    assert lib.cid_peer_inbox_bytes(2, 100) == 2 * 2 * 100 * 16 + 256
+    assert lib.cid_peer_inbox_bytes(8, 262144) == 2 * 8 * 262144 * 16 + 256
+    assert lib.cid_peer_inbox_bytes(9, 10) == 0 and lib.cid_peer_inbox_bytes(0, 10) == 0

@@ -1,0 +1,106 @@
+"""The peer record exchange (``cid_engine.parallel.PeerRecordExchange``) on
+one GPU: a one-rank exchange equals the record + combine path bit for bit
+over consecutive steps (both epoch parities), and a combine whose epoch no
+rank publishes gives up after its wait limit with a status bit and NaN
+statistics instead of hanging.  The multi-rank exchange over NVLink is
+checked in ``test_multi_gpu.py``."""
+
+from __future__ import annotations
+
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _engine():
+    import cid_engine  # noqa: F401
+
+    assert torch.cuda.is_available()
+    torch.cuda.set_device(0)
+    yield
+    torch.cuda.empty_cache()
+
+
+def _same(a, b):
+    torch.testing.assert_close(a, b, rtol=0, atol=0, equal_nan=True)
+
+
+def test_one_rank_exchange_equals_records_and_combine() -> None:
+    import cid_engine
+    from cid_engine import parallel
+
+    dev = torch.device("cuda", 0)
+    B, L, V = 3, 70, 5003
+    ex = parallel.PeerRecordExchange(B * L + 7)
+    try:
+        for step in range(3):
+            g = torch.Generator(device=dev).manual_seed(step)
+            logits = (torch.randn(B, L, V, generator=g, device=dev) * 3).to(torch.bfloat16)
+            logits[1, 4, [3, V - 1]] = 30.0  # tie: the lower column
+            logits[2, 9, 100] = float("nan")
+            ids = torch.randint(V, (B, L), generator=g, device=dev)
+            ids[0, 0] = V + 3  # outside the vocabulary
+            got = ex.statistics(ids, logits, vocab_offset=0, total_vocab=V, shard_offsets=[0, V])
+            rec = cid_engine.display_shard_records(ids, logits, vocab_offset=0, total_vocab=V)
+            exp = cid_engine.display_combine_records(rec.view(1, B * L, 4), ids, [0, V])
+            for a, e in zip(got, exp):
+                _same(a, e)
+        assert ex.epoch == 3
+    finally:
+        ex.close()
+
+
+def test_unpublished_epoch_times_out_with_status() -> None:
+    """A flag that nothing sets: the combine waits 0.2 s, then reports."""
+    import cid_engine
+    from cid_engine import parallel
+
+    dev = torch.device("cuda", 0)
+    B, L, V = 2, 40, 997
+    ex = parallel.PeerRecordExchange(B * L)
+    try:
+        g = torch.Generator(device=dev).manual_seed(5)
+        logits = torch.randn(B, L, V, generator=g, device=dev)
+        ids = torch.randint(V, (B, L), generator=g, device=dev)
+        ex.statistics(ids, logits, vocab_offset=0, total_vocab=V, shard_offsets=[0, V])
+        torch.cuda.synchronize()
+        cid_engine.device_status(0, reset=True)
+        conf = torch.empty(B, L, device=dev)
+        pred = torch.empty(B, L, dtype=torch.int64, device=dev)
+        cur = torch.empty(B, L, device=dev)
+        offs = (ctypes.c_int64 * 2)(0, V)
+        rc = ex.lib.cid_display_combine_inbox(
+            ex.own, 1, offs, ids.data_ptr(), B * L, B * L, ex.epoch + 2, 0.2, conf.data_ptr(),
+            pred.data_ptr(), cur.data_ptr(), cid_engine._C.status_word_ptr(0),
+            torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert cid_engine.device_status(0) & cid_engine.STATUS_PEER_TIMEOUT
+        assert bool(conf.isnan().all()) and bool(cur.isnan().all()) and bool((pred == 0).all())
+        cid_engine.device_status(0, reset=True)
+        # the exchange itself is unaffected: the next step still matches
+        got = ex.statistics(ids, logits, vocab_offset=0, total_vocab=V, shard_offsets=[0, V])
+        exp = cid_engine.display_token_statistics(ids, logits)
+        assert torch.equal(got[1], exp[1])
+        torch.cuda.synchronize()
+        assert cid_engine.device_status(0) == 0
+    finally:
+        ex.close()
+
+
+def test_exchange_validation() -> None:
+    from cid_engine import parallel
+
+    dev = torch.device("cuda", 0)
+    ex = parallel.PeerRecordExchange(10)
+    try:
+        ids = torch.zeros(2, 8, dtype=torch.int64, device=dev)
+        lg = torch.zeros(2, 8, 16, device=dev)
+        with pytest.raises(ValueError, match="capacity"):
+            ex.statistics(ids, lg, vocab_offset=0, total_vocab=16, shard_offsets=[0, 16])
+    finally:
+        ex.close()

@@ -73,6 +73,28 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
         expected = cid_engine.refine_display_from_statistics(ids, c, p, u, **kw)
         got = parallel.vocab_parallel_refine(ids, shard, total_vocab=V, **kw)
         assert torch.equal(got, expected)
+        # records stored into every rank's inbox by the statistics kernel (no
+        # collective) == the NCCL all-gather path, bit for bit, over steps of
+        # both epoch parities
+        ex = parallel.PeerRecordExchange(2 * 96, wait_seconds=10.0)
+        try:
+            for step in range(3):
+                V = 60013
+                g = torch.Generator(device=dev).manual_seed(100 + step)
+                logits = (torch.randn(2, 96, V, generator=g, device=dev) * 2).to(torch.bfloat16)
+                logits[1, 9, [1, V - 2]] = 40.0
+                ids = torch.randint(V, (2, 96), generator=g, device=dev)
+                offs = parallel.shard_offsets(V, world)
+                shard = logits[..., offs[rank]:offs[rank + 1]].contiguous()
+                got = ex.statistics(ids, shard, vocab_offset=offs[rank], total_vocab=V,
+                                    shard_offsets=offs)
+                exp = parallel.vocab_parallel_statistics(ids, shard, total_vocab=V)
+                for a, e in zip(got, exp):
+                    torch.testing.assert_close(a, e, rtol=0, atol=0, equal_nan=True)
+            torch.cuda.synchronize()
+            assert cid_engine.device_status(rank) == 0
+        finally:
+            ex.close()
         # vocabulary-parallel LM head: weight rows sharded, logits never written
         V, H = 32003, 128
         g = torch.Generator(device=dev).manual_seed(11)
