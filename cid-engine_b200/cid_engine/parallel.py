@@ -151,10 +151,12 @@ class PeerRecordExchange:
             dist.barrier(group=group)  # every inbox zeroed and mapped before any store
 
     def statistics(self, token_ids: Tensor, logits_shard: Tensor, *, vocab_offset: int,
-                   total_vocab: int, shard_offsets: list[int]):
+                   total_vocab: int, shard_offsets: list[int], timing: tuple | None = None):
         """(confidence, predicted, current) of ``display_token_statistics`` on
         the unsharded logits, from this rank's shard ``logits_shard`` [B, L, V_r]
-        (columns from ``vocab_offset``) and the ranks' ``shard_offsets``."""
+        (columns from ``vocab_offset``) and the ranks' ``shard_offsets``.
+        ``timing`` = (start, end) CUDA events recorded around the record
+        kernel."""
         import ctypes
 
         import cid_engine
@@ -170,12 +172,17 @@ class PeerRecordExchange:
         if rows == 0:
             return conf, pred, cur
         self.epoch += 1
-        stream = torch.cuda.current_stream(ids.device).cuda_stream
+        cur_stream = torch.cuda.current_stream(ids.device)
+        stream = cur_stream.cuda_stream
         status = cid_engine._C.status_word_ptr(ids.device.index)
+        if timing is not None:
+            timing[0].record(cur_stream)
         _check(self.lib, self.lib.cid_display_shard_records_to_peers(
             _DTYPE_CODES[lg.dtype], lg.data_ptr(), lg.shape[-1], ids.data_ptr(), rows,
             lg.shape[-1], vocab_offset, total_vocab, self.rank, self.world, self.inboxes,
             self.capacity, self.epoch & 0xffffffff, status, stream), "shard_records_to_peers")
+        if timing is not None:
+            timing[1].record(cur_stream)
         offs = (ctypes.c_int64 * (self.world + 1))(*shard_offsets)
         _check(self.lib, self.lib.cid_display_combine_inbox(
             self.own, self.world, offs, ids.data_ptr(), rows, self.capacity,
@@ -343,11 +350,19 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
     try:
         B, L, V = 64, 4096, 152064
         ids, logits, offs = sharded_display_inputs(B, L, V, rank, world, 3, dev)
+        peers = getattr(args, "exchange", "peers") == "peers"
+        ex = PeerRecordExchange(B * L, wait_seconds=30.0) if peers else None
 
         def step(ev):
-            vocab_parallel_refine(ids, logits, total_vocab=V, mask_token_id=0, eos_token_id=1,
-                                  reveal_fraction=0.25, revision_fraction=0.1,
-                                  revision_margin=0.05, timing=ev)
+            if ex is None:
+                vocab_parallel_refine(ids, logits, total_vocab=V, mask_token_id=0, eos_token_id=1,
+                                      reveal_fraction=0.25, revision_fraction=0.1,
+                                      revision_margin=0.05, timing=ev)
+                return
+            c, p, u = ex.statistics(ids, logits, vocab_offset=offs[rank], total_vocab=V,
+                                    shard_offsets=offs, timing=ev)
+            torch.ops.cid_engine.refine_display_from_statistics(ids, c, p, u, 0, 1, 0.25, 0.1,
+                                                                0.05)
 
         K, W = args.steps, args.warmup
         for _ in range(W):
@@ -373,6 +388,8 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
         t = torch.tensor([ms_local, kern_local], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, kern_ms = float(t[0]), float(t[1])
+        if ex is not None:
+            ex.close()
         e2e = None
         if not args.no_e2e:
             e2e = e2e_vocab_parallel(ids, logits, offs, rank, batch=4,
@@ -398,11 +415,15 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
             "data": "synthetic (seeded bf16 2*N(0,1) logits, 5% planted peaks)",
             "config": {"workload": "vocab-parallel display stats + refine, logits bf16 [64,4096,152064]",
                        "batch": B, "tokens": L, "vocab": V,
-                       "parallelism": f"vocab-sharded x{world} (NCCL all-gather of 16 B row records)",
+                       "parallelism": f"vocab-sharded x{world} " + (
+                           "(16 B row records stored into every rank's inbox by the statistics "
+                           "kernel over NVLink; no collective in the step)" if peers else
+                           "(NCCL all-gather of 16 B row records)"),
                        "l2": f"{shard_bytes / 1e9:.1f} GB per rank per step >> 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "display_stats_rows_kernel<bf16, records> (per rank, max over ranks)",
+                         "kernel": "display_stats_rows_kernel<bf16, " + ("peers" if peers else "records")
+                                   + "> (per rank, max over ranks)",
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
                          "algorithmic_bytes_per_launch": alg},
             "e2e": e2e,

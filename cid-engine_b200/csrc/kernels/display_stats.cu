@@ -231,37 +231,9 @@ struct StatsParams {
   cid_shard_record_t* records;
   int64_t vocab_offset;
   int64_t total_vocab;
-  // peer-exchange variant: this rank's record slot in every rank's inbox and
-  // this rank's flag word there; `counter` (local) counts the rows written
-  cid_shard_record_t* peer_records[kMaxPeers];
-  uint32_t* peer_flags[kMaxPeers];
-  int peers;
-  uint32_t epoch;
-  uint32_t* counter;
 };
 
-// kFinal: statistics; kRecord: one shard record per row; kPeers: the record
-// stored into every rank's inbox over peer memory, then the epoch published.
-enum class Mode { kFinal, kRecord, kPeers };
-
-// Stores a row's record into every rank's inbox (peer memory over NVLink for
-// the other ranks), and, from the writer of the last row, publishes the
-// epoch in every rank's flag word.  Called by the single writer thread of
-// each row: its stores are fenced at system scope before the row is counted,
-// so a rank that reads a published flag (acquire, system scope) sees every
-// record of that epoch.
-__device__ __forceinline__ void publish_record(const StatsParams& p, int64_t row,
-                                               const cid_shard_record_t& rec) {
-  for (int q = 0; q < p.peers; ++q) p.peer_records[q][row] = rec;
-  __threadfence_system();
-  if (atomicAdd(p.counter, 1u) == static_cast<uint32_t>(p.rows - 1)) {
-    *p.counter = 0;  // the next call counts from zero (stream order)
-    __threadfence_system();
-    for (int q = 0; q < p.peers; ++q)
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.peer_flags[q]), "r"(p.epoch)
-                   : "memory");
-  }
-}
+enum class Mode { kFinal, kRecord };
 
 // Adjacent-run repetition patch of one row: up to two columns whose logit is
 // raised by count*log(multiplier) (csrc/ops.cpp:505-551).
@@ -526,8 +498,7 @@ __device__ void write_special(const StatsParams& p, int64_t row, const T* rowp, 
                 (first_nan != kNone ? static_cast<int32_t>(0x80000000u) : 0);
     const int64_t id = p.ids[row] - p.vocab_offset;
     rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
-    if (kMode == Mode::kPeers) publish_record(p, row, rec);
-    else p.records[row] = rec;
+    p.records[row] = rec;
   }
 }
 
@@ -558,8 +529,7 @@ __device__ void write_normal(const StatsParams& p, int64_t row, const T* rowp, i
     rec.index = static_cast<int32_t>(p.vocab_offset + col);
     const int64_t id = p.ids[row] - p.vocab_offset;
     rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
-    if (kMode == Mode::kPeers) publish_record(p, row, rec);
-    else p.records[row] = rec;
+    p.records[row] = rec;
   }
 }
 
@@ -1123,14 +1093,41 @@ extern "C" int cid_display_combine_records(const cid_shard_record_t* records, in
 //
 // Inbox layout (one cudaMalloc per rank, mapped into the other ranks with
 // CUDA IPC): records [2 parities][world][rows_capacity] (16 B each), then a
-// 256-byte tail: flag words [world] (uint32, rank q's last published epoch)
-// at offset 0 and the local row counter at offset 128.
+// 256-byte tail whose first words are the flags [world] (uint32, rank q's
+// last published epoch).
 // ---------------------------------------------------------------------------
 
+namespace cid {
 namespace {
 
+struct PeerSlots {
+  cid_shard_record_t* dst[kMaxPeers];  // this rank's slot in the other ranks' inboxes
+  uint32_t* flags[kMaxPeers];          // this rank's flag word in every inbox
+};
+
+// Copies this rank's records (its slot in its own inbox) into its slot in
+// every other rank's inbox: coalesced 16-byte stores over NVLink.
+__global__ void push_records_kernel(const cid_shard_record_t* src, PeerSlots slots, int others,
+                                    int64_t rows) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const cid_shard_record_t rec = src[row];
+  for (int q = 0; q < others; ++q) slots.dst[q][row] = rec;
+}
+
+// Launched on the stream after the record and push kernels, so all their
+// stores have completed when it runs: a system-scope fence, then the epoch
+// released into this rank's flag word of every inbox.  A rank that acquires
+// the flag (combine_inbox_kernel) sees every record of the epoch.
+__global__ void publish_epoch_kernel(PeerSlots slots, int world, uint32_t epoch) {
+  __threadfence_system();
+  const int q = threadIdx.x;
+  if (q < world)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slots.flags[q]), "r"(epoch)
+                 : "memory");
+}
+
 constexpr size_t kInboxTail = 256;
-constexpr size_t kCounterOffset = 128;
 
 size_t inbox_record_bytes(int world, int64_t capacity) {
   return 2 * static_cast<size_t>(world) * static_cast<size_t>(capacity) *
@@ -1147,6 +1144,7 @@ uint32_t* inbox_flags(void* inbox, int world, int64_t capacity) {
 }
 
 }  // namespace
+}  // namespace cid
 
 extern "C" size_t cid_peer_inbox_bytes(int world, int64_t rows_capacity) {
   if (world < 1 || world > kMaxPeers || rows_capacity < 0) return 0;
@@ -1158,7 +1156,7 @@ extern "C" int cid_peer_inbox_alloc(size_t bytes, void** inbox) {
   *inbox = nullptr;
   cudaError_t e = cudaMalloc(inbox, bytes);
   if (e != cudaSuccess) return record_cuda_error(e);
-  e = cudaMemset(*inbox, 0, bytes);  // flags 0 (no epoch yet), counter 0
+  e = cudaMemset(*inbox, 0, bytes);  // flags 0: no epoch published yet
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     cudaFree(*inbox);
@@ -1222,16 +1220,27 @@ extern "C" int cid_display_shard_records_to_peers(
   prm.tokens = 1;
   prm.vocab_offset = vocab_offset;
   prm.total_vocab = total_vocab;
-  prm.peers = world;
-  prm.epoch = epoch;
+  cid_shard_record_t* own = inbox_records(inboxes[rank], world, rows_capacity, epoch & 1u, rank);
+  prm.records = own;
+  PeerSlots slots = {};
+  int others = 0;
   for (int q = 0; q < world; ++q) {
-    prm.peer_records[q] = inbox_records(inboxes[q], world, rows_capacity, epoch & 1u, rank);
-    prm.peer_flags[q] = inbox_flags(inboxes[q], world, rows_capacity) + rank;
+    slots.flags[q] = inbox_flags(inboxes[q], world, rows_capacity) + rank;
+    if (q != rank)
+      slots.dst[others++] = inbox_records(inboxes[q], world, rows_capacity, epoch & 1u, rank);
   }
-  prm.counter = reinterpret_cast<uint32_t*>(
-      reinterpret_cast<unsigned char*>(inbox_flags(inboxes[rank], world, rows_capacity)) +
-      kCounterOffset);
-  return dispatch_stats<false, Mode::kPeers>(dtype, prm, as_stream(stream));
+  rc = dispatch_stats<false, Mode::kRecord>(dtype, prm, as_stream(stream));
+  if (rc != CID_OK) return rc;
+  if (others > 0) {
+    const int threads = 256;
+    const int64_t blocks = (rows + threads - 1) / threads;
+    push_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(
+        own, slots, others, rows);
+    rc = launch_result();
+    if (rc != CID_OK) return rc;
+  }
+  publish_epoch_kernel<<<1, 32, 0, as_stream(stream)>>>(slots, world, epoch);
+  return launch_result();
 }
 
 extern "C" int cid_display_combine_inbox(void* inbox, int world,

@@ -354,8 +354,7 @@ CID_API int cid_lm_head_shard_records(const void* hidden, int64_t rows, int64_t 
 /* ---------------------------------------------------------------------- */
 
 /* Bytes of one rank's inbox for `world` ranks (<= 8) and up to rows_capacity
- * rows: records [2][world][rows_capacity] then a 256-byte tail (flag words,
- * row counter). */
+ * rows: records [2][world][rows_capacity] then a 256-byte tail (flag words). */
 CID_API size_t cid_peer_inbox_bytes(int world, int64_t rows_capacity);
 /* cudaMalloc'd, zeroed inbox on the current device (set-up, not per step). */
 CID_API int cid_peer_inbox_alloc(size_t bytes, void** inbox);
@@ -366,12 +365,13 @@ CID_API int cid_peer_inbox_export(void* inbox, unsigned char handle[64]);
 CID_API int cid_peer_inbox_import(const unsigned char handle[64], void** peer_inbox);
 CID_API int cid_peer_inbox_release(void* peer_inbox);
 
-/* The shard records of cid_display_shard_records, stored by the statistics
- * kernel into every rank's inbox (inboxes: `world` device pointers as this
- * process maps them, inboxes[rank] its own) in the slot of this rank and
- * epoch parity; the writer of the last row then publishes `epoch` in every
- * inbox's flag word of this rank (release, system scope).  1 <= rows <=
- * rows_capacity; `epoch` increases by one per step on every rank. */
+/* The shard records of cid_display_shard_records written into this rank's
+ * slot (of the epoch's parity) of its own inbox, copied into the same slot of
+ * every other rank's inbox over peer memory (inboxes: `world` device pointers
+ * as this process maps them, inboxes[rank] its own), then `epoch` published in
+ * this rank's flag word of every inbox (system fence, then release).
+ * 1 <= rows <= rows_capacity; `epoch` increases by one per step on every
+ * rank. */
 CID_API int cid_display_shard_records_to_peers(cid_dtype_t dtype, const void* logits,
                         int64_t row_stride, const int64_t* token_ids, int64_t rows,
                         int64_t shard_vocab, int64_t vocab_offset, int64_t total_vocab,
