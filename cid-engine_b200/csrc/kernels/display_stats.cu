@@ -852,14 +852,14 @@ constexpr int kUnroll = 4;
 // two full iterations of 32-byte loads.
 template <typename T, bool kRep, Mode kMode>
 int cluster_size(int64_t rows, int64_t vocab) {
-  static int resident_per_sm = 0;  // per template instance, from the occupancy API
-  if (resident_per_sm == 0) {
+  // per template instance, from the occupancy API (thread-safe one-time init)
+  static const int resident_per_sm = [] {
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, display_stats_kernel<T, kRep, kMode, kUnroll>,
                                                       kThreads, 0) != cudaSuccess || n <= 0)
       n = 4;
-    resident_per_sm = n;
-  }
+    return n;
+  }();
   const int64_t want = 2LL * sm_count() * resident_per_sm;
   const int64_t vecs = vocab * static_cast<int64_t>(sizeof(T)) / kVecBytes;
   const int64_t min_vecs = 2LL * kThreads * kUnroll;
@@ -878,16 +878,15 @@ int cluster_size(int64_t rows, int64_t vocab) {
 template <typename T, bool kRep, Mode kMode>
 bool use_row_warps(int64_t rows) {
   if (CID_STATS_ROW_MODE != 0) return CID_STATS_ROW_MODE == 2;
-  static int warps_per_sm = 0;
-  if (warps_per_sm == 0) {
+  static const int warps_per_sm = [] {  // thread-safe one-time init
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
             &n, display_stats_rows_kernel<T, kRep, kMode, kUnroll>, kRowWarps * 32, 0) !=
             cudaSuccess ||
         n <= 0)
       n = 8;
-    warps_per_sm = n * kRowWarps;
-  }
+    return n * kRowWarps;
+  }();
   return rows >= 2LL * sm_count() * warps_per_sm;
 }
 

@@ -532,15 +532,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {  // thread-safe one-time init
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
             cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  }
+      return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+  }();
   return fn;
 }
 
