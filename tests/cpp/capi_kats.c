@@ -1,8 +1,9 @@
 /* Known-answer tests through the C ABI only (no torch): the reference's
- * C++ KATs (tests/cpp/test_ops.cpp:10-64 of fwerkor/cid-engine v1.1.0) plus
- * the first-tie argmax KAT (tests/test_cuda.py:94-100).  Device memory comes
- * from the CUDA runtime; every entry point runs on the legacy default stream.
- * Exit status 0 = all passed. */
+ * C++ KATs (tests/cpp/test_ops.cpp:10-64 of fwerkor/cid-engine v1.1.0), the
+ * first-tie argmax KAT (tests/test_cuda.py:94-100), the same row through a
+ * one-rank peer record exchange, and the fused LM head on exactly
+ * representable logits.  Device memory comes from the CUDA runtime; every
+ * entry point runs on the legacy default stream.  Exit status 0 = all passed. */
 #include <cuda_runtime_api.h>
 #include <math.h>
 #include <stdio.h>
@@ -83,6 +84,51 @@ int main(void) {
   const double expect = 1.0 / (exp(-4.0) + 2.0 + exp(-3.0));
   CHECK(pred == 1, "argmax must keep the first tie");
   CHECK(fabs(conf - expect) < 2e-6 && fabs(cur - expect) < 2e-6, "statistics mismatch");
+
+  /* the same row through a one-rank peer exchange: inbox, records, combine */
+  size_t inbox_bytes = cid_peer_inbox_bytes(1, 1);
+  void* inbox = NULL;
+  CHECK(inbox_bytes > 0 && cid_peer_inbox_alloc(inbox_bytes, &inbox) == CID_OK, "inbox alloc");
+  void* inboxes[1] = {inbox};
+  CHECK(cid_display_shard_records_to_peers(CID_DTYPE_F32, d_row, 4, d_id, 1, 4, 0, 4, 0, 1,
+                                           inboxes, 1, 1u, NULL, NULL) == CID_OK,
+        "records to peers launch");
+  int64_t offs[2] = {0, 4};
+  CHECK(cid_display_combine_inbox(inbox, 1, offs, d_id, 1, 1, 1u, 5.0, d_conf, d_pred, d_cur,
+                                  NULL, NULL) == CID_OK, "combine inbox launch");
+  cudaMemcpy(&conf, d_conf, 4, cudaMemcpyDeviceToHost);
+  cudaMemcpy(&cur, d_cur, 4, cudaMemcpyDeviceToHost);
+  cudaMemcpy(&pred, d_pred, 8, cudaMemcpyDeviceToHost);
+  CHECK(pred == 1 && fabs(conf - expect) < 2e-6 && fabs(cur - expect) < 2e-6,
+        "peer exchange statistics mismatch");
+  CHECK(cid_peer_inbox_free(inbox) == CID_OK, "inbox free");
+
+  /* LM head fused with the statistics: hidden = e_0 (bf16 1.0), weight column
+   * 0 holds the logits exactly: 3 at columns 5 and 270 (a tie across vocabulary
+   * tiles: the lower column wins), 1 at column 7 (the token), 0 elsewhere;
+   * S = 2 + e^-2 + 297 e^-3 relative to the maximum */
+  enum { H = 64, V = 300 };
+  static uint16_t hid[H], wgt[V * H];
+  hid[0] = 0x3F80;           /* 1.0 */
+  wgt[5 * H] = 0x4040;       /* 3.0 */
+  wgt[270 * H] = 0x4040;     /* 3.0 */
+  wgt[7 * H] = 0x3F80;       /* 1.0 */
+  int64_t lid[1] = {7};
+  void* d_hid = dev_copy(hid, sizeof(hid));
+  void* d_wgt = dev_copy(wgt, sizeof(wgt));
+  int64_t* d_lid = dev_copy(lid, sizeof(lid));
+  size_t ws_bytes = cid_lm_head_workspace_bytes(1, V);
+  void* d_ws = NULL;
+  CHECK(d_hid && d_wgt && d_lid && cudaMalloc(&d_ws, ws_bytes) == cudaSuccess, "cudaMalloc");
+  CHECK(cid_lm_head_display_statistics(d_hid, 1, H, d_wgt, V, d_lid, 1, d_conf, d_pred, d_cur,
+                                       d_ws, ws_bytes, NULL, NULL) == CID_OK, "lm head launch");
+  cudaMemcpy(&conf, d_conf, 4, cudaMemcpyDeviceToHost);
+  cudaMemcpy(&cur, d_cur, 4, cudaMemcpyDeviceToHost);
+  cudaMemcpy(&pred, d_pred, 8, cudaMemcpyDeviceToHost);
+  const double s_lm = 2.0 + exp(-2.0) + 297.0 * exp(-3.0);
+  CHECK(pred == 5, "lm head argmax must keep the first tie");
+  CHECK(fabs(conf - 1.0 / s_lm) < 2e-6 && fabs(cur - exp(-2.0) / s_lm) < 2e-6,
+        "lm head statistics mismatch");
 
   CHECK(cudaDeviceSynchronize() == cudaSuccess, "device error");
   printf("cid-engine B200 C-ABI known-answer tests passed\n");

@@ -256,7 +256,8 @@ def test_assignment_invalid_rows_and_nonfinite_costs_do_not_hang() -> None:
 
 
 def test_c_abi_known_answers(tmp_path) -> None:
-    """The reference's C++ KATs through the C ABI from plain C."""
+    """The reference's C++ KATs, a peer-exchange round and an exact LM-head
+    case through the C ABI from plain C."""
     import subprocess
     from pathlib import Path
 
