@@ -81,6 +81,7 @@ def _capi():
         lib.cid_peer_inbox_release.argtypes = [P]
         lib.cid_display_shard_records_to_peers.argtypes = [
             I, P, I64, P, I64, I64, I64, I64, I, I, ctypes.POINTER(P), I64, U32, P, P]
+        lib.cid_peer_push_records.argtypes = [P, I64, I, I, ctypes.POINTER(P), I64, U32, P]
         lib.cid_display_combine_inbox.argtypes = [
             P, I, ctypes.POINTER(I64), P, I64, I64, U32, ctypes.c_double, P, P, P, P, P]
         lib.cid_result_string.restype = ctypes.c_char_p
@@ -183,12 +184,43 @@ class PeerRecordExchange:
             self.capacity, self.epoch & 0xffffffff, status, stream), "shard_records_to_peers")
         if timing is not None:
             timing[1].record(cur_stream)
+        self._combine(ids, shard_offsets, conf, pred, cur, status, stream)
+        return conf, pred, cur
+
+    def from_records(self, records: Tensor, token_ids: Tensor, *, shard_offsets: list[int]):
+        """The unsharded statistics from this rank's shard records [rows, 4]
+        (int32, e.g. ``lm_head_shard_records``): pushed into every rank's
+        inbox, then combined as in ``statistics``."""
+        ids = token_ids.contiguous()
+        rows = ids.numel()
+        if rows > self.capacity:
+            raise ValueError(f"{rows} rows exceed the exchange's capacity {self.capacity}")
+        assert records.shape == (rows, 4) and records.dtype == torch.int32, "records [rows, 4]"
+        conf = torch.empty(ids.shape, dtype=torch.float32, device=ids.device)
+        pred = torch.empty(ids.shape, dtype=torch.int64, device=ids.device)
+        cur = torch.empty(ids.shape, dtype=torch.float32, device=ids.device)
+        if rows == 0:
+            return conf, pred, cur
+        import cid_engine
+
+        self.epoch += 1
+        stream = torch.cuda.current_stream(ids.device).cuda_stream
+        rec = records.contiguous()
+        _check(self.lib, self.lib.cid_peer_push_records(
+            rec.data_ptr(), rows, self.rank, self.world, self.inboxes, self.capacity,
+            self.epoch & 0xffffffff, stream), "peer_push_records")
+        self._combine(ids, shard_offsets, conf, pred, cur,
+                      cid_engine._C.status_word_ptr(ids.device.index), stream)
+        return conf, pred, cur
+
+    def _combine(self, ids, shard_offsets, conf, pred, cur, status, stream) -> None:
+        import ctypes
+
         offs = (ctypes.c_int64 * (self.world + 1))(*shard_offsets)
         _check(self.lib, self.lib.cid_display_combine_inbox(
-            self.own, self.world, offs, ids.data_ptr(), rows, self.capacity,
+            self.own, self.world, offs, ids.data_ptr(), ids.numel(), self.capacity,
             self.epoch & 0xffffffff, self.wait_seconds, conf.data_ptr(), pred.data_ptr(),
             cur.data_ptr(), status, stream), "combine_inbox")
-        return conf, pred, cur
 
     def close(self) -> None:
         """Unmaps the peers' inboxes and frees this rank's (after every rank
@@ -206,15 +238,17 @@ class PeerRecordExchange:
 
 
 def vocab_parallel_lm_head_statistics(token_ids: Tensor, hidden: Tensor, weight_shard: Tensor, *,
-                                      total_vocab: int, round_bf16: bool = True,
-                                      group=None) -> tuple[Tensor, Tensor, Tensor]:
+                                      total_vocab: int, round_bf16: bool = True, group=None,
+                                      exchange: PeerRecordExchange | None = None
+                                      ) -> tuple[Tensor, Tensor, Tensor]:
     """``display_token_statistics`` of the logits of a vocabulary-parallel LM
     head: this rank holds ``weight_shard`` = the rows
     ``shard_offsets(total_vocab, world)[rank:rank+2]`` of the output
     embedding and the full ``hidden`` states.  Each rank reduces its logits
     to 16-byte row records inside the GEMM (the logits never reach memory),
-    the records are all-gathered over NCCL and combined; every rank returns
-    the unsharded statistics."""
+    the records are all-gathered over NCCL (or, with ``exchange``, pushed into
+    every rank's inbox over peer memory) and combined; every rank returns the
+    unsharded statistics."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     offs = shard_offsets(total_vocab, world)
@@ -222,6 +256,8 @@ def vocab_parallel_lm_head_statistics(token_ids: Tensor, hidden: Tensor, weight_
     ops = torch.ops.cid_engine
     records = ops.lm_head_shard_records(token_ids, hidden, weight_shard, offs[rank], total_vocab,
                                         round_bf16)
+    if exchange is not None:
+        return exchange.from_records(records, token_ids, shard_offsets=offs)
     ids = token_ids.reshape(1, -1)
     c, p, u = ops.display_combine_records(gather_records(records, group), ids, offs)
     return c.view(token_ids.shape), p.view(token_ids.shape), u.view(token_ids.shape)

@@ -1276,3 +1276,26 @@ extern "C" int cid_display_combine_inbox(void* inbox, int world,
       static_cast<unsigned long long>(wait_seconds * 1e9));
   return launch_result();
 }
+
+extern "C" int cid_peer_push_records(const cid_shard_record_t* records, int64_t rows, int rank,
+                                     int world, void* const* inboxes, int64_t rows_capacity,
+                                     uint32_t epoch, void* stream) {
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !inboxes || !records)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (rows < 1 || rows > rows_capacity) return CID_ERR_INVALID_ARGUMENT;
+  for (int q = 0; q < world; ++q)
+    if (!inboxes[q]) return CID_ERR_INVALID_ARGUMENT;
+  PeerSlots slots = {};
+  for (int q = 0; q < world; ++q) {
+    slots.dst[q] = inbox_records(inboxes[q], world, rows_capacity, epoch & 1u, rank);
+    slots.flags[q] = inbox_flags(inboxes[q], world, rows_capacity) + rank;
+  }
+  const int threads = 256;
+  const int64_t blocks = (rows + threads - 1) / threads;
+  push_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(
+      records, slots, world, rows);
+  int rc = launch_result();
+  if (rc != CID_OK) return rc;
+  publish_epoch_kernel<<<1, 32, 0, as_stream(stream)>>>(slots, world, epoch);
+  return launch_result();
+}

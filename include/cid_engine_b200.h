@@ -378,6 +378,14 @@ CID_API int cid_display_shard_records_to_peers(cid_dtype_t dtype, const void* lo
                         int rank, int world, void* const* inboxes, int64_t rows_capacity,
                         uint32_t epoch, uint32_t* status, void* stream);
 
+/* Any per-row shard records of this rank (rows x 16 bytes on the device,
+ * e.g. from cid_lm_head_shard_records) stored into this rank's slot of every
+ * inbox, own included, then `epoch` published as by
+ * cid_display_shard_records_to_peers. */
+CID_API int cid_peer_push_records(const cid_shard_record_t* records, int64_t rows, int rank,
+                        int world, void* const* inboxes, int64_t rows_capacity, uint32_t epoch,
+                        void* stream);
+
 /* cid_display_combine_records over this rank's inbox once every rank has
  * published `epoch` there; the wait is bounded by wait_seconds, after which
  * the statistics are NaN (predicted 0) and CID_STATUS_PEER_TIMEOUT is set. */

@@ -104,3 +104,27 @@ def test_exchange_validation() -> None:
             ex.statistics(ids, lg, vocab_offset=0, total_vocab=16, shard_offsets=[0, 16])
     finally:
         ex.close()
+
+
+def test_one_rank_exchange_from_lm_head_records() -> None:
+    """Records from the fused LM head through the exchange equal the fused
+    LM head's statistics (argmax exact; sums regrouped, rtol 1e-5)."""
+    import cid_engine
+    from cid_engine import parallel
+
+    dev = torch.device("cuda", 0)
+    R, V, H = 200, 9001, 128
+    g = torch.Generator(device=dev).manual_seed(8)
+    hid = (torch.randn(R, H, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    wgt = (torch.randn(V, H, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    ids = torch.randint(V, (R,), generator=g, device=dev)
+    ex = parallel.PeerRecordExchange(R)
+    try:
+        rec = cid_engine.lm_head_shard_records(ids, hid, wgt, vocab_offset=0, total_vocab=V)
+        c, p, u = ex.from_records(rec, ids, shard_offsets=[0, V])
+        e_c, e_p, e_u = cid_engine.lm_head_display_statistics(ids, hid, wgt)
+        assert torch.equal(p, e_p)
+        torch.testing.assert_close(c, e_c, rtol=1e-5, atol=1e-8)
+        torch.testing.assert_close(u, e_u, rtol=1e-5, atol=1e-8)
+    finally:
+        ex.close()

@@ -108,6 +108,16 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
         assert torch.equal(p, e_p)
         torch.testing.assert_close(c, e_c, rtol=1e-5, atol=1e-8)
         torch.testing.assert_close(u, e_u, rtol=1e-5, atol=1e-8)
+        # the same through the peer exchange: bit for bit the NCCL result
+        ex = parallel.PeerRecordExchange(3 * 40, wait_seconds=10.0)
+        try:
+            for _ in range(2):
+                pc, pp, pu = parallel.vocab_parallel_lm_head_statistics(
+                    lids, hid, w_shard, total_vocab=V, exchange=ex)
+                for x, y in ((pc, c), (pp, p), (pu, u)):
+                    torch.testing.assert_close(x, y, rtol=0, atol=0, equal_nan=True)
+        finally:
+            ex.close()
         torch.cuda.synchronize()
         Path(result_dir, f"ok{rank}").write_text("ok")
     finally:
