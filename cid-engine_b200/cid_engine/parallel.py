@@ -463,7 +463,9 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
                          "algorithmic_bytes_per_launch": alg},
             "e2e": e2e,
-            "gpu_launches": 3 * K,
+            # records, push, publish, combine, refine (peers); records, combine,
+            # refine (NCCL; its all-gather kernel is NCCL's)
+            "gpu_launches": (5 if peers else 3) * K,
             "clocks": clk.summary(),
         }
         if rank == 0 and not args.no_cpu_baseline:
