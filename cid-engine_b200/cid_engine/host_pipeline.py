@@ -9,8 +9,6 @@ buffering with CUDA events), so the kernel time hides under the transfer.
 
 from __future__ import annotations
 
-import time
-
 import torch
 from torch import Tensor
 
@@ -75,47 +73,3 @@ def display_token_statistics_from_host(token_ids: Tensor, logits: Tensor, *,
                                        device: torch.device | int = 0, chunk: int | None = None):
     pipe = HostStatisticsPipeline(*logits.shape, dtype=logits.dtype, device=device, chunk=chunk)
     return pipe.statistics(token_ids, logits)
-
-
-def bench_e2e(ids_dev: Tensor, logits_dev: Tensor, *, steps: int, warmup: int, mask_id: int,
-              eos_id: int, reveal: float, revision: float, margin: float) -> dict:
-    """End-to-end step through the public API from pinned host buffers: per
-    step the host->device copy of the logits and ids, statistics, refinement
-    and the device->host read of the refined ids, timed on the device."""
-    dev = logits_dev.device
-    logits_h = torch.empty(logits_dev.shape, dtype=logits_dev.dtype, pin_memory=True)
-    logits_h.copy_(logits_dev)
-    ids_h = torch.empty(ids_dev.shape, dtype=ids_dev.dtype, pin_memory=True)
-    ids_h.copy_(ids_dev)
-    out_h = torch.empty(ids_dev.shape, dtype=ids_dev.dtype, pin_memory=True)
-    pipe = HostStatisticsPipeline(*logits_dev.shape, dtype=logits_dev.dtype, device=dev)
-    ops = torch.ops.cid_engine
-
-    def step():
-        ids = ids_h.to(dev, non_blocking=True)
-        conf, pred, cur = pipe.statistics(ids, logits_h)
-        refined = ops.refine_display_from_statistics(ids, conf, pred, cur, mask_id, eos_id,
-                                                     reveal, revision, margin)
-        out_h.copy_(refined, non_blocking=True)
-        return refined
-
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0 = time.perf_counter()
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize(dev)
-    wall = (time.perf_counter() - w0) / steps
-    ms = a.elapsed_time(b) / steps
-    nbytes = logits_dev.numel() * logits_dev.element_size()
-    h2d = nbytes + ids_dev.numel() * ids_dev.element_size()
-    d2h = ids_dev.numel() * ids_dev.element_size()
-    del pipe, logits_h
-    return {"value": round(nbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": round(ms, 3), "wall_ms_per_step": round(wall * 1e3, 3),
-            "steps": steps, "api": "cid_engine.host_pipeline + refine_display_from_statistics"}

@@ -17,10 +17,6 @@ an all-gather of records followed by a deterministic device-side merge.
 
 from __future__ import annotations
 
-import json
-import os
-import statistics as pystats
-from datetime import timedelta
 
 import torch
 import torch.distributed as dist
@@ -288,193 +284,3 @@ def vocab_parallel_refine(token_ids: Tensor, logits_shard: Tensor, *, total_voca
     c, p, u = ops.display_combine_records(gather_records(rec, group), token_ids, offs)
     return ops.refine_display_from_statistics(token_ids, c, p, u, mask_token_id, eos_token_id,
                                               reveal_fraction, revision_fraction, revision_margin)
-
-
-# ---------------------------------------------------------------------------
-# multi-GPU bench arm (launched by bench.py under torchrun)
-# ---------------------------------------------------------------------------
-
-
-def sharded_display_inputs(B, L, V, rank, world, seed, device):
-    """This rank's vocabulary shard of the config-4 logits: bf16(2 N(0,1))
-    with a +8 peak in 5% of rows at a column drawn once for all ranks."""
-    offs = shard_offsets(V, world)
-    lo, hi = offs[rank], offs[rank + 1]
-    g = torch.Generator(device=device).manual_seed(seed * 1000 + rank)
-    logits = torch.randn((B, L, hi - lo), generator=g, device=device, dtype=torch.bfloat16)
-    logits.mul_(2.0)
-    gs = torch.Generator(device=device).manual_seed(seed)  # shared by all ranks
-    rows = B * L
-    peak = torch.rand(rows, generator=gs, device=device) < 0.05
-    col = torch.randint(V, (rows,), generator=gs, device=device)
-    mine = torch.nonzero(peak & (col >= lo) & (col < hi)).flatten()
-    flat = logits.view(rows, hi - lo)
-    flat[mine, col[mine] - lo] = (flat[mine, col[mine] - lo].float() + 8.0).to(torch.bfloat16)
-    # display ids (identical on every rank): masked with p=0.6, one EOS per row
-    ids = torch.randint(2, V, (B, L), generator=gs, device=device)
-    ids[torch.rand((B, L), generator=gs, device=device) < 0.6] = 0
-    eos_at = torch.randint(L // 2, L, (B,), generator=gs, device=device)
-    pos = torch.arange(L, device=device).expand(B, L)
-    ids[pos == eos_at[:, None]] = 1
-    ids[pos > eos_at[:, None]] = 0
-    return ids, logits, offs
-
-
-def e2e_vocab_parallel(ids: Tensor, logits: Tensor, offs: list[int], rank: int, *, batch: int,
-                       steps: int, warmup: int) -> dict:
-    """End-to-end vocabulary-parallel step through the public API from pinned
-    host memory on every rank: per step the ids and this rank's logits shard
-    (the first ``batch`` sequences) go host->device, overlapped in chunks with
-    the record kernel (``HostStatisticsPipeline``), the records are
-    all-gathered and combined, the rows refined and the refined ids read
-    back.  Device time, max over ranks."""
-    from cid_engine.host_pipeline import HostStatisticsPipeline
-
-    dev = logits.device
-    V, lo = offs[-1], offs[rank]
-    world = dist.get_world_size()
-    sub = logits[:batch]
-    logits_h = torch.empty(sub.shape, dtype=sub.dtype, pin_memory=True)
-    logits_h.copy_(sub)
-    ids_h = torch.empty(ids[:batch].shape, dtype=ids.dtype, pin_memory=True)
-    ids_h.copy_(ids[:batch])
-    out_h = torch.empty_like(ids_h, pin_memory=True)
-    ops = torch.ops.cid_engine
-    pipe = HostStatisticsPipeline(*sub.shape, dtype=sub.dtype, device=dev,
-                                  reduce=lambda i, x: ops.display_shard_records(i, x, lo, V))
-
-    def step():
-        i = ids_h.to(dev, non_blocking=True)
-        rec = pipe.statistics(i, logits_h)
-        c, p, u = ops.display_combine_records(gather_records(rec), i, offs)
-        refined = ops.refine_display_from_statistics(i, c, p, u, 0, 1, 0.25, 0.1, 0.05)
-        out_h.copy_(refined, non_blocking=True)
-
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([a.elapsed_time(b) / steps], device=dev, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0])
-    total = batch * ids.shape[1] * V * logits.element_size()
-    ids_bytes = ids_h.numel() * ids_h.element_size()
-    del pipe, logits_h
-    return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": total + world * ids_bytes,
-            "d2h_bytes_per_step": world * ids_bytes,
-            "ms_per_step": round(ms, 3), "steps": steps,
-            "sample": f"first {batch} of {ids.shape[0]} sequences on every rank (bytes: all ranks)",
-            "api": "cid_engine.host_pipeline (display_shard_records) + parallel.gather_records + "
-                   "display_combine_records + refine_display_from_statistics"}
-
-
-def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_baseline) -> dict:
-    rank = int(os.environ["RANK"])
-    world = int(os.environ["WORLD_SIZE"])
-    local = int(os.environ.get("LOCAL_RANK", rank))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    try:
-        B, L, V = 64, 4096, 152064
-        ids, logits, offs = sharded_display_inputs(B, L, V, rank, world, 3, dev)
-        peers = getattr(args, "exchange", "peers") == "peers"
-        ex = PeerRecordExchange(B * L, wait_seconds=30.0) if peers else None
-
-        def step(ev):
-            if ex is None:
-                vocab_parallel_refine(ids, logits, total_vocab=V, mask_token_id=0, eos_token_id=1,
-                                      reveal_fraction=0.25, revision_fraction=0.1,
-                                      revision_margin=0.05, timing=ev)
-                return
-            c, p, u = ex.statistics(ids, logits, vocab_offset=offs[rank], total_vocab=V,
-                                    shard_offsets=offs, timing=ev)
-            torch.ops.cid_engine.refine_display_from_statistics(ids, c, p, u, 0, 1, 0.25, 0.1,
-                                                                0.05)
-
-        K, W = args.steps, args.warmup
-        for _ in range(W):
-            step(None)
-        torch.cuda.synchronize()
-        dist.barrier()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                 for _ in range(K)]
-        with ClockSampler(local) as clk:
-            clk.mark_start()
-            a.record()
-            for k in range(K):
-                step(pairs[k])
-            b.record()
-            torch.cuda.synchronize()
-            clk.mark_end()
-        dist.barrier()
-        torch.cuda.synchronize()
-        ms_local = a.elapsed_time(b) / K
-        kern_local = pystats.mean(x.elapsed_time(y) for x, y in pairs)
-        t = torch.tensor([ms_local, kern_local], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, kern_ms = float(t[0]), float(t[1])
-        if ex is not None:
-            ex.close()
-        e2e = None
-        if not args.no_e2e:
-            e2e = e2e_vocab_parallel(ids, logits, offs, rank, batch=4,
-                                     steps=max(3, min(K, args.e2e_steps)), warmup=2)
-        total_bytes = B * L * V * 2
-        shard_bytes = logits.numel() * 2
-        peak, peak_kind = peaks()
-        rows = B * L
-        alg = shard_bytes + rows * (8 + 16)
-        achieved = alg / (kern_ms * 1e-3) / 1e9
-        line = {
-            "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
-            "value": round(total_bytes / (ms * 1e-3) / 1e9, 2),
-            "unit": "GB/s",
-            "n_gpus": world,
-            "steps": K,
-            "warmup": W,
-            "ms_per_step": round(ms, 4),
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic (seeded bf16 2*N(0,1) logits, 5% planted peaks)",
-            "config": {"workload": "vocab-parallel display stats + refine, logits bf16 [64,4096,152064]",
-                       "batch": B, "tokens": L, "vocab": V,
-                       "parallelism": f"vocab-sharded x{world} " + (
-                           "(16 B row records stored into every rank's inbox by the statistics "
-                           "kernel over NVLink; no collective in the step)" if peers else
-                           "(NCCL all-gather of 16 B row records)"),
-                       "l2": f"{shard_bytes / 1e9:.1f} GB per rank per step >> 126 MB L2"},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "display_stats_rows_kernel<bf16, " + ("peers" if peers else "records")
-                                   + "> (per rank, max over ranks)",
-                         "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
-                         "algorithmic_bytes_per_launch": alg},
-            "e2e": e2e,
-            # records, push, publish, combine, refine (peers); records, combine,
-            # refine (NCCL; its all-gather kernel is NCCL's)
-            "gpu_launches": (5 if peers else 3) * K,
-            "clocks": clk.summary(),
-        }
-        if rank == 0 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = run_cpu_baseline(sample=(1, 512, V), seconds=args.cpu_seconds)
-        dist.barrier()
-        return line
-    finally:
-        dist.destroy_process_group()
-
-
-if __name__ == "__main__":  # pragma: no cover
-    print(json.dumps(shard_offsets(152064, 8)))
