@@ -434,11 +434,20 @@ __device__ int64_t first_column(const Acc& a, float target, const T* row, int64_
   if (!(a.m == target)) return kNone;
   if (a.where < 0) return -a.where - 1;
   const Vec32* vrow = reinterpret_cast<const Vec32*>(row + head);
+  // all U vectors of the chunk requested before any is scanned: one L2
+  // round trip instead of up to U dependent ones
+  Vec32 v[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const int64_t vi = a.where + static_cast<int64_t>(k) * kStride;
+    if (vi < v_end) v[k] = vrow[vi];
+  }
+#pragma unroll
   for (int k = 0; k < U; ++k) {
     const int64_t vi = a.where + static_cast<int64_t>(k) * kStride;
     if (vi >= v_end) break;
     float x[N];
-    to_float32<T>(vrow[vi], x);
+    to_float32<T>(v[k], x);
 #pragma unroll
     for (int j = 0; j < N; ++j) {
       const int64_t col = head + vi * N + j;
@@ -478,12 +487,21 @@ __device__ __forceinline__ int64_t block_min_i64(int64_t v, int64_t* smem) {
   return r;
 }
 
+// The row's token id relative to this launch's columns, and the logit there
+// (0 outside them); loaded by the row's writer when the row starts, so that
+// both dependent loads complete under the streaming instead of after it.
+template <typename T, Mode kMode>
+__device__ __forceinline__ void load_current(const StatsParams& p, int64_t row, const T* rowp,
+                                             int64_t V, int64_t& id, float& x) {
+  id = __ldg(p.ids + row) - (kMode == Mode::kRecord ? p.vocab_offset : 0);
+  x = (id >= 0 && id < V) ? VecTraits<T>::scalar(rowp, id) : 0.0f;
+}
+
 // Outputs of one row whose maximum is not finite or whose sum is NaN:
 // predicted = first NaN, else first maximum; statistics NaN.
 template <typename T, Mode kMode>
-__device__ void write_special(const StatsParams& p, int64_t row, const T* rowp, int64_t V,
-                              float m, int64_t first_nan, int64_t first_max) {
-  using VT = VecTraits<T>;
+__device__ void write_special(const StatsParams& p, int64_t row, float cur_x, float m,
+                              int64_t first_nan, int64_t first_max) {
   const float qnan = __int_as_float(0x7fffffff);
   const int64_t local = first_nan != kNone ? first_nan : (first_max != kNone ? first_max : 0);
   if (kMode == Mode::kFinal) {
@@ -496,23 +514,20 @@ __device__ void write_special(const StatsParams& p, int64_t row, const T* rowp, 
     rec.sum_exp = m == -INFINITY ? 0.0f : qnan;
     rec.index = static_cast<int32_t>(p.vocab_offset + local) |
                 (first_nan != kNone ? static_cast<int32_t>(0x80000000u) : 0);
-    const int64_t id = p.ids[row] - p.vocab_offset;
-    rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
+    rec.current = cur_x;
     p.records[row] = rec;
   }
 }
 
 // Outputs of one ordinary row from its merged partial and argmax column.
 template <typename T, bool kRep, Mode kMode>
-__device__ void write_normal(const StatsParams& p, int64_t row, const T* rowp, int64_t V,
-                             const Patch& pt, const Partial& fin, int64_t col) {
-  using VT = VecTraits<T>;
+__device__ void write_normal(const StatsParams& p, int64_t row, int64_t V, int64_t id,
+                             float cur_x, const Patch& pt, const Partial& fin, int64_t col) {
   const float top = ex2(fmaf(fin.m, kLog2e, -fin.off));  // 2^(max*log2e - off)
   if (kMode == Mode::kFinal) {
-    const int64_t id = p.ids[row];
     float cur;
     if (id >= 0 && id < V) {
-      float x = VT::scalar(rowp, id);
+      float x = cur_x;
       if (kRep) x = patched(pt, id, x);
       cur = __fdiv_rn(ex2(fmaf(x, kLog2e, -fin.off)), fin.s);
     } else {
@@ -527,8 +542,7 @@ __device__ void write_normal(const StatsParams& p, int64_t row, const T* rowp, i
     rec.max_logit = fin.m;
     rec.sum_exp = __fdiv_rn(fin.s, top);  // sum of exp(x - max) over the shard
     rec.index = static_cast<int32_t>(p.vocab_offset + col);
-    const int64_t id = p.ids[row] - p.vocab_offset;
-    rec.current = (id >= 0 && id < V) ? VT::scalar(rowp, id) : 0.0f;
+    rec.current = cur_x;
     p.records[row] = rec;
   }
 }
@@ -571,6 +585,9 @@ __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) 
   const int64_t t_beg = rank == nrank - 1 ? tail_beg : V;
 
   Acc a{-INFINITY, -INFINITY, 0.0f, 0.0f, 0.0f, kNone};
+  int64_t cur_id = 0;
+  float cur_x = 0.0f;
+  if (threadIdx.x == 0 && rank == 0) load_current<T, kMode>(p, row, rowp, V, cur_id, cur_x);
   stream_row<T, kRep, kThreads, U>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
   Partial mine{a.m, a.om, a.off, a.s0 + a.s1};
   const Partial cta = block_merge(mine, warp_parts, &cta_part);
@@ -613,10 +630,10 @@ __global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) 
     }
     first_nan = block_min_i64(first_nan, red);
     first_max = block_min_i64(first_max, red);
-    if (threadIdx.x == 0) write_special<T, kMode>(p, row, rowp, V, fin.m, first_nan, first_max);
+    if (threadIdx.x == 0) write_special<T, kMode>(p, row, cur_x, fin.m, first_nan, first_max);
     return;
   }
-  if (threadIdx.x == 0) write_normal<T, kRep, kMode>(p, row, rowp, V, pt, fin, col);
+  if (threadIdx.x == 0) write_normal<T, kRep, kMode>(p, row, V, cur_id, cur_x, pt, fin, col);
 }
 
 // One warp per row (no block barriers): for many rows of moderate length,
@@ -654,6 +671,9 @@ __global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(Stat
   const int64_t tail_beg = head + nvec * N;
 
   Acc a{-INFINITY, -INFINITY, 0.0f, 0.0f, 0.0f, kNone};
+  int64_t cur_id = 0;
+  float cur_x = 0.0f;
+  if (lane == 0) load_current<T, kMode>(p, row, rowp, V, cur_id, cur_x);
   stream_row<T, kRep, 32, U>(rowp, head, 0, nvec, head, tail_beg, V, pt, a, lane);
   Partial fin{a.m, a.om, a.off, a.s0 + a.s1};
 #pragma unroll
@@ -669,11 +689,11 @@ __global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(Stat
     }
     first_nan = warp_min_i64(first_nan);
     first_max = warp_min_i64(first_max);
-    if (lane == 0) write_special<T, kMode>(p, row, rowp, V, fin.m, first_nan, first_max);
+    if (lane == 0) write_special<T, kMode>(p, row, cur_x, fin.m, first_nan, first_max);
     return;
   }
   const int64_t col = warp_min_i64(first_column<T, kRep, 32, U>(a, fin.m, rowp, head, nvec, pt));
-  if (lane == 0) write_normal<T, kRep, kMode>(p, row, rowp, V, pt, fin, col);
+  if (lane == 0) write_normal<T, kRep, kMode>(p, row, V, cur_id, cur_x, pt, fin, col);
 }
 
 // ---------------------------------------------------------------------------
