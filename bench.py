@@ -818,8 +818,8 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
                        "l2": f"{shard_bytes / 1e9:.1f} GB per rank per step >> 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "display_stats_rows_kernel<bf16, " + ("peers" if peers else "records")
-                                   + "> (per rank, max over ranks)",
+                         "kernel": "display_stats_rows_kernel<bf16, records> (per rank, max over ranks"
+                                   + ("; then pushed to the peers' inboxes)" if peers else ")"),
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
                          "algorithmic_bytes_per_launch": alg},
             "e2e": e2e,
