@@ -95,6 +95,30 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
             assert cid_engine.device_status(rank) == 0
         finally:
             ex.close()
+        # failure detection without a fault: the other ranks leave between steps
+        # (nothing of theirs in flight) and skip step 2; rank 0's combine waits
+        # out its limit, reports STATUS_PEER_TIMEOUT and leaves NaN statistics;
+        # the ranks then meet on the host and close
+        ex = parallel.PeerRecordExchange(2 * 96, wait_seconds=0.5)
+        try:
+            V = 60013
+            g = torch.Generator(device=dev).manual_seed(200)
+            logits = (torch.randn(2, 96, V, generator=g, device=dev) * 2).to(torch.bfloat16)
+            ids = torch.randint(V, (2, 96), generator=g, device=dev)
+            offs = parallel.shard_offsets(V, world)
+            shard = logits[..., offs[rank]:offs[rank + 1]].contiguous()
+            kw2 = dict(vocab_offset=offs[rank], total_vocab=V, shard_offsets=offs)
+            ok = ex.statistics(ids, shard, **kw2)
+            torch.cuda.synchronize()
+            assert cid_engine.device_status(rank, reset=True) == 0
+            assert not bool(ok[0].isnan().all())
+            if rank == 0:
+                lost = ex.statistics(ids, shard, **kw2)
+                torch.cuda.synchronize()
+                assert cid_engine.device_status(rank, reset=True) & cid_engine.STATUS_PEER_TIMEOUT
+                assert bool(lost[0].isnan().all()) and bool((lost[1] == 0).all())
+        finally:
+            ex.close()  # host barrier: every rank is between steps
         # vocabulary-parallel LM head: weight rows sharded, logits never written
         V, H = 32003, 128
         g = torch.Generator(device=dev).manual_seed(11)
