@@ -526,6 +526,38 @@ def bench_small_configs(dev) -> dict:
         ops.masked_diffusion_corrupt_from_random(*md)
 
     ms3 = _graph_time_ms(cfg3_call, 1000)
+
+    def rep_step():
+        lg = copies[state["k"] % len(copies)]
+        state["k"] += 1
+        ops.display_token_statistics_with_repetition(ids, lg, MASK_ID, EOS_ID, 0.7)
+
+    ms_rep = _graph_time_ms(rep_step, 64)
+
+    # display-token corruption at the masked-diffusion shape: ids [64,2048] over
+    # a 50257-token vocabulary, 85 % eligible, a quarter of the corrupted
+    # positions replaced by random tokens
+    gd = torch.Generator().manual_seed(11)
+    B3, T3, V3 = 64, 2048, 50257
+    dc = [torch.randint(0, V3, (B3, T3), generator=gd), torch.rand(B3, generator=gd),
+          torch.rand(B3, T3, generator=gd) > 0.15, torch.rand(B3, T3, generator=gd),
+          torch.rand(B3, T3, generator=gd), torch.randint(1, V3, (B3, T3), generator=gd)]
+    dc = [t.to(dev) for t in dc]
+
+    def dc_call():
+        ops.display_corrupt_from_random(*dc, V3 - 1, EOS_ID, V3, 0.25)
+
+    ms_dc = _graph_time_ms(dc_call, 1000)
+
+    # linear assignment: 4096 problems of 16 x 16 costs (the largest column
+    # count the warp solver takes), full rows
+    costs = torch.randn(4096, 16, 16, generator=gd).to(dev)
+    counts = torch.full((4096,), 16, dtype=torch.int64).to(dev)
+
+    def la_call():
+        ops.batched_linear_assignment(costs, counts)
+
+    ms_la = _graph_time_ms(la_call, 200)
     del copies
     torch.cuda.empty_cache()
     return {
@@ -537,6 +569,19 @@ def bench_small_configs(dev) -> dict:
                                   "us_per_call": round(ms3 * 1e3, 3),
                                   "GBps": round(2_753_032 / (ms3 * 1e-3) / 1e9, 1),
                                   "launches_per_call": 2, "timing": "CUDA graph, 1000 calls"},
+        "cfg1_repetition_stats": {"workload": "fp32 [4,256,32000], mask 0, eos 1, multiplier 0.7",
+                                  "us_per_call": round(ms_rep * 1e3, 2),
+                                  "logits_GBps": round(131_072_000 / (ms_rep * 1e-3) / 1e9, 1),
+                                  "timing": "CUDA graph, 64 calls, 8 rotating inputs"},
+        "display_corruption": {"workload": "ids [64,2048], vocab 50257, replacement 0.25",
+                               "us_per_call": round(ms_dc * 1e3, 3),
+                               # 25 B in + 18 B out per token, 4 B timestep per row
+                               "GBps": round((B3 * T3 * 43 + B3 * 4) / (ms_dc * 1e-3) / 1e9, 1),
+                               "timing": "CUDA graph, 1000 calls"},
+        "linear_assignment": {"workload": "4096 problems, 16 x 16 f32 costs",
+                              "us_per_call": round(ms_la * 1e3, 2),
+                              "problems_per_s": round(4096 / (ms_la * 1e-3)),
+                              "timing": "CUDA graph, 200 calls"},
     }
 
 
