@@ -7,7 +7,8 @@
 //  * thought corruption (csrc/ops.cpp:258-290): one CTA per slot row, alpha
 //    computed once per row, every arithmetic step rounded to the storage
 //    dtype as ATen does;
-//  * display corruption (csrc/ops.cpp:292-391): one CTA per row.
+//  * display corruption (csrc/ops.cpp:292-391): one CTA of 256 to 1024
+//    threads per row, four tokens' loads in flight per thread.
 #include <climits>
 #include <cmath>
 #include <mutex>
@@ -243,19 +244,48 @@ __device__ __forceinline__ int64_t floor_mod(int64_t a, int64_t m) {
   return (r != 0 && ((r < 0) != (m < 0))) ? r + m : r;
 }
 
-__global__ void __launch_bounds__(kT) display_corrupt_kernel(DisplayCorruptParams p) {
-  __shared__ int s_any[kWarps];
-  __shared__ int64_t s_first[kWarps];
+// torch.remainder(id + offset, vocab) for vocab >= 3 (ops.cpp:364-365): the
+// int64 sum wraps as ATen's does; a sum already in [0, vocab) needs no
+// division and one in [0, 2^32) a 32-bit one.
+__device__ __forceinline__ int64_t wrap_vocab(int64_t id, int64_t offset, int64_t vocab) {
+  const int64_t x = static_cast<int64_t>(static_cast<uint64_t>(id) + static_cast<uint64_t>(offset));
+  if (x >= 0 && x < vocab) return x;
+  if (x >= 0 && x <= int64_t{UINT32_MAX} && vocab <= int64_t{UINT32_MAX})
+    return static_cast<uint32_t>(x) % static_cast<uint32_t>(vocab);
+  return floor_mod(x, vocab);
+}
+
+constexpr int kCorruptBatch = 4;  // tokens per thread whose loads are issued together
+
+// One CTA of kBT threads per row, two passes over the row: the first finds
+// whether any eligible position falls below the timestep and the first
+// eligible position (the fallback, ops.cpp:326-337); the second writes the
+// four outputs.  Each thread issues the loads of kCorruptBatch tokens
+// (kBT apart, so every load instruction is coalesced) before it uses them.
+template <int kBT>
+__global__ void __launch_bounds__(kBT) display_corrupt_kernel(DisplayCorruptParams p) {
+  constexpr int kW = kBT / 32;
+  constexpr int U = kCorruptBatch;
+  __shared__ int64_t s_first[kW];
   const int64_t row = blockIdx.x;
   const int64_t base = row * p.tokens;
   const float t = load_float(p.tdt, p.ts, row);  // timesteps.to(float)
   int any_corrupt = 0;
   int64_t first_elig = LLONG_MAX;
-  for (int64_t k = threadIdx.x; k < p.tokens; k += kT) {
-    const bool el = load_truthy(p.edt, p.elig, base + k);
-    const float u = load_float(p.rdt, p.crand, base + k);
-    any_corrupt |= (u < t) && el;  // ops.cpp:326-328
-    if (el && k < first_elig) first_elig = k;
+  for (int64_t k0 = threadIdx.x; k0 < p.tokens; k0 += int64_t{kBT} * U) {
+    bool el[U];
+    float u[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t k = k0 + int64_t{j} * kBT;
+      el[j] = k < p.tokens && load_truthy(p.edt, p.elig, base + k);
+      u[j] = k < p.tokens ? load_float(p.rdt, p.crand, base + k) : 1.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      any_corrupt |= (u[j] < t) && el[j];  // ops.cpp:326-328
+      if (el[j] && first_elig == LLONG_MAX) first_elig = k0 + int64_t{j} * kBT;
+    }
   }
   any_corrupt = __syncthreads_or(any_corrupt);
 #pragma unroll
@@ -263,33 +293,49 @@ __global__ void __launch_bounds__(kT) display_corrupt_kernel(DisplayCorruptParam
   if ((threadIdx.x & 31) == 0) s_first[threadIdx.x >> 5] = first_elig;
   __syncthreads();
   int64_t fe = s_first[0];
-  for (int w = 1; w < kWarps; ++w) fe = min(fe, s_first[w]);
+#pragma unroll
+  for (int w = 1; w < kW; ++w) fe = min(fe, s_first[w]);
   // ops.cpp:330-337 first-eligible fallback
   const int64_t fallback = (!any_corrupt && t > 0.0f && fe != LLONG_MAX) ? fe : -1;
-  (void)s_any;
-  for (int64_t k = threadIdx.x; k < p.tokens; k += kT) {
-    const int64_t i = base + k;
-    const bool el = load_truthy(p.edt, p.elig, i);
-    const float u = load_float(p.rdt, p.crand, i);
-    const bool pos = ((u < t) && el) || k == fallback;
-    const int64_t id = p.ids[i];
-    bool rep = false;
-    int64_t value = id;
-    if (p.replace) {
-      rep = pos && (load_float(p.pdt, p.rrand, i) < p.repl_thr);  // ops.cpp:362-363
-      int64_t cand = floor_mod(id + p.roff[i], p.vocab);             // ops.cpp:364-365
-      for (int it = 0; it < 3; ++it) {                               // ops.cpp:366-376
-        const bool forbidden = cand == p.mask_id || cand == id || (p.has_eos && cand == p.eos_id);
-        if (forbidden) cand = floor_mod(cand + 1, p.vocab);
-      }
-      if (rep) value = cand;
+  for (int64_t k0 = threadIdx.x; k0 < p.tokens; k0 += int64_t{kBT} * U) {
+    bool el[U];
+    float u[U], rr[U];
+    int64_t id[U], off[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t k = k0 + int64_t{j} * kBT;
+      const bool in = k < p.tokens;
+      el[j] = in && load_truthy(p.edt, p.elig, base + k);
+      u[j] = in ? load_float(p.rdt, p.crand, base + k) : 1.0f;
+      id[j] = in ? p.ids[base + k] : 0;
+      rr[j] = in && p.replace ? load_float(p.pdt, p.rrand, base + k) : 1.0f;
+      off[j] = in && p.replace ? p.roff[base + k] : 0;
     }
-    const bool msk = pos && !rep;
-    if (msk) value = p.mask_id;
-    p.corrupted[i] = value;
-    p.labels[i] = pos ? id : -100;  // ops.cpp:386-389
-    p.masked[i] = msk;
-    p.replaced[i] = rep;
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t k = k0 + int64_t{j} * kBT;
+      if (k >= p.tokens) break;
+      const int64_t i = base + k;
+      const bool pos = ((u[j] < t) && el[j]) || k == fallback;
+      bool rep = false;
+      int64_t value = id[j];
+      if (p.replace) {
+        rep = pos && (rr[j] < p.repl_thr);  // ops.cpp:362-363
+        int64_t cand = wrap_vocab(id[j], off[j], p.vocab);
+        for (int it = 0; it < 3; ++it) {  // ops.cpp:366-376; cand stays in [0, vocab)
+          const bool forbidden =
+              cand == p.mask_id || cand == id[j] || (p.has_eos && cand == p.eos_id);
+          if (forbidden) cand = cand + 1 == p.vocab ? 0 : cand + 1;
+        }
+        if (rep) value = cand;
+      }
+      const bool msk = pos && !rep;
+      if (msk) value = p.mask_id;
+      p.corrupted[i] = value;
+      p.labels[i] = pos ? id[j] : -100;  // ops.cpp:386-389
+      p.masked[i] = msk;
+      p.replaced[i] = rep;
+    }
   }
 }
 
@@ -463,6 +509,14 @@ extern "C" int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype
                          vocab_size, has_eos, replace,
                          static_cast<float>(replacement_fraction), corrupted, labels, masked,
                          replaced};
-  display_corrupt_kernel<<<static_cast<unsigned>(batch), kT, 0, as_stream(stream)>>>(p);
+  // a row's tokens in one batch of loads where the row allows it
+  const unsigned grid = static_cast<unsigned>(batch);
+  cudaStream_t s = as_stream(stream);
+  if (tokens <= 256 * kCorruptBatch)
+    display_corrupt_kernel<256><<<grid, 256, 0, s>>>(p);
+  else if (tokens <= 512 * kCorruptBatch)
+    display_corrupt_kernel<512><<<grid, 512, 0, s>>>(p);
+  else
+    display_corrupt_kernel<1024><<<grid, 1024, 0, s>>>(p);
   return launch_result();
 }

@@ -774,7 +774,8 @@ int cid_oracle_display_corrupt(const int64_t* ids, int t_dtype,
       int64_t value = id;
       if (replace) {
         rep = pos && ((float)load(repl_dtype, replacement_random, i) < repl_thr);
-        int64_t cand = floor_mod(id + replacement_offsets[i], vocab); /* :364 */
+        /* :364, the int64 sum wrapping as ATen's add does */
+        int64_t cand = floor_mod((int64_t)((uint64_t)id + (uint64_t)replacement_offsets[i]), vocab);
         for (int it = 0; it < 3; ++it) {                            /* :366 */
           int forbidden = cand == mask_id || cand == id ||
                           (has_eos && cand == eos_id);

@@ -681,6 +681,27 @@ def display_corrupt_cases() -> Iterator[Case]:
         ro = torch.randint(-5, 2 * v, (b, t), generator=g) if frac > 0 else None
         eos = None if k % 5 == 0 else 1
         yield Case(f"dc/random_{k}", op, [ids, ts, el, torch.rand(b, t, generator=g), rr, ro, 0, eos, v, frac])
+    # long rows (one, two and three batches of loads per thread at each block
+    # size), vocabularies at and past 2^32, offsets at the int64 limits (the
+    # id + offset sum wraps as ATen's int64 add does)
+    top = torch.iinfo(torch.int64).max
+    shapes = ((3, 1025, 50257, 0.25), (2, 2049, 7, 1.0), (4, 5000, (1 << 33) + 7, 0.25),
+              (2, 9000, 1 << 32, 1.0), (2, 4097, (1 << 32) - 1, 0.5))
+    for k, (b, t, v, frac) in enumerate(shapes):
+        g = _g(9800 + k)
+        ids = torch.randint(0, min(v, 1 << 40), (b, t), generator=g)
+        ts = torch.rand(b, generator=g)
+        ts[0] = 0.0
+        el = torch.rand(b, t, generator=g) > 0.15
+        ro = torch.randint(-(1 << 62), 1 << 62, (b, t), generator=g)
+        ro[0, :64] = top - torch.arange(64)
+        ro[1, :64] = -top - 1 + torch.arange(64)
+        ro[1, 64:128] = torch.randint(-5, 2 * min(v, 1 << 40), (64,), generator=g)
+        yield Case(
+            f"dc/long_{k}", op,
+            [ids, ts, el, torch.rand(b, t, generator=g), torch.rand(b, t, generator=g), ro,
+             v - 1, None if k == 1 else 1, v, frac],
+        )
 
 
 def assignment_cases() -> Iterator[Case]:
