@@ -1,5 +1,6 @@
 // Training-corruption kernels (fwerkor/cid-engine v1.1.0 semantics):
-//  * masked diffusion (csrc/ops.cpp:394-444): one CTA per row, mask =
+//  * masked diffusion (csrc/ops.cpp:394-444): one CTA per row (256 to
+//    1024 threads, four tokens' loads in flight per thread), mask =
 //    u < ratio, empty-row fallback on argmin(u); the two metrics are summed
 //    by a second one-block kernel in a fixed order from per-row counts kept
 //    in a caller-provided workspace, so they are bit-identical run to run
@@ -47,10 +48,19 @@ __device__ __forceinline__ bool min_better(float v, int64_t i, float bv, int64_t
   return v < bv || (v == bv && i < bi);
 }
 
-__global__ void __launch_bounds__(kT) masked_diffusion_kernel(MaskedParams p) {
-  __shared__ int64_t s_cnt[kWarps];
-  __shared__ float s_min[kWarps];
-  __shared__ int64_t s_idx[kWarps];
+constexpr int kRowBatch = 4;  // tokens per thread whose loads are issued together
+
+// One CTA of kBT threads per row.  Each thread issues the loads of kRowBatch
+// tokens (kBT apart: every load instruction is coalesced) before it writes
+// any output, so a row costs one or two memory round trips, not one per
+// token a thread handles.
+template <int kBT>
+__global__ void __launch_bounds__(kBT) masked_diffusion_kernel(MaskedParams p) {
+  constexpr int kW = kBT / 32;
+  constexpr int U = kRowBatch;
+  __shared__ int64_t s_cnt[kW];
+  __shared__ float s_min[kW];
+  __shared__ int64_t s_idx[kW];
   const int64_t row = blockIdx.x;
   const int64_t base = row * p.tokens;
   // ratio = float32(float32(r * span) + lo) (ops.cpp:424-425)
@@ -58,15 +68,27 @@ __global__ void __launch_bounds__(kT) masked_diffusion_kernel(MaskedParams p) {
   int64_t cnt = 0;
   float bv = __int_as_float(0x7f800000);  // +inf
   int64_t bi = LLONG_MAX;
-  for (int64_t t = threadIdx.x; t < p.tokens; t += kT) {
-    const float u = p.mask_random[base + t];
-    const bool m = u < r;  // ops.cpp:426
-    p.masked[base + t] = m;
-    p.corrupted[base + t] = m ? p.mask_id : p.clean[base + t];
-    cnt += m;
-    if (bi == LLONG_MAX || min_better(u, t, bv, bi)) {
-      bv = u;
-      bi = t;
+  for (int64_t t0 = threadIdx.x; t0 < p.tokens; t0 += int64_t{kBT} * U) {
+    float u[U];
+    int64_t id[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t t = t0 + int64_t{j} * kBT;
+      u[j] = t < p.tokens ? p.mask_random[base + t] : 0.0f;
+      id[j] = t < p.tokens ? p.clean[base + t] : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t t = t0 + int64_t{j} * kBT;
+      if (t >= p.tokens) break;
+      const bool m = u[j] < r;  // ops.cpp:426
+      p.masked[base + t] = m;
+      p.corrupted[base + t] = m ? p.mask_id : id[j];
+      cnt += m;
+      if (bi == LLONG_MAX || min_better(u[j], t, bv, bi)) {
+        bv = u[j];
+        bi = t;
+      }
     }
   }
   // block reductions (count; NaN-first argmin)
@@ -91,7 +113,7 @@ __global__ void __launch_bounds__(kT) masked_diffusion_kernel(MaskedParams p) {
     int64_t total = 0;
     float mv = s_min[0];
     int64_t mi = s_idx[0];
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < kW; ++w) {
       total += s_cnt[w];
       if (s_idx[w] != LLONG_MAX && (mi == LLONG_MAX || min_better(s_min[w], s_idx[w], mv, mi))) {
         mv = s_min[w];
@@ -108,7 +130,18 @@ __global__ void __launch_bounds__(kT) masked_diffusion_kernel(MaskedParams p) {
   }
 }
 
-// metrics = [mean(masked), mean(ratio)] (ops.cpp:441-442), fixed-order sums.
+// Row kernel at the block size that covers a row in one batch of loads
+// where the row allows it.
+void launch_masked_rows(const MaskedParams& p, cudaStream_t s) {
+  const unsigned grid = static_cast<unsigned>(p.batch);
+  if (p.tokens <= 256 * kRowBatch)
+    masked_diffusion_kernel<256><<<grid, 256, 0, s>>>(p);
+  else if (p.tokens <= 512 * kRowBatch)
+    masked_diffusion_kernel<512><<<grid, 512, 0, s>>>(p);
+  else
+    masked_diffusion_kernel<1024><<<grid, 1024, 0, s>>>(p);
+}
+
 __global__ void __launch_bounds__(kT) masked_metrics_kernel(const int64_t* counts,
                                                             const float* ratio, int64_t batch,
                                                             int64_t tokens, float* metrics) {
@@ -376,7 +409,7 @@ extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const floa
   p.metrics = metrics;
   p.counts = static_cast<int64_t*>(workspace);
   cudaStream_t s = as_stream(stream);
-  masked_diffusion_kernel<<<static_cast<unsigned>(batch), kT, 0, s>>>(p);
+  launch_masked_rows(p, s);
   int rc = launch_result();
   if (rc != CID_OK) return rc;
   masked_metrics_kernel<<<1, kT, 0, s>>>(p.counts, ratio, batch, tokens, metrics);
@@ -459,7 +492,7 @@ extern "C" int cid_masked_diffusion_corrupt_no_alloc(
   p.metrics = metrics;
   p.counts = scratch;
   cudaStream_t s = as_stream(stream);
-  masked_diffusion_kernel<<<static_cast<unsigned>(batch), kT, 0, s>>>(p);
+  launch_masked_rows(p, s);
   rc = launch_result();
   if (rc != CID_OK) return rc;
   masked_metrics_kernel<<<1, kT, 0, s>>>(p.counts, ratio, batch, tokens, metrics);

@@ -586,6 +586,15 @@ def masked_diffusion_cases() -> Iterator[Case]:
         if k % 4 == 0:
             mr = (mr * 4).floor() / 4  # ties for the argmin fallback
         yield Case(f"md/random_{k}", op, [torch.randint(0, 500, (b, t), generator=g), rr, mr, 499, lo, hi])
+    # long rows (one to three batches of loads per thread at each block size);
+    # ratio-0 rows take the argmin fallback, quantised uniforms make it a tie
+    for k, (b, t) in enumerate(((3, 1025), (5, 4097), (2, 9000))):
+        g = _g(9050 + k)
+        rr = torch.rand(b, 1, generator=g)
+        rr[0] = 0.0
+        mr = torch.rand(b, t, generator=g)
+        mr[0] = (mr[0] * 64).floor() / 64
+        yield Case(f"md/long_{k}", op, [torch.randint(0, 50257, (b, t), generator=g), rr, mr, 50256, 1.0e-6, 1.0])
 
 
 def cfg3_masked_diffusion(seed: int = 2):
