@@ -349,6 +349,17 @@ __device__ __forceinline__ void to_float32(const Vec32& v, float* x) {
   VecTraits<T>::to_float(v.hi, x + VecTraits<T>::N);
 }
 
+// d[k] for a run-time k, by selects over the constant-index registers (a
+// run-time index into d would place the array in local memory).
+template <int U>
+__device__ __forceinline__ Vec32 pick(const Vec32 (&d)[U], int k) {
+  Vec32 r = d[0];
+#pragma unroll
+  for (int i = 1; i < U; ++i)
+    if (k == i) r = d[i];
+  return r;
+}
+
 // Streams this thread's share of one row: the unaligned head columns
 // [0, s_head_end), 32-byte vectors [v_beg, v_end) of the aligned region that
 // starts at column `head` (thread t takes v_beg + t, + stride, ...; U loads
@@ -364,6 +375,15 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
   for (int64_t c = tid; c < s_head_end; c += kStride) consume_scalar<kRep>(a, VT::scalar(row, c), c, pt);
 
   const Vec32* vrow = reinterpret_cast<const Vec32*>(row + head);
+  // repetition variant: the vectors (relative to `head`) holding the patched
+  // columns, -1 where none; only a chunk holding one takes the element-wise
+  // path below
+  int64_t pvec[2] = {-1, -1};
+  if (kRep) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+      if (q < pt.n && pt.col[q] >= head) pvec[q] = (pt.col[q] - head) / N;
+  }
   for (int64_t v = v_beg + tid; v < v_end; v += kStride * U) {
     Vec32 d[U];
 #pragma unroll
@@ -371,33 +391,45 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
       const int64_t vi = v + static_cast<int64_t>(k) * kStride;
       d[k] = vi < v_end ? load_vec32(vrow + vi) : neg_inf_vec32<T>();
     }
+    bool hit = false;
     if (kRep) {
-      // repetition variant: patched values take part in the maximum
-      float x[U][N];
-      float cm = -INFINITY;
 #pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int64_t dv = pvec[q] - v;
+        hit |= dv >= 0 && dv < int64_t{kStride} * U && dv % kStride == 0;
+      }
+    }
+    if (hit) {
+      // patched values take part in the maximum; two sweeps over the loaded
+      // vectors (maximum, then sums), one vector at a time, so this rare
+      // path adds few registers to the kernel
+      float cm = -INFINITY;
+#pragma unroll 1
       for (int k = 0; k < U; ++k) {
-        to_float32<T>(d[k], x[k]);
+        float x[N];
+        to_float32<T>(pick(d, k), x);
         const int64_t c0 = head + (v + static_cast<int64_t>(k) * kStride) * N;
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-          x[k][j] = patched(pt, c0 + j, x[k][j]);
-          cm = fmaxf(cm, x[k][j]);
-        }
+        for (int j = 0; j < N; ++j) cm = fmaxf(cm, patched(pt, c0 + j, x[j]));
       }
       const bool up = cm > a.m;
       a.m = up ? cm : a.m;
       a.where = up ? v : a.where;
       maybe_reoffset(a);
       const float noff = -a.off;
-#pragma unroll
-      for (int k = 0; k < U; ++k)
+#pragma unroll 1
+      for (int k = 0; k < U; ++k) {
+        float x[N];
+        to_float32<T>(pick(d, k), x);
+        const int64_t c0 = head + (v + static_cast<int64_t>(k) * kStride) * N;
 #pragma unroll
         for (int j = 0; j < N; j += 2) {
           float t0, t1;
-          fma2(t0, t1, x[k][j], x[k][j + 1], kLog2e, noff);
+          fma2(t0, t1, patched(pt, c0 + j, x[j]), patched(pt, c0 + j + 1, x[j + 1]), kLog2e,
+               noff);
           add2(a.s0, a.s1, ex2(t0), ex2(t1));
         }
+      }
       continue;
     }
     float cm = vmax32<T>(d[0]);

@@ -176,6 +176,35 @@ def test_repetition_long_runs() -> None:
     compare.assert_matches("display_token_statistics_with_repetition", got, exp, "long runs")
 
 
+@pytest.mark.parametrize("rows_per_seq,seqs", [(64, 2), (1000, 12)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_repetition_patch_moves_row_maximum(rows_per_seq, seqs, dtype) -> None:
+    """Every position's right neighbour holds that position's argmax column,
+    so the patch lowers the row maximum (the argmax moves, or ties with the
+    runner-up: the planted runner-up equals the patched maximum); 128 rows
+    run one CTA (cluster) per row, 12000 rows one warp per row."""
+    V = 4099  # odd: unaligned row starts, head and tail columns
+    g = torch.Generator().manual_seed(41)
+    lg = (torch.randn(seqs, rows_per_seq, V, generator=g) * 2).to(dtype).float()
+    top = lg.argmax(-1)
+    ids = torch.roll(top, 1, dims=1)  # ids[p + 1] = argmax of row p
+    ids[:, ::7] = 0  # mask ids (no patch from these)
+    mult = 0.5
+    # runner-up at a later column equal to the patched maximum on every third row
+    flat = lg.view(-1, V)
+    right = torch.roll(ids, -1, dims=1).view(-1)  # the right neighbour's id of each row
+    patched_max = flat.gather(1, top.view(-1, 1)).squeeze(1) + torch.log(torch.tensor(mult))
+    for r in range(0, flat.shape[0], 3):
+        if int(right[r]) == int(top.view(-1)[r]) and int(right[r]) > 1:
+            c = (int(top.view(-1)[r]) + 1 + r) % V
+            flat[r, c] = patched_max[r]
+    lg = lg.to(dtype)
+    got = torch.ops.cid_engine.display_token_statistics_with_repetition(ids.cuda(), lg.cuda(), 0, 1, mult)
+    exp = oracle.display_token_statistics_with_repetition(ids, lg, 0, 1, mult)
+    compare.assert_matches("display_token_statistics_with_repetition", got, exp,
+                           f"patch at maximum {rows_per_seq}x{seqs} {dtype}")
+
+
 def test_unaligned_and_strided_rows() -> None:
     """Row strides that break 16-byte alignment (odd vocab, sliced views)."""
     g = torch.Generator().manual_seed(5)
