@@ -266,20 +266,29 @@ __device__ int64_t run_length(const int64_t* seq, int64_t tokens, int64_t q, int
   }
 }
 
-// Computes the repetition patch for row `row` (warp 0 of the CTA).
+// Computes the repetition patch for row `row` (one whole warp).  Lanes 0-15
+// read the 16 positions left of the row's position, lanes 16-31 the 16 to
+// its right, in one round of loads; a run that fills its 16 lanes is
+// finished by the ballot scan.
 __device__ void repetition_patch(const StatsParams& p, int64_t row, Patch* out) {
   const int lane = threadIdx.x & 31;
   const int64_t pos = row % p.tokens;
   const int64_t* seq = p.ids + (row - pos);
+  const int my_dir = lane < 16 ? -1 : 1;
+  const int64_t at = pos + my_dir * (1 + (lane & 15));
+  const bool in = at >= 0 && at < p.tokens;
+  const int64_t v = in ? seq[at] : 0;
+  const unsigned full = 0xffffffffu;
   Patch pt;
   pt.n = 0;
   int64_t cnt[2] = {0, 0};
-  for (int side = 0; side < 2; ++side) {
+  for (int side = 0; side < 2; ++side) {  // left, then right (csrc/ops.cpp:505-533)
     const int dir = side == 0 ? -1 : 1;
     const int64_t q = pos + dir;
     if (q < 0 || q >= p.tokens) continue;
-    const int64_t tok = seq[q];
-    const int64_t n = 1 + run_length(seq, p.tokens, q + dir, dir, tok);
+    const int64_t tok = __shfl_sync(full, v, side * 16);  // seq[q]
+    const unsigned stop = (__ballot_sync(full, !in || v != tok) >> (side * 16)) & 0xffffu;
+    const int64_t n = stop ? __ffs(stop) - 1 : 16 + run_length(seq, p.tokens, q + 16 * dir, dir, tok);
     if (tok == p.mask_id || (p.has_eos && tok == p.eos_id)) continue;
     if (pt.n == 1 && pt.col[0] == tok) {
       cnt[0] += n;
@@ -579,8 +588,13 @@ __device__ void write_normal(const StatsParams& p, int64_t row, int64_t V, int64
   }
 }
 
+// Resident CTAs per SM asked of the register allocator: 0 (no request) for
+// the plain statistics, whose natural allocation already fits four CTAs; the
+// repetition variant is held to four (62 registers, no spills; measured 13 %
+// faster than its natural 74 on fp32 [1024, 32000]).  An explicit 1 would lift
+// the default cap and raise the plain kernels to 92-124 registers.
 template <typename T, bool kRep, Mode kMode, int U>
-__global__ void __launch_bounds__(kThreads) display_stats_kernel(StatsParams p) {
+__global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(StatsParams p) {
   using VT = VecTraits<T>;
   constexpr int N = 2 * VT::N;
   __shared__ Partial warp_parts[kThreads / 32];
@@ -679,8 +693,11 @@ __device__ __forceinline__ int64_t warp_min_i64(int64_t v) {
   return v;
 }
 
+// Plain statistics: no residency request (as above); the repetition
+// variant is held to seven 4-warp blocks per SM (72 registers; measured 6 %
+// faster than its natural 80 on bf16 [32768, 128256]).
 template <typename T, bool kRep, Mode kMode, int U>
-__global__ void __launch_bounds__(kRowWarps * 32) display_stats_rows_kernel(StatsParams p) {
+__global__ void __launch_bounds__(kRowWarps * 32, kRep ? 7 : 0) display_stats_rows_kernel(StatsParams p) {
   using VT = VecTraits<T>;
   constexpr int N = 2 * VT::N;
   __shared__ Patch patches[kRowWarps];
