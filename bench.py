@@ -915,6 +915,27 @@ def profile_case(name: str) -> None:
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": name, "mean_conf": float(c.mean())}))
         return
+    if name == "corruption":  # training corruption, two launches of each kernel
+        sys.path.insert(0, str(ROOT / "tests" / "golden"))
+        import cases
+
+        ops = torch.ops.cid_engine
+        md = [a.cuda() if isinstance(a, torch.Tensor) else a for a in cases.cfg3_masked_diffusion()]
+        gd = torch.Generator().manual_seed(11)
+        B3, T3, V3 = 64, 2048, 50257
+        dc = [torch.randint(0, V3, (B3, T3), generator=gd), torch.rand(B3, generator=gd),
+              torch.rand(B3, T3, generator=gd) > 0.15, torch.rand(B3, T3, generator=gd),
+              torch.rand(B3, T3, generator=gd), torch.randint(1, V3, (B3, T3), generator=gd)]
+        dc = [t.cuda() for t in dc]
+        th = [t.cuda() for t in cases.cfg1_thought()]
+        for _ in range(2):
+            m = ops.masked_diffusion_corrupt_from_random(*md)
+            d = ops.display_corrupt_from_random(*dc, V3 - 1, EOS_ID, V3, 0.25)
+            t = ops.thought_corrupt_from_epsilon(*th)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "masked": int(m[1].sum()),
+                          "replaced": int(d[3].sum()), "thought": float(t[0].sum())}))
+        return
     shape = {"cta": (1, 4096, 128256), "rows": (1, 10240, 128256)}[name]
     g = torch.Generator(device="cuda").manual_seed(1)
     lg = torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) * 2
@@ -940,7 +961,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-min-reps", type=int, default=3)
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
-    ap.add_argument("--profile-case", choices=("cta", "rows", "lm_head", "refine"), default=None,
+    ap.add_argument("--profile-case", choices=("cta", "rows", "lm_head", "refine", "corruption"), default=None,
                     help="run a small statistics case for ncu and exit")
     ap.add_argument("--sample-b", type=int, default=1)
     ap.add_argument("--sample-l", type=int, default=1024)
