@@ -30,8 +30,21 @@ struct AssignParams {
   uint32_t* status;
 };
 
+// Unsigned key whose order is the order of doubles (no NaN): -0 and +0 give
+// the same key, as they compare equal.
+__device__ __forceinline__ unsigned long long order_key(double x) {
+  long long b = __double_as_longlong(x);
+  if (b == static_cast<long long>(0x8000000000000000ull)) b = 0;  // -0 -> +0
+  return b >= 0 ? static_cast<unsigned long long>(b) ^ 0x8000000000000000ull
+                : ~static_cast<unsigned long long>(b);
+}
+
 __global__ void assignment_kernel(AssignParams p) {
   __shared__ double u_all[kWarpsPerBlock][kMaxColumns + 1];
+  // the batch element's active rows of costs, as float32 (one coalesced
+  // read; the column search then reads shared memory, not one dependent
+  // global load per step)
+  __shared__ float c_all[kWarpsPerBlock][kMaxColumns * kMaxColumns];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + warp;
   if (b >= p.batch) return;  // uniform per warp
@@ -46,12 +59,15 @@ __global__ void assignment_kernel(AssignParams p) {
     return;
   }
   if (lane <= kMaxColumns) u[lane] = 0.0;
+  float* cost = c_all[warp];
+  const int64_t base = b * rows * m;
+  for (int64_t e = lane; e < active * m; e += 32)
+    cost[e] = load_float(p.dtype, p.costs, base + e);
   __syncwarp();
   const bool col = lane >= 1 && lane <= m;  // a real column
   double v = 0.0;                           // potential of column `lane`
   int pj = 0;                               // row matched to column `lane` (0 = none)
   int way = 0;
-  const int64_t base = b * rows * m;
   bool ok = true;
   for (int row = 1; row <= active && ok; ++row) {
     if (lane == 0) pj = row;
@@ -64,8 +80,7 @@ __global__ void assignment_kernel(AssignParams p) {
       const int i0 = __shfl_sync(0xffffffffu, pj, j0);
       // reduced costs of the unused columns, in double: (c - u[i0]) - v[j]
       if (col && !used) {
-        const double c = static_cast<double>(
-            load_float(p.dtype, p.costs, base + static_cast<int64_t>(i0 - 1) * m + (lane - 1)));
+        const double c = static_cast<double>(cost[(i0 - 1) * m + (lane - 1)]);
         const double cur = __dsub_rn(__dsub_rn(c, u[i0]), v);
         if (cur < minv) {
           minv = cur;
@@ -73,20 +88,19 @@ __global__ void assignment_kernel(AssignParams p) {
         }
       }
       // delta = smallest slack among unused columns, lowest column on ties;
-      // only values below +inf can be chosen (the reference's strict `<`)
-      double dv = (col && !used && minv < INFINITY) ? minv : INFINITY;
-      int dj = (col && !used && minv < INFINITY) ? lane : 0;
-#pragma unroll
-      for (int d = 16; d > 0; d >>= 1) {
-        const double ov = __shfl_xor_sync(0xffffffffu, dv, d);
-        const int oj = __shfl_xor_sync(0xffffffffu, dj, d);
-        if (oj != 0 && (dj == 0 || ov < dv || (ov == dv && oj < dj))) {
-          dv = ov;
-          dj = oj;
-        }
-      }
-      const double delta = dv;
-      const int j1 = dj;
+      // only values below +inf can be chosen (the reference's strict `<`):
+      // three warp min-reductions over the slack's order key (high word, low
+      // word, then the lane among equal keys), the winner's slack by shuffle
+      const bool cand = col && !used && minv < INFINITY;
+      const unsigned long long key = cand ? order_key(minv) : ~0ull;
+      const unsigned khi = static_cast<unsigned>(key >> 32), klo = static_cast<unsigned>(key);
+      const unsigned hi = __reduce_min_sync(0xffffffffu, khi);
+      const unsigned lo = __reduce_min_sync(0xffffffffu, khi == hi ? klo : 0xffffffffu);
+      const unsigned wl =
+          __reduce_min_sync(0xffffffffu, cand && khi == hi && klo == lo ? unsigned(lane) : 32u);
+      const double win = __shfl_sync(0xffffffffu, minv, wl & 31u);
+      const double delta = wl < 32u ? win : INFINITY;
+      const int j1 = wl < 32u ? static_cast<int>(wl) : 0;
       // potentials: u[p[j]] += delta, v[j] -= delta for used columns (each
       // used column holds a distinct row); slack -= delta for the others
       if (lane <= m) {
