@@ -1,6 +1,7 @@
 // Batched linear assignment (Hungarian method with potentials) for at most 16
 // columns: one warp per batch element, lane j owning column j (lane 0 is the
-// method's virtual column 0).  Semantics of the reference
+// method's virtual column 0) with the column's potential, its matched row and
+// that row's potential, all in registers.  Semantics of the reference
 // (csrc/ops.cpp:68-175 of fwerkor/cid-engine v1.1.0): costs are read as
 // float32 and every reduced cost, potential and slack is computed in double
 // with the same operations in the same order, so the assignment is
@@ -40,7 +41,6 @@ __device__ __forceinline__ unsigned long long order_key(double x) {
 }
 
 __global__ void assignment_kernel(AssignParams p) {
-  __shared__ double u_all[kWarpsPerBlock][kMaxColumns + 1];
   // the batch element's active rows of costs, as float32 (one coalesced
   // read; the column search then reads shared memory, not one dependent
   // global load per step)
@@ -48,7 +48,6 @@ __global__ void assignment_kernel(AssignParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + warp;
   if (b >= p.batch) return;  // uniform per warp
-  double* u = u_all[warp];
   const int m = static_cast<int>(p.columns);
   const int64_t rows = p.rows;
   for (int64_t r = lane; r < rows; r += 32) p.out[b * rows + r] = -1;
@@ -58,7 +57,6 @@ __global__ void assignment_kernel(AssignParams p) {
     if (lane == 0 && p.status) atomicOr(p.status, CID_STATUS_ASSIGNMENT_INVALID);
     return;
   }
-  if (lane <= kMaxColumns) u[lane] = 0.0;
   float* cost = c_all[warp];
   const int64_t base = b * rows * m;
   for (int64_t e = lane; e < active * m; e += 32)
@@ -67,10 +65,14 @@ __global__ void assignment_kernel(AssignParams p) {
   const bool col = lane >= 1 && lane <= m;  // a real column
   double v = 0.0;                           // potential of column `lane`
   int pj = 0;                               // row matched to column `lane` (0 = none)
+  double uj = 0.0;                          // potential of row `pj` (moves with the row)
   int way = 0;
   bool ok = true;
   for (int row = 1; row <= active && ok; ++row) {
-    if (lane == 0) pj = row;
+    if (lane == 0) {
+      pj = row;
+      uj = 0.0;  // a row's potential is 0 until its own search starts
+    }
     int j0 = 0;
     double minv = INFINITY;
     bool used = false;
@@ -78,10 +80,11 @@ __global__ void assignment_kernel(AssignParams p) {
     for (;;) {
       if (lane == j0) used = true;
       const int i0 = __shfl_sync(0xffffffffu, pj, j0);
+      const double ui0 = __shfl_sync(0xffffffffu, uj, j0);  // u[i0]
       // reduced costs of the unused columns, in double: (c - u[i0]) - v[j]
       if (col && !used) {
         const double c = static_cast<double>(cost[(i0 - 1) * m + (lane - 1)]);
-        const double cur = __dsub_rn(__dsub_rn(c, u[i0]), v);
+        const double cur = __dsub_rn(__dsub_rn(c, ui0), v);
         if (cur < minv) {
           minv = cur;
           way = j0;
@@ -105,13 +108,12 @@ __global__ void assignment_kernel(AssignParams p) {
       // used column holds a distinct row); slack -= delta for the others
       if (lane <= m) {
         if (used) {
-          u[pj] = __dadd_rn(u[pj], delta);
+          uj = __dadd_rn(uj, delta);
           v = __dsub_rn(v, delta);
         } else {
           minv = __dsub_rn(minv, delta);
         }
       }
-      __syncwarp();
       j0 = j1;
       const int pj0 = __shfl_sync(0xffffffffu, pj, j0);
       if (pj0 == 0) break;
@@ -125,7 +127,11 @@ __global__ void assignment_kernel(AssignParams p) {
     for (int k = 0; k <= m + 1; ++k) {
       const int j1 = __shfl_sync(0xffffffffu, way, j0);
       const int pnew = __shfl_sync(0xffffffffu, pj, j1);
-      if (lane == j0) pj = pnew;
+      const double unew = __shfl_sync(0xffffffffu, uj, j1);
+      if (lane == j0) {
+        pj = pnew;
+        uj = unew;
+      }
       j0 = j1;
       if (j0 == 0) break;
     }
