@@ -47,6 +47,8 @@ sys.path.insert(0, str(ROOT))
 
 MASK_ID, EOS_ID = 0, 1
 REVEAL, REVISION, MARGIN = 0.25, 0.1, 0.05
+# the headline metric, the same in every arm (B200 at N=1 and N>1, reference)
+METRIC = "display logits GB/s (display_token_statistics + refine_display_from_statistics step)"
 CFG2 = dict(B=32, L=1024, V=128256)
 CFG4 = dict(B=64, L=4096, V=152064)
 CFG5 = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64)
@@ -310,7 +312,7 @@ def bench_single(args) -> dict:
     lm_head = None if args.no_loop else bench_lm_head(dev)
     cpu = None if args.no_cpu_baseline else run_cpu_baseline(seconds=args.cpu_seconds)
     line = {
-        "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
+        "metric": METRIC,
         "value": round(value, 2),
         "unit": "GB/s",
         "n_gpus": 1,
@@ -662,7 +664,7 @@ def bench_reference(args, world: int = 1) -> dict:
         scaling = "weak"
     val = res.get("value") if res else None
     return {
-        "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
+        "metric": METRIC,
         "value": None if val is None else round(val, 3),
         "unit": "GB/s",
         "impl": "reference",
@@ -842,7 +844,7 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
         alg = shard_bytes + rows * (8 + 16)
         achieved = alg / (kern_ms * 1e-3) / 1e9
         line = {
-            "metric": "display logits GB/s (display_token_statistics + refine_display_from_statistics step)",
+            "metric": METRIC,
             "value": round(total_bytes / (ms * 1e-3) / 1e9, 2),
             "unit": "GB/s",
             "n_gpus": world,
