@@ -176,14 +176,15 @@ def test_repetition_long_runs() -> None:
     compare.assert_matches("display_token_statistics_with_repetition", got, exp, "long runs")
 
 
-@pytest.mark.parametrize("rows_per_seq,seqs", [(64, 2), (1000, 12)])
+@pytest.mark.parametrize("rows_per_seq,seqs,V", [(64, 2, 4099), (1000, 12, 4099), (8, 2, 152063)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_repetition_patch_moves_row_maximum(rows_per_seq, seqs, dtype) -> None:
+def test_repetition_patch_moves_row_maximum(rows_per_seq, seqs, V, dtype) -> None:
     """Every position's right neighbour holds that position's argmax column,
     so the patch lowers the row maximum (the argmax moves, or ties with the
     runner-up: the planted runner-up equals the patched maximum); 128 rows
-    run one CTA (cluster) per row, 12000 rows one warp per row."""
-    V = 4099  # odd: unaligned row starts, head and tail columns
+    run one CTA per row, 12000 rows one warp per row, 16 rows of 152063 a
+    cluster of CTAs per row (each CTA streams a slice of the row).  Odd
+    vocabularies: unaligned row starts, head and tail columns."""
     g = torch.Generator().manual_seed(41)
     lg = (torch.randn(seqs, rows_per_seq, V, generator=g) * 2).to(dtype).float()
     top = lg.argmax(-1)
