@@ -244,6 +244,30 @@ struct Candidate {
 
 // Strict order of refine.cpp:30-43 extended by `kind` so that, for one
 // start, an equal deletion does not displace the insertion found before it.
+// Length of the run i = 0, 1, ... with a[x0 + i] == b[y0 + i], x0 + i < xlim
+// and y0 + i < ylim.  Eight positions' loads are issued before any compare
+// and the first mismatch is found with one bit scan, so a run of n costs
+// n / 8 dependent round trips (anchors on a shifted prediction run to the
+// end of the row).
+__device__ __forceinline__ int64_t match_run(const int64_t* a, int64_t x0, int64_t xlim,
+                                             const int64_t* b, int64_t y0, int64_t ylim) {
+  const int64_t n = imin(xlim - x0, ylim - y0);
+  if (n <= 0) return 0;
+  for (int64_t run = 0;; run += 8) {
+    int64_t av[8], bv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool in = run + j < n;
+      av[j] = in ? a[x0 + run + j] : 0;
+      bv[j] = in ? b[y0 + run + j] : 1;  // past the end: a mismatch
+    }
+    unsigned miss = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) miss |= static_cast<unsigned>(av[j] != bv[j]) << j;
+    if (miss) return run + (__ffs(miss) - 1);
+  }
+}
+
 __device__ __forceinline__ bool cand_better(const Candidate& a, const Candidate& b) {
   if (!b.valid) return a.valid;
   if (!a.valid) return false;
@@ -396,9 +420,7 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
         bool ok = true;  // pred[s, q) must hold neither mask nor EOS
         for (int64_t k = s; k < q_hit && ok; ++k) ok = pred[k] != mask && pred[k] != eos;
         if (ok) {
-          int64_t anchor = 0;
-          while (q_hit + anchor < L && s + anchor < alen && pred[q_hit + anchor] == tok[s + anchor])
-            ++anchor;
+          const int64_t anchor = match_run(pred, q_hit, L, tok, s, alen);
           const int64_t growth = q_hit - s;
           if (anchor >= 2 && static_cast<double>(gs) >= p.margin && eos_pos + 1 + growth <= L) {
             const Candidate c{anchor, gs, -growth, s, 1, 0, growth, 1};
@@ -407,9 +429,7 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
         }
       }
       if (r_hit >= 0) {
-        int64_t anchor = 0;
-        while (s + anchor < L && r_hit + anchor < alen && pred[s + anchor] == tok[r_hit + anchor])
-          ++anchor;
+        const int64_t anchor = match_run(pred, s, L, tok, r_hit, alen);
         const int64_t del = r_hit - s;
         if (anchor >= 2 && static_cast<double>(gs) >= p.margin && eos_pos + 1 - del <= L) {
           const Candidate c{anchor, gs, -del, s, 0, del, 0, 1};
