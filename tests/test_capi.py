@@ -111,6 +111,63 @@ def test_host_validation_rejects_without_a_device(lib: ctypes.CDLL) -> None:
     assert lib.cid_masked_diffusion_workspace_bytes(i64(64)) == 64 * 8
 
 
+def test_host_validation_of_the_other_entry_points(lib: ctypes.CDLL) -> None:
+    """Display corruption, linear assignment, thought corruption and the LM
+    head reject invalid arguments before any CUDA call.  The LM-head checks
+    never dereference their pointers, so 16-byte-aligned stand-in addresses
+    are enough here."""
+    null = ctypes.c_void_p(0)
+    i64, dbl, c_int = ctypes.c_int64, ctypes.c_double, ctypes.c_int
+    F32, I64 = 0, 5
+
+    def display_corrupt(t_dtype, vocab, frac, rr=null, ro=null):
+        return lib.cid_display_corrupt(null, t_dtype, null, 4, null, F32, null, F32, rr, ro,
+                                       i64(2), i64(8), i64(0), c_int(1), i64(1), i64(vocab),
+                                       dbl(frac), null, null, null, null, null)
+
+    # replacement_fraction outside [0, 1] (csrc/ops.cpp:320-322)
+    assert display_corrupt(F32, 100, 1.5) == CID_ERR_INVALID_ARGUMENT
+    # replacement needs vocab >= 3 and both random tensors (csrc/ops.cpp:343-348)
+    assert display_corrupt(F32, 2, 0.25, ctypes.c_void_p(16), ctypes.c_void_p(16)) == CID_ERR_INVALID_ARGUMENT
+    assert display_corrupt(F32, 100, 0.25) == CID_ERR_INVALID_ARGUMENT
+    # integer timesteps are not a floating dtype (csrc/ops.cpp:317-319)
+    assert display_corrupt(I64, 100, 0.0) == CID_ERR_UNSUPPORTED_DTYPE
+
+    # linear assignment: at most 16 columns, rows <= columns (csrc/ops.cpp:71-86)
+    def assign(dtype, rows, cols):
+        return lib.cid_batched_linear_assignment(dtype, null, null, i64(1), i64(rows),
+                                                 i64(cols), null, null, null)
+
+    assert assign(F32, 4, 17) == CID_ERR_INVALID_ARGUMENT
+    assert assign(F32, 5, 4) == CID_ERR_INVALID_ARGUMENT
+    assert assign(I64, 4, 4) == CID_ERR_UNSUPPORTED_DTYPE
+    assert assign(F32, 0, 4) == CID_OK  # nothing to assign: no launch
+
+    # thought corruption: semantic and timesteps must be floating
+    rc = lib.cid_thought_corrupt(I64, null, F32, null, F32, null, null, i64(1), i64(8),
+                                 null, null, null, null)
+    assert rc == CID_ERR_UNSUPPORTED_DTYPE
+    rc = lib.cid_thought_corrupt(F32, null, F32, null, F32, null, null, i64(-1), i64(8),
+                                 null, null, null, null)
+    assert rc == CID_ERR_INVALID_ARGUMENT
+
+    # LM head: hidden width a multiple of 8 (16-byte TMA rows), 16-byte-aligned
+    # operands, a workspace of cid_lm_head_workspace_bytes
+    lib.cid_lm_head_workspace_bytes.restype = ctypes.c_size_t
+    ws_need = lib.cid_lm_head_workspace_bytes(i64(4), i64(300))
+    assert ws_need > 0
+
+    def lm_head(hidden_dim, hidden_addr, ws_bytes):
+        p = ctypes.c_void_p
+        return lib.cid_lm_head_display_statistics(
+            p(hidden_addr), i64(4), i64(hidden_dim), p(0x2000), i64(300), p(0x3000), c_int(1),
+            p(0x4000), p(0x5000), p(0x6000), p(0x7000), ctypes.c_size_t(ws_bytes), null, null)
+
+    assert lm_head(12, 0x1000, ws_need) == CID_ERR_INVALID_ARGUMENT
+    assert lm_head(64, 0x1008, ws_need) == CID_ERR_INVALID_ARGUMENT
+    assert lm_head(64, 0x1000, ws_need - 1) == 6  # CID_ERR_SCRATCH_LIMIT
+
+
 def test_peer_inbox_layout_sizes() -> None:
     """Inbox bytes: records [2][world][capacity] x 16 B + a 256-byte tail."""
     import ctypes
