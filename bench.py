@@ -19,7 +19,7 @@ no host sync (the "fused display-stats + refine step").
   CUDA-event duration, against the measured HBM copy bandwidth.
 * ``cpu_baseline`` = the reference's own CPU backend (built from its sources
   into oracle/_ref) on a bounded sample, in a separate process.
-* ``refine_loop`` = config-5 decode loop: B=256, L=512, V=32000 bf16, 128
+* ``refine_loop`` = decode loop: B=256, L=512, V=32000 bf16, 128
   slots, stats -> refine -> rollout -> live occupancy -> snapshot per step,
   64 steps, steps/s.
 
@@ -49,11 +49,14 @@ MASK_ID, EOS_ID = 0, 1
 REVEAL, REVISION, MARGIN = 0.25, 0.1, 0.05
 # the headline metric, the same in every arm (B200 at N=1 and N>1, reference)
 METRIC = "display logits GB/s (display_token_statistics + refine_display_from_statistics step)"
-CFG2 = dict(B=32, L=1024, V=128256)
-CFG4 = dict(B=64, L=4096, V=152064)
-CFG5 = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64)
+# display step at N=1: logits bf16 [32, 1024, 128256]
+STEP = dict(B=32, L=1024, V=128256)
+# vocabulary-parallel step at N>1: logits bf16 [64, 4096, 152064] sharded by columns
+SHARDED = dict(B=64, L=4096, V=152064)
+# decode loop: 256 sequences of 512 over 32000 tokens, 128 thought slots, 64 steps
+LOOP = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64)
 # DRAM bytes (read + write) per row of the statistics kernel that serves the
-# config-2 shape (warp per row), measured by ncu (dram__bytes_read.sum +
+# [32, 1024, 128256] step (warp per row), measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on a [1, 10240, 128256] bf16 launch and divided by
 # its 10240 rows; traffic grows in proportion to rows.
 NCU_TRAFFIC_PER_ROW = (2_631_003_000 + 4_521_216) / 10240
@@ -271,7 +274,7 @@ def bench_single(args) -> dict:
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    B, L, V = CFG2["B"], CFG2["L"], CFG2["V"]
+    B, L, V = STEP["B"], STEP["L"], STEP["V"]
     ids, logits = display_inputs(B, L, V, seed=1, device=dev)
     stream = torch.cuda.current_stream()
     ops = torch.ops.cid_engine
@@ -308,7 +311,7 @@ def bench_single(args) -> dict:
     torch.cuda.empty_cache()
 
     loop = None if args.no_loop else bench_refine_loop(dev)
-    small = None if args.no_loop else bench_small_configs(dev)
+    small = None if args.no_loop else bench_small_workloads(dev)
     lm_head = None if args.no_loop else bench_lm_head(dev)
     cpu = None if args.no_cpu_baseline else run_cpu_baseline(seconds=args.cpu_seconds)
     line = {
@@ -337,7 +340,7 @@ def bench_single(args) -> dict:
         "clocks": clocks,
         "cpu_baseline": cpu,
         "refine_loop": loop,
-        "small_configs": small,
+        "small_workloads": small,
         "lm_head": lm_head,
     }
     return line
@@ -392,13 +395,14 @@ def bench_e2e(ids_dev: Tensor, logits_dev: Tensor, *, steps: int, warmup: int, m
 
 
 def bench_refine_loop(dev) -> dict:
-    """Config 5: 64 consecutive steps of the fused chain, no host sync."""
+    """Decode loop (B=256, L=512, V=32000, 128 slots): 64 consecutive steps
+    of the fused chain, no host sync."""
     import torch
 
     from cid_engine.loop import DisplayRefineLoop
     from cid_engine.step import SlotInputs
 
-    c = CFG5
+    c = LOOP
     B, L, V, S = c["B"], c["L"], c["V"], c["S"]
     ring = []
     for k in range(3):  # ring of pre-generated logits (each 8.4 GB > L2)
@@ -487,11 +491,12 @@ def _graph_time_ms(fn, reps: int) -> float:
     return a.elapsed_time(b) / reps
 
 
-def bench_small_configs(dev) -> dict:
-    """Config 1 (fp32 [4,256,32000] chain: statistics, refinement, rollout
-    and live occupancy of 32 slots, thought corruption [4,32,512]) and
-    config 3 (masked diffusion [64,2048]); both are launch-bound, so each is
-    timed as CUDA-graph replays (inputs rotate over 8 copies for config 1,
+def bench_small_workloads(dev) -> dict:
+    """The small workloads: the fp32 [4,256,32000] chain (statistics,
+    refinement, rollout and live occupancy of 32 slots, thought corruption
+    [4,32,512]), masked diffusion [64,2048], repetition statistics, display
+    corruption and linear assignment; all launch-bound, so each is timed as
+    CUDA-graph replays (the [4,256,32000] logits rotate over 8 copies,
     1 GB > L2)."""
     import torch
 
@@ -499,7 +504,7 @@ def bench_small_configs(dev) -> dict:
     import cases
 
     ops = torch.ops.cid_engine
-    ids, logits = cases.cfg1_display()
+    ids, logits = cases.display_f32_4x256x32000()
     ids, logits = ids.to(dev), logits.to(dev)
     copies = [logits] + [logits.clone() for _ in range(7)]
     g = torch.Generator().manual_seed(10)
@@ -509,10 +514,10 @@ def bench_small_configs(dev) -> dict:
     life = life.to(dev)
     al = torch.randn(4, 32, generator=g).to(dev)
     rv = torch.randn(4, 32, 3, generator=g).to(dev)
-    th = [t.to(dev) for t in cases.cfg1_thought()]
+    th = [t.to(dev) for t in cases.thought_4x32x512()]
     state = {"k": 0}
 
-    def cfg1_step():
+    def chain_step():
         lg = copies[state["k"] % len(copies)]
         state["k"] += 1
         c, p, u = ops.display_token_statistics(ids, lg)
@@ -521,13 +526,13 @@ def bench_small_configs(dev) -> dict:
         ops.live_slot_occupancy(occ, life, 3)
         ops.thought_corrupt_from_epsilon(*th)
 
-    ms1 = _graph_time_ms(cfg1_step, 64)
-    md = [a.to(dev) if isinstance(a, torch.Tensor) else a for a in cases.cfg3_masked_diffusion()]
+    ms1 = _graph_time_ms(chain_step, 64)
+    md = [a.to(dev) if isinstance(a, torch.Tensor) else a for a in cases.masked_diffusion_64x2048()]
 
-    def cfg3_call():
+    def md_call():
         ops.masked_diffusion_corrupt_from_random(*md)
 
-    ms3 = _graph_time_ms(cfg3_call, 1000)
+    ms3 = _graph_time_ms(md_call, 1000)
 
     def rep_step():
         lg = copies[state["k"] % len(copies)]
@@ -563,15 +568,15 @@ def bench_small_configs(dev) -> dict:
     del copies
     torch.cuda.empty_cache()
     return {
-        "cfg1_chain": {"workload": "fp32 [4,256,32000] stats+refine, 32 slots rollout+live, "
+        "chain_f32_4x256x32000": {"workload": "fp32 [4,256,32000] stats+refine, 32 slots rollout+live, "
                                    "thought [4,32,512]", "us_per_step": round(ms1 * 1e3, 2),
                        "logits_GBps": round(131_072_000 / (ms1 * 1e-3) / 1e9, 1),
                        "launches_per_step": 5, "timing": "CUDA graph, 64 steps"},
-        "cfg3_masked_diffusion": {"workload": "ids [64,2048], mask id 50256",
+        "masked_diffusion_64x2048": {"workload": "ids [64,2048], mask id 50256",
                                   "us_per_call": round(ms3 * 1e3, 3),
                                   "GBps": round(2_753_032 / (ms3 * 1e-3) / 1e9, 1),
                                   "launches_per_call": 2, "timing": "CUDA graph, 1000 calls"},
-        "cfg1_repetition_stats": {"workload": "fp32 [4,256,32000], mask 0, eos 1, multiplier 0.7",
+        "repetition_stats_f32_4x256x32000": {"workload": "fp32 [4,256,32000], mask 0, eos 1, multiplier 0.7",
                                   "us_per_call": round(ms_rep * 1e3, 2),
                                   "logits_GBps": round(131_072_000 / (ms_rep * 1e-3) / 1e9, 1),
                                   "timing": "CUDA graph, 64 calls, 8 rotating inputs"},
@@ -588,16 +593,17 @@ def bench_small_configs(dev) -> dict:
 
 
 def bench_lm_head(dev) -> dict:
-    """LM head fused with the display statistics on the config-2 rows:
-    hidden bf16 [32*1024, 4096] x weight bf16 [128256, 4096] (the display
-    logits of config 2 produced by a 4096-wide LM head), statistics of the
+    """LM head fused with the display statistics on the display step's rows:
+    hidden bf16 [32*1024, 4096] x weight bf16 [128256, 4096] (the
+    [32, 1024, 128256] display logits produced by a 4096-wide LM head),
+    statistics of the
     bf16-rounded logits; against cuBLAS writing the bf16 logits and the
     statistics kernel reading them back, timed in the same run."""
     import torch
 
     import cid_engine
 
-    R, H, V = CFG2["B"] * CFG2["L"], 4096, CFG2["V"]
+    R, H, V = STEP["B"] * STEP["L"], 4096, STEP["V"]
     g = torch.Generator(device=dev).manual_seed(5)
     h = (torch.randn(R, H, generator=g, device=dev) * 0.05).to(torch.bfloat16)
     w = (torch.randn(V, H, generator=g, device=dev) * 0.05).to(torch.bfloat16)
@@ -649,16 +655,17 @@ def bench_lm_head(dev) -> dict:
 
 def bench_reference(args, world: int = 1) -> dict:
     """Reference CPU backend on the host cores, on the B200 arm's workload,
-    metric and unit: config 2 at N=1, the vocabulary-parallel config 4 under
+    metric and unit: logits [32, 1024, 128256] at N=1, the vocabulary-parallel
+    [64, 4096, 152064] under
     torchrun (rank 0 only; a CPU sample of one sequence's rows over the full
     vocabulary stands for it)."""
     if world > 1:
-        B, L, V = CFG4["B"], CFG4["L"], CFG4["V"]
+        B, L, V = SHARDED["B"], SHARDED["L"], SHARDED["V"]
         res = run_cpu_baseline(sample=(1, 512, V), seconds=args.cpu_seconds)
         workload = "vocab-parallel display stats + refine, logits bf16 [64,4096,152064]"
         scaling = "strong"
     else:
-        B, L, V = CFG2["B"], CFG2["L"], CFG2["V"]
+        B, L, V = STEP["B"], STEP["L"], STEP["V"]
         res = run_cpu_baseline(seconds=args.cpu_seconds)
         workload = "display stats + refine, logits bf16 [32,1024,128256]"
         scaling = "weak"
@@ -686,12 +693,12 @@ def bench_reference(args, world: int = 1) -> dict:
 
 
 # ---------------------------------------------------------------------------
-# multi-GPU arm (torchrun, N>1): vocabulary-parallel config 4
+# multi-GPU arm (torchrun, N>1): vocabulary-parallel [64, 4096, 152064]
 # ---------------------------------------------------------------------------
 
 
 def sharded_display_inputs(B, L, V, rank, world, seed, device):
-    """This rank's vocabulary shard of the config-4 logits: bf16(2 N(0,1))
+    """This rank's vocabulary shard of the [64, 4096, 152064] logits: bf16(2 N(0,1))
     with a +8 peak in 5% of rows at a column drawn once for all ranks."""
     import torch
     from cid_engine.parallel import shard_offsets
@@ -884,14 +891,13 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
 
 
 def profile_case(name: str) -> None:
-    """Small launches for ncu: three statistics launches on the config-2 row
-    shape, large enough to leave L2 (CTA-per-row kernel: [1, 4096, 128256]
+    """Small launches for ncu: three statistics launches on rows of 128256, large enough to leave L2 (CTA-per-row kernel: [1, 4096, 128256]
     bf16, 1.05 GB; warp-per-row kernel: [1, 10240, 128256] bf16, 2.6 GB)."""
     import torch
 
     import cid_engine
 
-    if name == "refine":  # refinement alone on config-2 and config-4 row shapes
+    if name == "refine":  # refinement alone on rows [32, 1024] and [64, 4096]
         g = torch.Generator(device="cuda").manual_seed(1)
         for B, L in ((32, 1024), (64, 4096)):
             ids = torch.randint(2, 32000, (B, L), generator=g, device="cuda")
@@ -922,14 +928,14 @@ def profile_case(name: str) -> None:
         import cases
 
         ops = torch.ops.cid_engine
-        md = [a.cuda() if isinstance(a, torch.Tensor) else a for a in cases.cfg3_masked_diffusion()]
+        md = [a.cuda() if isinstance(a, torch.Tensor) else a for a in cases.masked_diffusion_64x2048()]
         gd = torch.Generator().manual_seed(11)
         B3, T3, V3 = 64, 2048, 50257
         dc = [torch.randint(0, V3, (B3, T3), generator=gd), torch.rand(B3, generator=gd),
               torch.rand(B3, T3, generator=gd) > 0.15, torch.rand(B3, T3, generator=gd),
               torch.rand(B3, T3, generator=gd), torch.randint(1, V3, (B3, T3), generator=gd)]
         dc = [t.cuda() for t in dc]
-        th = [t.cuda() for t in cases.cfg1_thought()]
+        th = [t.cuda() for t in cases.thought_4x32x512()]
         for _ in range(2):
             m = ops.masked_diffusion_corrupt_from_random(*md)
             d = ops.display_corrupt_from_random(*dc, V3 - 1, EOS_ID, V3, 0.25)

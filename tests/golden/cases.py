@@ -86,8 +86,8 @@ def adversarial_logits(vocab: int, dtype: torch.dtype, pattern: str):
     return ids, logits
 
 
-def cfg1_display(seed: int = 0):
-    """Config 1: fp32 [4,256,32000] = 3*N(0,1); ids uniform; display mask
+def display_f32_4x256x32000(seed: int = 0):
+    """Display logits fp32 [4,256,32000] = 3*N(0,1); ids uniform; display mask
     Bernoulli(0.5) (inactive positions hold the mask id); an EOS planted per
     row with the tail masked, as tests/test_fuzz.py:232-237 does."""
     g = _g(seed)
@@ -103,9 +103,10 @@ def cfg1_display(seed: int = 0):
     return ids, logits
 
 
-def cfg2_display_rows(rows: int, seed: int = 1, vocab: int = 128256):
-    """Config 2 distribution: bf16(2*N(0,1)) with a +8 peak in 10% of rows and
-    an exact two-way tie at rowmax+1 in 1% of rows (lowest index wins)."""
+def peaked_display_rows(rows: int, seed: int = 1, vocab: int = 128256):
+    """Rows of the [32, 1024, 128256] bench distribution: bf16(2*N(0,1)) with
+    a +8 peak in 10% of rows and an exact two-way tie at rowmax+1 in 1% of
+    rows (lowest index wins)."""
     g = _g(seed)
     logits = (torch.randn((rows, vocab), generator=g) * 2.0).to(torch.bfloat16)
     peak = torch.rand(rows, generator=g) < 0.10
@@ -179,11 +180,11 @@ def stats_cases() -> Iterator[Case]:
         if k % 3 == 0:
             lg = _strided_last_dim(lg)
         yield Case(f"stats/fuzz_{k}", op, [ids, lg])
-    yield Case("stats/cfg1", op, list(cfg1_display()))
-    yield Case("stats/cfg2_rows256", op, list(cfg2_display_rows(256)))
+    yield Case("stats/f32_4x256x32000", op, list(display_f32_4x256x32000()))
+    yield Case("stats/peaked_rows256", op, list(peaked_display_rows(256)))
     g = _g(4)
     lg = (torch.randn(2, 512, 32000, generator=g) * 3.0).to(torch.bfloat16)
-    yield Case("stats/cfg5_rows", op, [torch.randint(32000, (2, 512), generator=g), lg])
+    yield Case("stats/bf16_2x512x32000", op, [torch.randint(32000, (2, 512), generator=g), lg])
 
 
 # --------------------------------------------------------------------------
@@ -488,10 +489,10 @@ def rollout_cases() -> Iterator[Case]:
     il[1, 3, 1] = float("nan")
     occ = torch.randint(0, 2, (4, 33, 1), generator=g).float()
     yield Case("rollout/ties_nan", op, [occ, torch.randn(4, 33, generator=g), lc, rv, il, 0.5, 5, 1])
-    g = _g(4)  # config 5 slot state: B=256, S=128, F=4, Rv=3, retired index 3
+    g = _g(4)  # decode-loop slot state: B=256, S=128, F=4, Rv=3, retired index 3
     occ = (torch.rand(256, 128, generator=g) < 0.4).float().unsqueeze(-1)
     yield Case(
-        "rollout/cfg5", op,
+        "rollout/256x128", op,
         [occ, torch.randn(256, 128, generator=g), torch.randn(256, 128, 4, generator=g),
          torch.randn(256, 128, 3, generator=g), torch.randn(256, 128, 4, generator=g),
          0.5, 8, 3],
@@ -536,7 +537,7 @@ def snapshot_cases() -> Iterator[Case]:
         )
     g = _g(903)
     yield Case(
-        "snapshot/cfg5", op,
+        "snapshot/8x128x512", op,
         [torch.randn(8, 128, 512, generator=g).to(torch.bfloat16),
          torch.randn(8, 128, 6, generator=g).to(torch.bfloat16),
          torch.rand(8, 128, 1, generator=g).to(torch.bfloat16),
@@ -574,7 +575,7 @@ def masked_diffusion_cases() -> Iterator[Case]:
         [torch.randint(0, 32000, (8, 2048), generator=g), torch.rand(8, 1, generator=g),
          torch.rand(8, 2048, generator=g), 31999, 0.001, 1.0],
     )
-    yield Case("md/cfg3", op, list(cfg3_masked_diffusion()))
+    yield Case("md/64x2048", op, list(masked_diffusion_64x2048()))
     for k in range(30):
         g = _g(9000 + k)
         b, t = 1 + k % 7, [1, 2, 5, 64, 333][k % 5]
@@ -597,8 +598,8 @@ def masked_diffusion_cases() -> Iterator[Case]:
         yield Case(f"md/long_{k}", op, [torch.randint(0, 50257, (b, t), generator=g), rr, mr, 50256, 1.0e-6, 1.0])
 
 
-def cfg3_masked_diffusion(seed: int = 2):
-    """Config 3: ids [64,2048] uniform in [0,50257); ratio U(0,1) with 3 of
+def masked_diffusion_64x2048(seed: int = 2):
+    """Masked diffusion: ids [64,2048] uniform in [0,50257); ratio U(0,1) with 3 of
     64 rows forced to 0; uniforms fp32; mask id 50256; min 1e-6, max 1."""
     g = _g(seed)
     clean = torch.randint(0, 50257, (64, 2048), generator=g)
@@ -641,11 +642,11 @@ def thought_cases() -> Iterator[Case]:
              torch.randint(0, 2, (b, s, 1), generator=g).to(dt),
              torch.randn(b, s, h, generator=g).to(dt)],
         )
-    yield Case("thought/cfg1", op, list(cfg1_thought()))
+    yield Case("thought/4x32x512", op, list(thought_4x32x512()))
 
 
-def cfg1_thought(seed: int = 0):
-    """Config 1 thought state: fp32 [4,32,512] N(0,1), eps N(0,1), t = 0.3,
+def thought_4x32x512(seed: int = 0):
+    """Thought state fp32 [4,32,512] N(0,1), eps N(0,1), t = 0.3,
     occupancy Bernoulli(0.4)."""
     g = _g(seed + 100)
     sem = torch.randn(4, 32, 512, generator=g)

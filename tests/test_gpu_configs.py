@@ -35,8 +35,8 @@ def _check_stats(out, ids, logits, name):
     compare.assert_matches(STATS, out, expected, name)
 
 
-def test_cfg2_full_size_rows_match_oracle() -> None:
-    """Config 2: bf16 [32, 1024, 128256] with planted peaks and exact ties."""
+def test_full_size_32x1024x128256_rows_match_oracle() -> None:
+    """The bench step's logits, bf16 [32, 1024, 128256], with planted peaks and exact ties."""
     import bench
 
     dev = torch.device("cuda", 0)
@@ -57,16 +57,16 @@ def test_cfg2_full_size_rows_match_oracle() -> None:
     sub_ids = ids.view(-1)[sel].view(1, -1).cpu()
     sub_lg = flat[sel].view(1, -1, 128256).cpu()
     out = (conf.view(-1)[sel].view(1, -1), pred.view(-1)[sel].view(1, -1), cur.view(-1)[sel].view(1, -1))
-    _check_stats(out, sub_ids, sub_lg, "cfg2 rows")
+    _check_stats(out, sub_ids, sub_lg, "32x1024x128256 rows")
     assert bool(torch.isfinite(conf).all()) and bool(((conf > 0) & (conf <= 1)).all())
     assert bool((cur <= conf * (1 + 1e-6)).all())
 
 
-def test_cfg1_chain_matches_oracle() -> None:
-    """Config 1: fp32 [4, 256, 32000] stats -> refine, S=32 slots, thought t=0.3."""
-    ids, logits = cases.cfg1_display()
+def test_chain_4x256x32000_matches_oracle() -> None:
+    """fp32 [4, 256, 32000] stats -> refine, S=32 slots, thought t=0.3."""
+    ids, logits = cases.display_f32_4x256x32000()
     conf, pred, cur = torch.ops.cid_engine.display_token_statistics(ids.cuda(), logits.cuda())
-    _check_stats((conf, pred, cur), ids, logits, "cfg1 stats")
+    _check_stats((conf, pred, cur), ids, logits, "4x256x32000 stats")
     refined = torch.ops.cid_engine.refine_display_from_statistics(
         ids.cuda(), conf, pred, cur, 0, 1, 0.25, 0.1, 0.05)
     expected = oracle.refine_display_from_statistics(ids, conf.cpu(), pred.cpu(), cur.cpu(),
@@ -78,27 +78,27 @@ def test_cfg1_chain_matches_oracle() -> None:
     life[..., 3] = (torch.rand(4, 32, generator=g) < 0.1).float()
     live = torch.ops.cid_engine.live_slot_occupancy(occ.cuda(), life.cuda(), 3)
     assert torch.equal(live.cpu(), oracle.live_slot_occupancy(occ, life, 3))
-    th = cases.cfg1_thought()
+    th = cases.thought_4x32x512()
     got = torch.ops.cid_engine.thought_corrupt_from_epsilon(*[t.cuda() for t in th])
     compare.assert_matches("thought_corrupt_from_epsilon", got,
-                           oracle.thought_corrupt_from_epsilon(*th), "cfg1 thought")
+                           oracle.thought_corrupt_from_epsilon(*th), "4x32x512 thought")
 
 
-def test_cfg3_masked_diffusion_full_and_deterministic() -> None:
-    args = list(cases.cfg3_masked_diffusion())
+def test_masked_diffusion_64x2048_deterministic() -> None:
+    args = list(cases.masked_diffusion_64x2048())
     dev_args = [a.cuda() if isinstance(a, torch.Tensor) else a for a in args]
     out1 = torch.ops.cid_engine.masked_diffusion_corrupt_from_random(*dev_args)
     out2 = torch.ops.cid_engine.masked_diffusion_corrupt_from_random(*dev_args)
     for a, b in zip(out1, out2):
         assert torch.equal(a, b)  # fixed-order metrics: bit-identical
     compare.assert_matches("masked_diffusion_corrupt_from_random", out1,
-                           oracle.masked_diffusion_corrupt_from_random(*args), "cfg3")
+                           oracle.masked_diffusion_corrupt_from_random(*args), "64x2048")
     assert bool(out1[1].any(dim=1).all())  # zero-ratio rows took the fallback
 
 
 @pytest.mark.parametrize("tokens", [512, 4096, 8192])
-def test_cfg5_refine_rows_match_oracle(tokens: int) -> None:
-    """Config-5 refine shape (B=256, L=512) plus long rows that exceed the
+def test_refine_large_rows_match_oracle(tokens: int) -> None:
+    """Decode-loop refine shape (B=256, L=512) plus long rows that exceed the
     shared-memory staging (global-memory path)."""
     batch = 256 if tokens == 512 else 4
     ids, (conf, pred, cur) = cases.refine_inputs_large(77 + tokens, batch, tokens)
