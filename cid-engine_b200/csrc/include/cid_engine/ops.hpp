@@ -7,7 +7,7 @@
 //   * CUDA: enqueues the sm_100a kernels through the C ABI
 //     (include/cid_engine_b200.h) on the current stream of the inputs' device;
 //   * Meta: returns empty outputs of the right shapes and dtypes;
-//   * CPU:  raises — this build has no CPU backend.
+//   * CPU:  raises — this library has no CPU backend.
 #pragma once
 
 #include <ATen/ATen.h>
@@ -84,7 +84,7 @@ at::Tensor materialize_cell_snapshot(Backend backend, const at::Tensor& thought_
                                      const at::Tensor& selected,
                                      const at::Tensor& semantic_indices);
 
-// Vocabulary-parallel statistics (additive operators of this build).
+// Vocabulary-parallel statistics (additive operators of this library).
 at::Tensor display_shard_records(Backend backend, const at::Tensor& token_ids,
                                  const at::Tensor& logits_shard, std::int64_t vocab_offset,
                                  std::int64_t total_vocab);

@@ -57,7 +57,7 @@ std::uint32_t* status_word(const at::Device& device) {
 
 [[noreturn]] void no_cpu_backend(const char* op) {
   TORCH_CHECK(false, "cid_engine.", op,
-              ": this build runs on CUDA devices only (sm_100a kernels, no CPU "
+              ": cid-engine-b200 runs on CUDA devices only (sm_100a kernels, no CPU "
               "fallback); move the inputs to a CUDA device");
 }
 

@@ -1,7 +1,7 @@
 // Host entry of the display refinement policy.  The reference runs the policy
 // on host copies of the statistics (csrc/refine.cpp:246-250, 428 of
 // fwerkor/cid-engine v1.1.0: four device->host copies and one host->device
-// copy per call, i.e. a host sync every decode step); this build validates on
+// copy per call, i.e. a host sync every decode step); this library validates on
 // the host and runs the whole policy on the device (one CTA per row).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>

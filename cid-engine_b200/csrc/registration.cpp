@@ -7,7 +7,7 @@
 // Kernels are registered per dispatch key (the reference registers
 // CompositeImplicitAutograd ATen implementations plus CUDA overrides):
 //   CUDA -> sm_100a kernels, Meta -> shape functions, CPU -> validation and
-//   a clear error (this build has no CPU backend).
+//   a clear error (this library has no CPU backend).
 #include <torch/library.h>
 
 #include "cid_engine/ops.hpp"
