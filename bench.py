@@ -74,6 +74,54 @@ def _peaks() -> tuple[float, str]:
 # ---------------------------------------------------------------------------
 
 
+def loop_logits(step: int, device, batch: int | None = None):
+    """Decode-loop logits of step ``step``: bf16 [256, 512, 32000] =
+    bf16(3 N(0,1)) from seed 4 + step (the first ``batch`` sequences)."""
+    import torch
+
+    B, L, V = LOOP["B"], LOOP["L"], LOOP["V"]
+    g = torch.Generator(device=device).manual_seed(4 + step)
+    lg = torch.randn((B, L, V), generator=g, device=device, dtype=torch.bfloat16)
+    lg.mul_(3.0)
+    return lg if batch is None else lg[:batch].contiguous()
+
+
+def loop_state(device):
+    """Decode-loop start state (seed 4): display ids [256, 512] over 32000
+    tokens with positions masked with probability 0.6, and the 128-slot
+    thought state with occupancy Bernoulli(0.4)."""
+    import torch
+
+    from cid_engine.step import SlotInputs
+
+    c = LOOP
+    B, L, V, S = c["B"], c["L"], c["V"], c["S"]
+    dev = device
+    g = torch.Generator(device=dev).manual_seed(4)
+    ids0 = torch.randint(2, V, (B, L), generator=g, device=dev)
+    ids0[torch.rand((B, L), generator=g, device=dev) < 0.6] = MASK_ID
+    occ = (torch.rand((B, S, 1), generator=g, device=dev) < 0.4).float()
+    slot = SlotInputs(
+        occupancy=occ,
+        allocation_logits=torch.randn((B, S), generator=g, device=dev),
+        lifecycle_logits=torch.randn((B, S, c["F"]), generator=g, device=dev),
+        revision_logits=torch.randn((B, S, c["Rv"]), generator=g, device=dev),
+        input_lifecycle=torch.randn((B, S, c["F"]), generator=g, device=dev),
+        semantic=torch.randn((B, S, c["H"]), generator=g, device=dev),
+        role_logits=torch.randn((B, S, c["Rr"]), generator=g, device=dev),
+        uncertainty=torch.rand((B, S, 1), generator=g, device=dev),
+        noise_delta=torch.randn((B, S, 1), generator=g, device=dev),
+        semantic_indices=torch.randint(0, c["H"], (c["K"],), generator=g, device=dev),
+        threshold=0.5, max_allocations=8, retired_index=3,
+    )
+    return ids0, slot
+
+
+def loop_initial_ids(device):
+    """Display ids the decode loop starts from."""
+    return loop_state(device)[0]
+
+
 def display_inputs(B, L, V, seed, device, dtype=None):
     """bf16(2 N(0,1)) logits with planted peaks/ties, display ids with masked
     positions (p=0.6) and one EOS per row."""
@@ -400,33 +448,12 @@ def bench_refine_loop(dev) -> dict:
     import torch
 
     from cid_engine.loop import DisplayRefineLoop
-    from cid_engine.step import SlotInputs
 
     c = LOOP
     B, L, V, S = c["B"], c["L"], c["V"], c["S"]
-    ring = []
-    for k in range(3):  # ring of pre-generated logits (each 8.4 GB > L2)
-        g = torch.Generator(device=dev).manual_seed(4 + k)
-        lg = torch.randn((B, L, V), generator=g, device=dev, dtype=torch.bfloat16)
-        lg.mul_(3.0)
-        ring.append(lg)
-    g = torch.Generator(device=dev).manual_seed(4)
-    ids0 = torch.randint(2, V, (B, L), generator=g, device=dev)
-    ids0[torch.rand((B, L), generator=g, device=dev) < 0.6] = MASK_ID
-    occ = (torch.rand((B, S, 1), generator=g, device=dev) < 0.4).float()
-    slot = SlotInputs(
-        occupancy=occ,
-        allocation_logits=torch.randn((B, S), generator=g, device=dev),
-        lifecycle_logits=torch.randn((B, S, c["F"]), generator=g, device=dev),
-        revision_logits=torch.randn((B, S, c["Rv"]), generator=g, device=dev),
-        input_lifecycle=torch.randn((B, S, c["F"]), generator=g, device=dev),
-        semantic=torch.randn((B, S, c["H"]), generator=g, device=dev),
-        role_logits=torch.randn((B, S, c["Rr"]), generator=g, device=dev),
-        uncertainty=torch.rand((B, S, 1), generator=g, device=dev),
-        noise_delta=torch.randn((B, S, 1), generator=g, device=dev),
-        semantic_indices=torch.randint(0, c["H"], (c["K"],), generator=g, device=dev),
-        threshold=0.5, max_allocations=8, retired_index=3,
-    )
+    # ring of pre-generated logits (each 8.4 GB > L2)
+    ring = [loop_logits(k, dev) for k in range(3)]
+    ids0, slot = loop_state(dev)
     params = dict(mask_token_id=MASK_ID, eos_token_id=EOS_ID, reveal_fraction=REVEAL,
                   revision_fraction=REVISION, revision_margin=MARGIN)
     steps = c["steps"]

@@ -34,6 +34,7 @@ STATUS_REPETITION_ID_OUT_OF_RANGE = 0x4
 STATUS_ASSIGNMENT_INVALID = 0x8
 STATUS_LM_HEAD_TIMEOUT = 0x10
 STATUS_PEER_TIMEOUT = 0x20
+STATUS_PEER_OUT_OF_STEP = 0x40
 
 
 def device_status(device: int | torch.device = 0, *, reset: bool = False) -> int:

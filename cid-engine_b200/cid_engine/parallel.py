@@ -106,10 +106,18 @@ class PeerRecordExchange:
     the epoch in this rank's inbox, then merges.  Two parities make reuse
     safe: a rank starts step k+2 only after every rank's step-k combine.  A
     wait that runs out sets ``cid_engine.STATUS_PEER_TIMEOUT`` in the device
-    status word and leaves NaN statistics.  Every rank must call
-    ``statistics`` the same number of times."""
+    status word and leaves NaN statistics.  That breaks the two-parity
+    argument (the rank that gave up may overwrite a slower rank's slot), so
+    from then on the exchange is poisoned on the device: a combine that finds
+    a peer two epochs ahead sets ``STATUS_PEER_OUT_OF_STEP``, and every
+    combine on a device whose status word holds either bit writes NaN without
+    waiting.  ``healthy()`` reads the word (a host sync); after a failure the
+    caller resets the word (``cid_engine.device_status(reset=True)``) and
+    builds a new exchange on every rank.  Every rank must call ``statistics``
+    the same number of times.  ``wait_seconds`` (at most 60) bounds each
+    combine's wait."""
 
-    def __init__(self, rows_capacity: int, *, group=None, wait_seconds: float = 5.0) -> None:
+    def __init__(self, rows_capacity: int, *, group=None, wait_seconds: float = 2.0) -> None:
         import ctypes
 
         self.lib = _capi()
@@ -117,6 +125,8 @@ class PeerRecordExchange:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.capacity = int(rows_capacity)
+        if not 0.0 < wait_seconds <= 60.0:
+            raise ValueError("wait_seconds must be in (0, 60]")
         self.wait_seconds = float(wait_seconds)
         self.device = torch.device("cuda", torch.cuda.current_device())
         nbytes = self.lib.cid_peer_inbox_bytes(self.world, self.capacity)
@@ -217,6 +227,14 @@ class PeerRecordExchange:
             self.own, self.world, offs, ids.data_ptr(), ids.numel(), self.capacity,
             self.epoch & 0xffffffff, self.wait_seconds, conf.data_ptr(), pred.data_ptr(),
             cur.data_ptr(), status, stream), "combine_inbox")
+
+    def healthy(self) -> bool:
+        """False once a combine on this device has timed out or met a peer out
+        of step (reads the device status word: synchronises the device)."""
+        import cid_engine
+
+        bad = cid_engine.STATUS_PEER_TIMEOUT | cid_engine.STATUS_PEER_OUT_OF_STEP
+        return not (cid_engine.device_status(self.device) & bad)
 
     def close(self) -> None:
         """Unmaps the peers' inboxes and frees this rank's (after every rank

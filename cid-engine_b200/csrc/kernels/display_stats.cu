@@ -822,40 +822,76 @@ __global__ void combine_records_kernel(CombineParams p) {
 // its flag word there (thread 0 of each CTA waits, acquire at system scope,
 // bounded by wait_ns; a wait that runs out sets CID_STATUS_PEER_TIMEOUT and
 // the CTA writes NaN statistics with predicted 0).
+//
+// A rank can run at most one epoch ahead of another while every combine
+// waits for all flags (its push of epoch e+2 is ordered after a combine of
+// e+1 that needs this rank's e+1 records, which follow this rank's combine of
+// e), so a flag of epoch or epoch+1 means the parity slot of `epoch` holds
+// that epoch's records.  A flag two or more epochs ahead means that peer gave
+// up waiting on this rank earlier and may already have overwritten the slot:
+// the CTA then sets CID_STATUS_PEER_OUT_OF_STEP and writes NaN.  The flags
+// are read once more after the rows are combined, so a peer that overtook
+// the slot while it was being read is caught too (the step's statistics are
+// then invalid and the bit says so).  Once either peer bit is set in the
+// status word the exchange is poisoned: later combines write NaN without
+// waiting until the host clears the word and rebuilds the exchange.
+__device__ __forceinline__ int32_t peer_lead(const uint32_t* flag, uint32_t epoch) {
+  uint32_t f;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flag) : "memory");
+  return static_cast<int32_t>(f - epoch);
+}
+
 __global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uint32_t epoch,
                                      unsigned long long wait_ns) {
+  constexpr uint32_t kPoisoned = CID_STATUS_PEER_TIMEOUT | CID_STATUS_PEER_OUT_OF_STEP;
   __shared__ int ready;
   if (threadIdx.x == 0) {
+    bool ok = !(p.status && (*reinterpret_cast<volatile uint32_t*>(p.status) & kPoisoned));
+    uint32_t bit = 0;
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    bool ok = true;
     for (int q = 0; q < p.world && ok; ++q) {
       for (;;) {
-        uint32_t f;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flags + q) : "memory");
-        if (static_cast<int32_t>(f - epoch) >= 0) break;
+        const int32_t lead = peer_lead(flags + q, epoch);
+        if (lead == 0 || lead == 1) break;
+        if (lead > 1) {
+          ok = false;
+          bit = CID_STATUS_PEER_OUT_OF_STEP;
+          break;
+        }
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         if (t - t0 > wait_ns) {
           ok = false;
+          bit = CID_STATUS_PEER_TIMEOUT;
           break;
         }
         __nanosleep(256);
       }
     }
-    if (!ok && p.status) atomicOr(p.status, CID_STATUS_PEER_TIMEOUT);
+    if (bit && p.status) atomicOr(p.status, bit);
     ready = ok ? 1 : 0;
   }
   __syncthreads();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (row >= p.rows) return;
   if (!ready) {
-    p.predicted[row] = 0;
-    p.confidence[row] = __int_as_float(0x7fffffff);
-    p.current[row] = __int_as_float(0x7fffffff);
+    if (row < p.rows) {
+      p.predicted[row] = 0;
+      p.confidence[row] = __int_as_float(0x7fffffff);
+      p.current[row] = __int_as_float(0x7fffffff);
+    }
     return;
   }
-  combine_row(p, row);
+  if (row < p.rows) combine_row(p, row);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < p.world; ++q) {
+      if (peer_lead(flags + q, epoch) > 1) {
+        if (p.status) atomicOr(p.status, CID_STATUS_PEER_OUT_OF_STEP);
+        break;
+      }
+    }
+  }
 }
 
 // Merges the records of W ascending column ranges of each row into the one
@@ -1320,7 +1356,7 @@ extern "C" int cid_display_combine_inbox(void* inbox, int world,
                                          uint32_t* status, void* stream) {
   if (world < 1 || world > kMaxPeers || !shard_offsets_host || !inbox)
     return CID_ERR_INVALID_ARGUMENT;
-  if (rows < 1 || rows > rows_capacity || !(wait_seconds > 0.0 && wait_seconds < 3600.0))
+  if (rows < 1 || rows > rows_capacity || !(wait_seconds > 0.0 && wait_seconds <= 60.0))
     return CID_ERR_INVALID_ARGUMENT;
   if (!token_ids || !confidence || !predicted || !current_confidence)
     return CID_ERR_INVALID_ARGUMENT;

@@ -69,6 +69,10 @@ typedef enum cid_result {
 /* A rank's records of this epoch did not arrive in a peer exchange's wait
  * (its statistics are NaN). */
 #define CID_STATUS_PEER_TIMEOUT 0x20u
+/* A rank ran two or more epochs ahead of this rank's combine in a peer
+ * exchange (it gave up waiting on this rank earlier), so this rank's inbox
+ * may hold a later step's records: the step's statistics are invalid. */
+#define CID_STATUS_PEER_OUT_OF_STEP 0x40u
 
 CID_API int cid_abi_version(void);
 CID_API const char* cid_result_string(int result);
@@ -387,8 +391,13 @@ CID_API int cid_peer_push_records(const cid_shard_record_t* records, int64_t row
                         void* stream);
 
 /* cid_display_combine_records over this rank's inbox once every rank has
- * published `epoch` there; the wait is bounded by wait_seconds, after which
- * the statistics are NaN (predicted 0) and CID_STATUS_PEER_TIMEOUT is set. */
+ * published `epoch` there; the wait is bounded by wait_seconds (at most 60),
+ * after which the statistics are NaN (predicted 0) and
+ * CID_STATUS_PEER_TIMEOUT is set.  A peer found two or more epochs ahead
+ * (before or after the rows are read) sets CID_STATUS_PEER_OUT_OF_STEP.
+ * While either bit is set in *status, the exchange is poisoned: every
+ * combine writes NaN statistics without waiting, until the caller clears the
+ * word and builds a new exchange (fresh inboxes, epochs from 1). */
 CID_API int cid_display_combine_inbox(void* inbox, int world, const int64_t* shard_offsets_host,
                         const int64_t* token_ids, int64_t rows, int64_t rows_capacity,
                         uint32_t epoch, double wait_seconds, float* confidence,

@@ -153,15 +153,99 @@ static void stats_row(const float* x, int64_t vocab, int64_t id, float* conf,
   *cur = (float)(exp((double)x[id] - (double)m) / s);
 }
 
+/* Reference-order statistics.  The reference's CPU kernel sums
+ * exp(x - max) in float32 through at::vec::map_reduce_all
+ * (csrc/cpu/display_stats.cpp:37-42).  That translation unit is built
+ * without ATen's CPU_CAPABILITY dispatch macros, so Vectorized<float> is
+ * ATen's generic 32-byte vector: 8 float lanes, exp() applied lane by lane
+ * with std::exp (libm expf), lanes summed element-wise, and the final
+ * horizontal sum taken serially, lane 0 + lane 1 + ... + lane 7
+ * (ATen/cpu/vec/functional_base.h map_reduce_all / vec_reduce_all).  For
+ * f16/bf16 logits the reduced-float overload
+ * (ATen/cpu/vec/functional_bfloat16.h) loads 16 values, converts them to two
+ * float vectors with one accumulator each, and adds the second accumulator
+ * into the first before the serial horizontal sum.  Tails shorter than a
+ * vector update only their own lanes; rows shorter than a vector sum their
+ * lanes serially.  Evaluated in this order with the same expf, the float32
+ * result reproduces the reference's own rounding, which the double-precision
+ * stats_row above does not (it returns the exactly rounded value). */
+enum { REF_LANES = 8 };
+
+static float ref_serial_lanes(const float* lanes, int64_t n) {
+  float r = lanes[0];
+  for (int64_t j = 1; j < n; ++j) r += lanes[j];
+  return r;
+}
+
+static float ref_sum_f32(const float* x, int64_t n, float m) {
+  float acc[REF_LANES];
+  if (n < REF_LANES) {
+    for (int64_t j = 0; j < n; ++j) acc[j] = expf(x[j] - m);
+    return ref_serial_lanes(acc, n);
+  }
+  for (int j = 0; j < REF_LANES; ++j) acc[j] = expf(x[j] - m);
+  int64_t d = REF_LANES;
+  const int64_t body = n - n % REF_LANES;
+  for (; d < body; d += REF_LANES)
+    for (int j = 0; j < REF_LANES; ++j) acc[j] += expf(x[d + j] - m);
+  for (int64_t j = 0; j < n - d; ++j) acc[j] += expf(x[d + j] - m);
+  return ref_serial_lanes(acc, REF_LANES);
+}
+
+static float ref_sum_reduced(const float* x, int64_t n, float m) {
+  enum { W = REF_LANES, B = 2 * REF_LANES };
+  float a0[W], a1[W];
+  if (n < B) {
+    if (n > W) {
+      for (int j = 0; j < W; ++j) a0[j] = expf(x[j] - m);
+      for (int64_t j = 0; j < n - W; ++j) a0[j] += expf(x[W + j] - m);
+      return ref_serial_lanes(a0, W);
+    }
+    for (int64_t j = 0; j < n; ++j) a0[j] = expf(x[j] - m);
+    return ref_serial_lanes(a0, n);
+  }
+  for (int j = 0; j < W; ++j) {
+    a0[j] = expf(x[j] - m);
+    a1[j] = expf(x[W + j] - m);
+  }
+  int64_t d = B;
+  const int64_t body = n - n % B;
+  for (; d < body; d += B)
+    for (int j = 0; j < W; ++j) {
+      a0[j] += expf(x[d + j] - m);
+      a1[j] += expf(x[d + W + j] - m);
+    }
+  const int64_t r = n - d;
+  if (r > W) {
+    for (int j = 0; j < W; ++j) a0[j] += expf(x[d + j] - m);
+    for (int64_t j = 0; j < r - W; ++j) a1[j] += expf(x[d + W + j] - m);
+  } else {
+    for (int64_t j = 0; j < r; ++j) a0[j] += expf(x[d + j] - m);
+  }
+  for (int j = 0; j < W; ++j) a0[j] += a1[j];
+  return ref_serial_lanes(a0, W);
+}
+
+static void stats_row_reference_order(int dtype, const float* x, int64_t vocab,
+                                      int64_t id, float* conf, int64_t* pred,
+                                      float* cur) {
+  float m;
+  *pred = first_argmax_f(x, vocab, &m); /* display_stats.cpp:86-88 */
+  const float s = dtype == CID_DT_F32 ? ref_sum_f32(x, vocab, m)
+                                      : ref_sum_reduced(x, vocab, m);
+  *conf = 1.0f / s;                    /* display_stats.cpp:46 */
+  *cur = expf(x[id] - m) / s;          /* display_stats.cpp:44-47 */
+}
+
 static void row_to_float(int dtype, const void* logits, int64_t row,
                          int64_t vocab, float* dst) {
   for (int64_t v = 0; v < vocab; ++v)
     dst[v] = (float)load(dtype, logits, row * vocab + v);
 }
 
-int cid_oracle_display_stats(int dtype, const void* logits, const int64_t* ids,
-                             int64_t rows, int64_t vocab, float* confidence,
-                             int64_t* predicted, float* current) {
+static int stats_rows(int dtype, const void* logits, const int64_t* ids,
+                      int64_t rows, int64_t vocab, float* confidence,
+                      int64_t* predicted, float* current, int reference_order) {
   if (vocab <= 0) return -1; /* ops.cpp:456 */
   int bad = 0;
 #pragma omp parallel
@@ -175,11 +259,38 @@ int cid_oracle_display_stats(int dtype, const void* logits, const int64_t* ids,
         continue;
       }
       row_to_float(dtype, logits, r, vocab, buf);
-      stats_row(buf, vocab, id, &confidence[r], &predicted[r], &current[r]);
+      if (reference_order)
+        stats_row_reference_order(dtype, buf, vocab, id, &confidence[r],
+                                  &predicted[r], &current[r]);
+      else
+        stats_row(buf, vocab, id, &confidence[r], &predicted[r], &current[r]);
     }
     free(buf);
   }
   return bad ? -2 : 0;
+}
+
+int cid_oracle_display_stats(int dtype, const void* logits, const int64_t* ids,
+                             int64_t rows, int64_t vocab, float* confidence,
+                             int64_t* predicted, float* current) {
+  return stats_rows(dtype, logits, ids, rows, vocab, confidence, predicted,
+                    current, 0);
+}
+
+/* f32/f16/bf16 logits take the reference's CPU kernel
+ * (csrc/cpu/display_stats.cpp:14-50) in its own float32 summation order;
+ * other dtypes go through the reference's composite (csrc/ops.cpp:446-474,
+ * ATen logsumexp), whose order depends on the host's SIMD dispatch, so
+ * there this returns the exactly rounded value like
+ * cid_oracle_display_stats. */
+int cid_oracle_display_stats_reference_order(int dtype, const void* logits,
+                                             const int64_t* ids, int64_t rows,
+                                             int64_t vocab, float* confidence,
+                                             int64_t* predicted,
+                                             float* current) {
+  const int ref = dtype == CID_DT_F32 || dtype == CID_DT_F16 || dtype == CID_DT_BF16;
+  return stats_rows(dtype, logits, ids, rows, vocab, confidence, predicted,
+                    current, ref);
 }
 
 /* display_token_statistics_with_repetition — csrc/ops.cpp:477-552.  The

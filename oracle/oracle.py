@@ -83,7 +83,22 @@ def _check(rc: int, message: str) -> None:
 
 
 def display_token_statistics(token_ids: torch.Tensor, logits: torch.Tensor):
-    """csrc/cpu/display_stats.cpp:54-126 (f32/f16/bf16) and csrc/ops.cpp:446-474."""
+    """csrc/cpu/display_stats.cpp:54-126 (f32/f16/bf16) and csrc/ops.cpp:446-474.
+
+    Confidences are the exactly rounded values: the sum of exp(x - max) is
+    taken in double and rounded to float32 once."""
+    return _stats(token_ids, logits, "cid_oracle_display_stats")
+
+
+def display_token_statistics_reference_order(token_ids: torch.Tensor, logits: torch.Tensor):
+    """csrc/cpu/display_stats.cpp:14-50 evaluated in the reference's own
+    float32 order (8 lanes of ATen's generic Vectorized<float>, libm expf,
+    serial horizontal sum), so the confidences carry the reference's own
+    rounding; argmax is identical to ``display_token_statistics``."""
+    return _stats(token_ids, logits, "cid_oracle_display_stats_reference_order")
+
+
+def _stats(token_ids: torch.Tensor, logits: torch.Tensor, entry: str):
     ids = _host(token_ids)
     lg = _host(logits)
     if ids.dtype != torch.int64:
@@ -94,7 +109,7 @@ def display_token_statistics(token_ids: torch.Tensor, logits: torch.Tensor):
     rows = ids.numel()
     if rows == 0:
         return conf, pred, cur
-    rc = lib().cid_oracle_display_stats(
+    rc = getattr(lib(), entry)(
         DT[lg.dtype], _p(lg), _p(ids), _i(rows), _i(lg.shape[-1]),
         _p(conf), _p(pred), _p(cur),
     )

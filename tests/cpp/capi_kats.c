@@ -19,6 +19,11 @@
     }                                          \
   } while (0)
 
+/* float32 statistics: within a pure relative 1e-5 of the exact value */
+static int rel_close(float got, double expect) {
+  return fabs((double)got - expect) <= 1e-5 * fabs(expect);
+}
+
 static void* dev_copy(const void* host, size_t bytes) {
   void* d = NULL;
   if (cudaMalloc(&d, bytes) != cudaSuccess) return NULL;
@@ -83,7 +88,7 @@ int main(void) {
   cudaMemcpy(&pred, d_pred, 8, cudaMemcpyDeviceToHost);
   const double expect = 1.0 / (exp(-4.0) + 2.0 + exp(-3.0));
   CHECK(pred == 1, "argmax must keep the first tie");
-  CHECK(fabs(conf - expect) < 2e-6 && fabs(cur - expect) < 2e-6, "statistics mismatch");
+  CHECK(rel_close(conf, expect) && rel_close(cur, expect), "statistics mismatch");
 
   /* the same row through a one-rank peer exchange: inbox, records, combine */
   size_t inbox_bytes = cid_peer_inbox_bytes(1, 1);
@@ -99,7 +104,7 @@ int main(void) {
   cudaMemcpy(&conf, d_conf, 4, cudaMemcpyDeviceToHost);
   cudaMemcpy(&cur, d_cur, 4, cudaMemcpyDeviceToHost);
   cudaMemcpy(&pred, d_pred, 8, cudaMemcpyDeviceToHost);
-  CHECK(pred == 1 && fabs(conf - expect) < 2e-6 && fabs(cur - expect) < 2e-6,
+  CHECK(pred == 1 && rel_close(conf, expect) && rel_close(cur, expect),
         "peer exchange statistics mismatch");
   CHECK(cid_peer_inbox_free(inbox) == CID_OK, "inbox free");
 
@@ -127,7 +132,7 @@ int main(void) {
   cudaMemcpy(&pred, d_pred, 8, cudaMemcpyDeviceToHost);
   const double s_lm = 2.0 + exp(-2.0) + 297.0 * exp(-3.0);
   CHECK(pred == 5, "lm head argmax must keep the first tie");
-  CHECK(fabs(conf - 1.0 / s_lm) < 2e-6 && fabs(cur - exp(-2.0) / s_lm) < 2e-6,
+  CHECK(rel_close(conf, 1.0 / s_lm) && rel_close(cur, exp(-2.0) / s_lm),
         "lm head statistics mismatch");
 
   CHECK(cudaDeviceSynchronize() == cudaSuccess, "device error");

@@ -1,11 +1,21 @@
 """Comparison helpers shared by the golden and GPU parity tests.
 
-Tolerances per operator follow the reference's own tests and the path's
-parity contract: decisions, token ids, masks and argmax indices are compared
-exactly; float32 statistics within rtol 2e-5 / atol 2e-6
-(tests/test_engine.py:24-26 of the reference); snapshot values, which pass
-through float32 sigmoid, within one float32 ulp; thought corruption within
-one ulp of the storage type (alpha passes through cos).
+Tolerances per operator follow the path's parity contract: decisions, token
+ids, masks and argmax indices are compared exactly; float32 statistics
+(confidence, current confidence) within a pure relative 1e-5 of the exactly
+rounded value, with an absolute floor of 1e-30 that only matters below the
+float32 normal range (subnormal results, which the device flushes to zero);
+snapshot values, which pass through float32 sigmoid, within one float32 ulp;
+thought corruption within one ulp of the storage type (alpha passes through
+cos).
+
+The reference's own float32 statistics are not the exactly rounded value:
+its CPU kernel sums exp(x - max) serially in 8 float lanes, which drifts by
+up to about 1.3e-5 relative on 32000-wide fp32 rows
+(``oracle.display_token_statistics_reference_order`` reproduces those
+outputs bit for bit).  A comparison against the reference's numbers
+therefore widens the 1e-5 per element by the reference's own measured drift
+at that element (``stats_tolerance_vs_reference``).
 """
 
 from __future__ import annotations
@@ -14,10 +24,17 @@ import torch
 
 import cases
 
+# float32 statistics: pure relative tolerance; the absolute floor only
+# covers results below the float32 normal range
+STATS_RTOL = 1e-5
+STATS_ATOL = 1e-30
+STATS_OPS = ("display_token_statistics", "display_token_statistics_with_repetition")
+
 # op -> per-output (rtol, atol); None = exact
 TOLERANCES: dict[str, list] = {
-    "display_token_statistics": [(2e-5, 2e-6), None, (2e-5, 2e-6)],
-    "display_token_statistics_with_repetition": [(2e-5, 2e-6), None, (2e-5, 2e-6)],
+    "display_token_statistics": [(STATS_RTOL, STATS_ATOL), None, (STATS_RTOL, STATS_ATOL)],
+    "display_token_statistics_with_repetition": [
+        (STATS_RTOL, STATS_ATOL), None, (STATS_RTOL, STATS_ATOL)],
     "refine_display_from_statistics": [None],
     "prefix_allocation_mask": [None],
     "rollout_slot_transition": [None] * 6,
@@ -95,3 +112,40 @@ def assert_matches(op: str, actual, expected, name: str, ambiguous=None) -> None
             torch.testing.assert_close(
                 a, e, rtol=tol[0], atol=tol[1], equal_nan=True, msg=f"{name}[{k}]"
             )
+
+
+def assert_stats_close(actual: torch.Tensor, expected: torch.Tensor, msg: str = "") -> None:
+    """float32 confidences against the exactly rounded value: pure relative
+    1e-5 (absolute floor 1e-30, below the float32 normal range)."""
+    torch.testing.assert_close(actual.detach().cpu(), expected.detach().cpu(), rtol=STATS_RTOL,
+                               atol=STATS_ATOL, equal_nan=True, msg=msg or None)
+
+
+def stats_drift(reference: torch.Tensor, exact: torch.Tensor) -> torch.Tensor:
+    """Per-element relative distance of the reference's float32 statistic
+    from the exactly rounded one (0 where either is not finite or the exact
+    value lies below the float32 normal range, which the absolute floor
+    covers)."""
+    r = reference.detach().cpu().double()
+    e = exact.detach().cpu().double()
+    ok = torch.isfinite(r) & torch.isfinite(e) & (e.abs() >= torch.finfo(torch.float32).tiny)
+    drift = torch.zeros_like(e)
+    drift[ok] = (r[ok] - e[ok]).abs() / e[ok].abs()
+    return drift
+
+
+def assert_stats_vs_reference(actual: torch.Tensor, reference: torch.Tensor,
+                              exact: torch.Tensor, msg: str = "") -> None:
+    """float32 statistics against the reference's own outputs: relative 1e-5
+    of the reference value, widened per element by the reference's own drift
+    from the exactly rounded value (triangle inequality: the device value is
+    within 1e-5 of the exact one, the reference within its drift)."""
+    a = actual.detach().cpu().double()
+    r = reference.detach().cpu().double()
+    tol = (STATS_RTOL + stats_drift(reference, exact)) * r.abs() + STATS_ATOL
+    both_nan = torch.isnan(a) & torch.isnan(r)
+    same_inf = torch.isinf(a) & (a == r)
+    bad = ~(both_nan | same_inf | ((a - r).abs() <= tol))
+    assert not bool(bad.any()), (
+        f"{msg}: {int(bad.sum())} of {bad.numel()} outside 1e-5 + reference drift; "
+        f"first at {int(torch.nonzero(bad.flatten())[0])}")

@@ -134,8 +134,8 @@ def test_vocab_sharded_records_equal_unsharded(world: int, dtype: torch.dtype) -
     got = torch.ops.cid_engine.display_combine_records(recs, idd, offs)
     unsharded = torch.ops.cid_engine.display_token_statistics(idd, lgd)
     assert torch.equal(got[1], unsharded[1])
-    torch.testing.assert_close(got[0], unsharded[0], rtol=2e-5, atol=2e-6, equal_nan=True)
-    torch.testing.assert_close(got[2], unsharded[2], rtol=2e-5, atol=2e-6, equal_nan=True)
+    torch.testing.assert_close(got[0], unsharded[0], rtol=compare.STATS_RTOL, atol=compare.STATS_ATOL, equal_nan=True)
+    torch.testing.assert_close(got[2], unsharded[2], rtol=compare.STATS_RTOL, atol=compare.STATS_ATOL, equal_nan=True)
     compare.assert_matches(STATS, got, oracle.display_token_statistics(ids, lg), "sharded")
     # the device records agree with the oracle's records
     orc = torch.stack([oracle.display_shard_records(ids, lg[..., offs[r]:offs[r + 1]], offs[r], V)

@@ -157,8 +157,8 @@ def test_lm_head_shard_records_combine_to_unsharded(world) -> None:
         for r in range(world)])
     c, p, u = cid_engine.display_combine_records(recs, ids.view(1, -1), offs)
     assert torch.equal(p.view(-1), pred)
-    torch.testing.assert_close(c.view(-1), conf, rtol=1e-5, atol=1e-8)
-    torch.testing.assert_close(u.view(-1), cur, rtol=1e-5, atol=1e-8)
+    torch.testing.assert_close(c.view(-1), conf, rtol=1e-5, atol=1e-30)
+    torch.testing.assert_close(u.view(-1), cur, rtol=1e-5, atol=1e-30)
 
 
 def test_lm_head_shard_records_validation() -> None:

@@ -4,8 +4,11 @@ For each case of ``tests/golden/cases.py`` the inputs are rebuilt, placed on
 ``cuda:0`` with their strides preserved, and run through
 ``torch.ops.cid_engine``; the outputs must match the CPU oracle on the same
 inputs with the tolerances of ``compare.py`` (exact for decisions, ids, masks
-and argmax).  Where the input digest matches the stored one, the reference's
-own golden outputs are checked too.
+and argmax; float32 statistics within a pure relative 1e-5 of the exactly
+rounded value).  Where the input digest matches the stored one, the
+reference's own golden outputs are checked too (statistics: within 1e-5 of
+the reference's value widened by the reference's own float32 summation drift
+at that element).
 """
 
 from __future__ import annotations
@@ -68,5 +71,21 @@ def test_cuda_matches_oracle(case: cases.Case) -> None:
     if isinstance(expected, torch.Tensor):
         expected = (expected,)
     compare.assert_matches(case.op, out, expected, case.name, _ambiguous(case))
-    if cases.digest(case.args) == entry["digest"]:
-        compare.assert_matches(case.op, out, entry["out"], case.name + "/golden", _ambiguous(case))
+    if cases.digest(case.args) != entry["digest"]:
+        return
+    if case.op in compare.STATS_OPS:
+        # argmax exactly; confidences within 1e-5 of the reference's own
+        # values, widened by the reference's drift from the exact value
+        compare.assert_matches(case.op, (out[0], out[1], out[2]),
+                               (expected[0], entry["out"][1], expected[2]),
+                               case.name + "/golden argmax")
+        for k in (0, 2):
+            enc = entry["out"][k]
+            a, r, e = out[k].cpu().flatten(), None, expected[k].flatten()
+            if "full" in enc:
+                r = enc["full"].flatten()
+            else:
+                a, e, r = a[:: enc["step"]], e[:: enc["step"]], enc["sample"].flatten()
+            compare.assert_stats_vs_reference(a, r, e, f"{case.name}/golden[{k}]")
+        return
+    compare.assert_matches(case.op, out, entry["out"], case.name + "/golden", _ambiguous(case))

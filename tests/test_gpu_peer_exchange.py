@@ -2,8 +2,10 @@
 one GPU: a one-rank exchange equals the record + combine path bit for bit
 over consecutive steps (both epoch parities), and a combine whose epoch no
 rank publishes gives up after its wait limit with a status bit and NaN
-statistics instead of hanging.  The multi-rank exchange over NVLink is
-checked in ``test_multi_gpu.py``."""
+statistics instead of hanging; from then on the exchange is poisoned (NaN at
+once, no wait) until the status word is cleared, and a flag two epochs ahead
+(a peer that moved on) is refused with its own bit.  The multi-rank exchange
+over NVLink is checked in ``test_multi_gpu.py``."""
 
 from __future__ import annotations
 
@@ -81,13 +83,61 @@ def test_unpublished_epoch_times_out_with_status() -> None:
         torch.cuda.synchronize()
         assert cid_engine.device_status(0) & cid_engine.STATUS_PEER_TIMEOUT
         assert bool(conf.isnan().all()) and bool(cur.isnan().all()) and bool((pred == 0).all())
+        # while the bit is set the exchange is poisoned: the next step
+        # writes NaN at once, without waiting
+        assert not ex.healthy()
+        got = ex.statistics(ids, logits, vocab_offset=0, total_vocab=V, shard_offsets=[0, V])
+        torch.cuda.synchronize()
+        assert bool(got[0].isnan().all()) and bool((got[1] == 0).all())
         cid_engine.device_status(0, reset=True)
-        # the exchange itself is unaffected: the next step still matches
+        # with the word cleared (one rank: no peer can be out of step) the
+        # exchange serves again
+        assert ex.healthy()
         got = ex.statistics(ids, logits, vocab_offset=0, total_vocab=V, shard_offsets=[0, V])
         exp = cid_engine.display_token_statistics(ids, logits)
         assert torch.equal(got[1], exp[1])
         torch.cuda.synchronize()
         assert cid_engine.device_status(0) == 0
+    finally:
+        ex.close()
+
+
+def test_peer_out_of_step_sets_its_bit() -> None:
+    """A flag two epochs ahead of the combine's epoch (a peer that gave up
+    waiting and moved on) is refused at once: NaN statistics and
+    STATUS_PEER_OUT_OF_STEP, no wait."""
+    import ctypes
+
+    import cid_engine
+    from cid_engine import parallel
+
+    dev = torch.device("cuda", 0)
+    B, L, V = 1, 64, 512
+    ex = parallel.PeerRecordExchange(B * L)
+    try:
+        g = torch.Generator(device=dev).manual_seed(6)
+        logits = torch.randn(B, L, V, generator=g, device=dev)
+        ids = torch.randint(V, (B, L), generator=g, device=dev)
+        for _ in range(3):
+            ex.statistics(ids, logits, vocab_offset=0, total_vocab=V, shard_offsets=[0, V])
+        torch.cuda.synchronize()
+        cid_engine.device_status(0, reset=True)
+        conf = torch.empty(B, L, device=dev)
+        pred = torch.empty(B, L, dtype=torch.int64, device=dev)
+        cur = torch.empty(B, L, device=dev)
+        offs = (ctypes.c_int64 * 2)(0, V)
+        rc = ex.lib.cid_display_combine_inbox(
+            ex.own, 1, offs, ids.data_ptr(), B * L, B * L, ex.epoch - 2, 1.0, conf.data_ptr(),
+            pred.data_ptr(), cur.data_ptr(), cid_engine._C.status_word_ptr(0),
+            torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        st = cid_engine.device_status(0, reset=True)
+        assert st & cid_engine.STATUS_PEER_OUT_OF_STEP
+        assert not st & cid_engine.STATUS_PEER_TIMEOUT
+        assert bool(conf.isnan().all()) and bool((pred == 0).all())
+        with pytest.raises(ValueError, match="wait_seconds"):
+            parallel.PeerRecordExchange(4, wait_seconds=120.0)
     finally:
         ex.close()
 
@@ -124,7 +174,7 @@ def test_one_rank_exchange_from_lm_head_records() -> None:
         c, p, u = ex.from_records(rec, ids, shard_offsets=[0, V])
         e_c, e_p, e_u = cid_engine.lm_head_display_statistics(ids, hid, wgt)
         assert torch.equal(p, e_p)
-        torch.testing.assert_close(c, e_c, rtol=1e-5, atol=1e-8)
-        torch.testing.assert_close(u, e_u, rtol=1e-5, atol=1e-8)
+        torch.testing.assert_close(c, e_c, rtol=1e-5, atol=1e-30)
+        torch.testing.assert_close(u, e_u, rtol=1e-5, atol=1e-30)
     finally:
         ex.close()

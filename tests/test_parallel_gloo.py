@@ -44,6 +44,7 @@ def _worker(rank: int, world: int, port: int, dtype_name: str, result_dir: str) 
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
     try:
         import cases
+        import compare
         from cid_engine import parallel
         from oracle import oracle
 
@@ -63,8 +64,8 @@ def _worker(rank: int, world: int, port: int, dtype_name: str, result_dir: str) 
             c, p, u = oracle.display_combine_records(gathered, tid, offs)
             e = oracle.display_token_statistics(tid, lg)
             assert torch.equal(p, e[1])
-            torch.testing.assert_close(c, e[0], rtol=2e-5, atol=2e-6, equal_nan=True)
-            torch.testing.assert_close(u, e[2], rtol=2e-5, atol=2e-6, equal_nan=True)
+            torch.testing.assert_close(c, e[0], rtol=compare.STATS_RTOL, atol=compare.STATS_ATOL, equal_nan=True)
+            torch.testing.assert_close(u, e[2], rtol=compare.STATS_RTOL, atol=compare.STATS_ATOL, equal_nan=True)
         Path(result_dir, f"ok{rank}").write_text("ok")
     finally:
         dist.destroy_process_group()
