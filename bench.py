@@ -230,14 +230,43 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 
+def _reference_inputs(args):
+    """The CPU sample's inputs: rows of the B200 arm's own workload.  With
+    ``--sample-gen cuda`` they are generated on the GPU by the same
+    generators as the B200 arm (so the values are identical) and copied to
+    the host; otherwise on the host.  Only plain torch runs here: this
+    process must not load this repository's extension."""
+    import torch
+
+    dev = "cuda" if args.sample_gen == "cuda" and torch.cuda.is_available() else "cpu"
+    B, L, V = args.sample_b, args.sample_l, args.sample_v
+    if dev == "cpu" and B * L * V > (1 << 28):
+        # host generation runs at ~25 M values/s: without a GPU, keep the
+        # sample to one sequence's first 1024 rows
+        B, L = 1, min(L, 1024)
+    if args.sample_world:  # vocabulary-parallel workload: its shards side by side
+        W = args.sample_world
+        parts, ids = [], None
+        for r in range(W):
+            i, lg, _ = sharded_display_inputs(SHARDED["B"], SHARDED["L"], V, r, W, 3, dev)
+            parts.append(lg[:B, :L].cpu())
+            ids = i[:B, :L].cpu()
+            del lg
+        return ids, torch.cat(parts, dim=-1), dev
+    ids, logits = display_inputs(B, L, V, seed=1, device=dev)
+    return ids.cpu(), logits.cpu(), dev
+
+
 def cpu_reference_worker(args) -> None:
     import torch
 
     lib = ROOT / "oracle" / "_ref" / "libcid_engine_ref.so"
+    ids, logits, gen = _reference_inputs(args)
+    if torch.cuda.is_available():
+        torch.cuda.empty_cache()
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    B, L, V = args.sample_b, args.sample_l, args.sample_v
-    ids, logits = display_inputs(B, L, V, seed=1, device="cpu")
+    B, L, V = logits.shape
     if lib.exists():
         torch.ops.load_library(str(lib))
         kind = "reference"
@@ -269,17 +298,21 @@ def cpu_reference_worker(args) -> None:
         "value": nbytes / per / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
         "ms_per_step": per * 1e3, "reps": len(times),
         "sample": f"stats+refine on logits bf16 [{B},{L},{V}] ({nbytes / 1e9:.3f} GB) per step, "
-                  f"median of {len(times)} reps",
+                  f"median of {len(times)} reps (inputs generated on {gen})",
     }))
 
 
-def run_cpu_baseline(sample=(1, 1024, 128256), seconds=10.0) -> dict | None:
+def run_cpu_baseline(sample=(1, 1024, 128256), seconds=10.0, *, gen="cpu", world=0,
+                     min_reps=3) -> dict | None:
     cmd = [sys.executable, str(ROOT / "bench.py"), "--cpu-worker", "--sample-b", str(sample[0]),
            "--sample-l", str(sample[1]), "--sample-v", str(sample[2]),
-           "--cpu-seconds", str(seconds)]
-    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+           "--cpu-seconds", str(seconds), "--cpu-min-reps", str(min_reps),
+           "--sample-gen", gen, "--sample-world", str(world)]
+    env = dict(os.environ)
+    if gen == "cpu":
+        env["CUDA_VISIBLE_DEVICES"] = ""
     try:
-        res = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600)
+        res = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=900)
         return json.loads(res.stdout.strip().splitlines()[-1])
     except Exception as exc:  # the baseline is reported, never fatal
         return {"error": f"{type(exc).__name__}: {exc}"[:300]}
@@ -358,9 +391,11 @@ def bench_single(args) -> dict:
     del logits
     torch.cuda.empty_cache()
 
+    vp1 = None if args.no_loop else bench_vocab_parallel_n1(dev)
     loop = None if args.no_loop else bench_refine_loop(dev)
     small = None if args.no_loop else bench_small_workloads(dev)
     lm_head = None if args.no_loop else bench_lm_head(dev)
+    decode = None if args.no_loop else bench_decode_and_reference_cuda(dev)
     cpu = None if args.no_cpu_baseline else run_cpu_baseline(seconds=args.cpu_seconds)
     line = {
         "metric": METRIC,
@@ -388,10 +423,47 @@ def bench_single(args) -> dict:
         "clocks": clocks,
         "cpu_baseline": cpu,
         "refine_loop": loop,
+        "vocab_parallel_n1": vp1,
         "small_workloads": small,
         "lm_head": lm_head,
+        "decode_rows": None if decode is None else decode["decode_rows"],
+        "reference_cuda": None if decode is None else decode["reference_cuda"],
     }
     return line
+
+
+def bench_vocab_parallel_n1(dev, steps: int = 20) -> dict:
+    """The vocabulary-parallel workload, logits bf16 [64, 4096, 152064]
+    (79.7 GB), on one GPU: statistics + refinement of the whole tensor, the
+    one-GPU anchor of the multi-GPU lines (same problem, same generator as
+    rank 0 of one)."""
+    import torch
+
+    B, L, V = SHARDED["B"], SHARDED["L"], SHARDED["V"]
+    ids, logits, _ = sharded_display_inputs(B, L, V, 0, 1, 3, dev)
+    ops = torch.ops.cid_engine
+    stream = torch.cuda.current_stream()
+
+    def step(ev):
+        if ev is not None:
+            ev[0].record(stream)
+        c, p, u = ops.display_token_statistics(ids, logits)
+        if ev is not None:
+            ev[1].record(stream)
+        ops.refine_display_from_statistics(ids, c, p, u, MASK_ID, EOS_ID, REVEAL, REVISION, MARGIN)
+
+    total_ms, kern = time_device_steps(step, steps, 3, stream)
+    ms = total_ms / steps
+    kern_ms = statistics.mean(kern)
+    nbytes = logits.numel() * logits.element_size()
+    peak, peak_kind = _peaks()
+    alg = nbytes + B * L * (8 + 4 + 8 + 4)
+    del logits
+    torch.cuda.empty_cache()
+    return {"workload": "display stats + refine, logits bf16 [64,4096,152064] on one GPU",
+            "value": round(nbytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "steps": steps, "kernel_ms": round(kern_ms, 4),
+            "kernel_frac": round(alg / (kern_ms * 1e-3) / 1e9 / peak, 4), "peak_kind": peak_kind}
 
 
 def bench_e2e(ids_dev: Tensor, logits_dev: Tensor, *, steps: int, warmup: int, mask_id: int,
@@ -489,8 +561,8 @@ def bench_refine_loop(dev) -> dict:
             "logits_GBps": round(logits_bytes / (ms * 1e-3) / 1e9, 1),
             "roofline_steps_per_s": round(peak * 1e9 / logits_bytes, 1),
             "snapshot_d2h_bytes_per_step": snap_bytes,
-            "launches_per_step": 5,
-            "torch_copies_per_step": 3}
+            "launches_per_step": 4,
+            "device_copies_per_step": {"graph": 2, "eager": 0}}
 
 
 def _graph_time_ms(fn, reps: int) -> float:
@@ -549,8 +621,8 @@ def bench_small_workloads(dev) -> dict:
         state["k"] += 1
         c, p, u = ops.display_token_statistics(ids, lg)
         ops.refine_display_from_statistics(ids, c, p, u, MASK_ID, EOS_ID, REVEAL, REVISION, MARGIN)
-        ops.rollout_slot_transition(occ, al, life, rv, life, 0.5, 8, 3)
-        ops.live_slot_occupancy(occ, life, 3)
+        # slot rollout with the live occupancy of its next state, one kernel
+        ops.rollout_slot_transition_with_live(occ, al, life, rv, life, 0.5, 8, 3)
         ops.thought_corrupt_from_epsilon(*th)
 
     ms1 = _graph_time_ms(chain_step, 64)
@@ -598,7 +670,7 @@ def bench_small_workloads(dev) -> dict:
         "chain_f32_4x256x32000": {"workload": "fp32 [4,256,32000] stats+refine, 32 slots rollout+live, "
                                    "thought [4,32,512]", "us_per_step": round(ms1 * 1e3, 2),
                        "logits_GBps": round(131_072_000 / (ms1 * 1e-3) / 1e9, 1),
-                       "launches_per_step": 5, "timing": "CUDA graph, 64 steps"},
+                       "launches_per_step": 4, "timing": "CUDA graph, 64 steps"},
         "masked_diffusion_64x2048": {"workload": "ids [64,2048], mask id 50256",
                                   "us_per_call": round(ms3 * 1e3, 3),
                                   "GBps": round(2_753_032 / (ms3 * 1e-3) / 1e9, 1),
@@ -617,6 +689,244 @@ def bench_small_workloads(dev) -> dict:
                               "problems_per_s": round(4096 / (ms_la * 1e-3)),
                               "timing": "CUDA graph, 200 calls"},
     }
+
+
+# ---------------------------------------------------------------------------
+# decode shapes and the reference's own CUDA kernels (secondary GPU bar)
+# ---------------------------------------------------------------------------
+
+# the reference's published microbenchmark shapes: display rows x 155136-token
+# vocabulary, bf16 logits, one sequence; refinement at 64 display rows in
+# four scenarios (all masked / EOS at 16 or 48, revision off or on)
+DECODE = dict(V=155136, rows=(32, 64, 128, 256), refine_rows=64)
+DECODE_SCENARIOS = (("all masked, no revision", None, 0.0),
+                    ("EOS at 16, no revision", 16, 0.0),
+                    ("EOS at 16, revision=1", 16, 1.0),
+                    ("EOS at 48, revision=1", 48, 1.0))
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _ring(make, nbytes: int) -> list:
+    """Enough copies of an input that one pass over them is twice the L2."""
+    n = max(2, -(-2 * L2_BYTES // max(1, nbytes)))
+    return [make(k) for k in range(n)]
+
+
+def _events_time_ms(fn, reps: int) -> float:
+    """Per-call device time of `fn` issued eagerly `reps` times (for calls
+    that synchronise inside and cannot be captured)."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def decode_logits(rows: int, k: int, dev):
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(20 + 1000 * rows + k)
+    lg = torch.randn((1, rows, DECODE["V"]), generator=g, device=dev, dtype=torch.bfloat16)
+    return lg.mul_(2.0)
+
+
+def decode_ids(rows: int, eos_at, dev):
+    import torch
+
+    g = torch.Generator(device=dev).manual_seed(30 + rows)
+    ids = torch.randint(2, DECODE["V"], (1, rows), generator=g, device=dev)
+    if eos_at is None:
+        ids.fill_(MASK_ID)
+    else:
+        ids[torch.rand((1, rows), generator=g, device=dev) < 0.5] = MASK_ID
+        ids[0, eos_at] = EOS_ID
+        ids[0, eos_at + 1:] = MASK_ID
+    return ids
+
+
+def decode_suite(dev, graphs: bool) -> dict:
+    """Statistics of [1, rows, 155136] bf16 logits for the published row
+    counts, and statistics + refinement at 64 rows, through whichever
+    ``torch.ops.cid_engine`` this process has loaded.  Inputs rotate over
+    copies totalling twice the L2.  ``graphs``: time as CUDA-graph replays
+    (statistics + refinement then runs without a host round trip)."""
+    import torch
+
+    ops = torch.ops.cid_engine
+    timer = _graph_time_ms if graphs else _events_time_ms
+    out = {"stats": {}, "stats_refine": {}}
+    for rows in DECODE["rows"]:
+        nbytes = rows * DECODE["V"] * 2
+        ring = _ring(lambda k: decode_logits(rows, k, dev), nbytes)
+        ids = decode_ids(rows, 16, dev)
+        st = {"k": 0}
+
+        def call():
+            lg = ring[st["k"] % len(ring)]
+            st["k"] += 1
+            ops.display_token_statistics(ids, lg)
+
+        out["stats"][rows] = timer(call, 20 * len(ring)) * 1e3
+        del ring
+    rows = DECODE["refine_rows"]
+    ring = _ring(lambda k: decode_logits(rows, k, dev), rows * DECODE["V"] * 2)
+    for name, eos_at, revision in DECODE_SCENARIOS:
+        ids = decode_ids(rows, eos_at, dev)
+        st = {"k": 0}
+
+        def step():
+            lg = ring[st["k"] % len(ring)]
+            st["k"] += 1
+            c, p, u = ops.display_token_statistics(ids, lg)
+            ops.refine_display_from_statistics(ids, c, p, u, MASK_ID, EOS_ID, REVEAL, revision,
+                                               MARGIN)
+
+        out["stats_refine"][name] = timer(step, 10 * len(ring)) * 1e3
+    del ring
+    torch.cuda.empty_cache()
+    return out
+
+
+def secondary_suite(dev, graphs: bool) -> dict:
+    """Per-call device time (us) of the operators the reference also ships as
+    CUDA kernels, on the benchmark shapes, through whichever
+    ``torch.ops.cid_engine`` this process has loaded."""
+    import torch
+
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import cases
+
+    ops = torch.ops.cid_engine
+    timer = _graph_time_ms if graphs else _events_time_ms
+    res = {}
+    # statistics of the [32, 1024, 128256] display step (8.4 GB > L2)
+    ids, logits = display_inputs(STEP["B"], STEP["L"], STEP["V"], seed=1, device=dev)
+    res["stats_32x1024x128256_ms"] = _events_time_ms(
+        lambda: ops.display_token_statistics(ids, logits), 10)
+    del logits
+    torch.cuda.empty_cache()
+    md = [a.to(dev) if isinstance(a, torch.Tensor) else a for a in cases.masked_diffusion_64x2048()]
+    res["masked_diffusion_64x2048_us"] = timer(
+        lambda: ops.masked_diffusion_corrupt_from_random(*md), 1000) * 1e3
+    th = [t.to(dev) for t in cases.thought_4x32x512()]
+    res["thought_corruption_4x32x512_us"] = timer(
+        lambda: ops.thought_corrupt_from_epsilon(*th), 1000) * 1e3
+    # slot kernels at the decode loop's 256 x 128 slots
+    g = torch.Generator().manual_seed(40)
+    B, S = LOOP["B"], LOOP["S"]
+    occ = (torch.rand(B, S, 1, generator=g) < 0.4).float().to(dev)
+    al = torch.randn(B, S, generator=g).to(dev)
+    lc = torch.randn(B, S, LOOP["F"], generator=g).to(dev)
+    rv = torch.randn(B, S, LOOP["Rv"], generator=g).to(dev)
+    il = torch.randn(B, S, LOOP["F"], generator=g).to(dev)
+    res["rollout_256x128_us"] = timer(
+        lambda: ops.rollout_slot_transition(occ, al, lc, rv, il, 0.5, 8, 3), 1000) * 1e3
+    # prefix allocation over 128 slots, the reference's published cases
+    for dt in (torch.float32, torch.bfloat16):
+        for b in (1, 8):
+            o = (torch.rand(b, 128, generator=g) < 0.4).to(dt).to(dev)
+            lg = torch.randn(b, 128, generator=g).to(dt).to(dev)
+            res[f"prefix_allocation_{str(dt)[6:]}_b{b}_us"] = timer(
+                lambda o=o, lg=lg: ops.prefix_allocation_mask(o, lg, 0.5, 8), 1000) * 1e3
+    # snapshot of 128 slots x 4096 semantic dims, bf16 (published case)
+    sem = torch.randn(1, 128, 4096, generator=g).to(torch.bfloat16).to(dev)
+    roles = torch.randn(1, 128, 6, generator=g).to(torch.bfloat16).to(dev)
+    unc = torch.rand(1, 128, 1, generator=g).to(torch.bfloat16).to(dev)
+    noise = torch.randn(1, 128, 1, generator=g).to(torch.bfloat16).to(dev)
+    life = torch.randn(1, 128, 4, generator=g).to(torch.bfloat16).to(dev)
+    sel = (torch.rand(1, 128, generator=g) < 0.5).to(dev)
+    idx = torch.randint(0, 4096, (12,), generator=g).to(dev)
+    res["snapshot_128x4096_bf16_us"] = timer(
+        lambda: ops.materialize_cell_snapshot(sem, roles, unc, noise, life, sel, idx), 1000) * 1e3
+    torch.cuda.empty_cache()
+    return res
+
+
+def ref_cuda_worker(args) -> None:
+    """The reference's own CUDA kernels (compiled unchanged for sm_100a by
+    ``make -C oracle ref-cuda``), in a process that never loads this
+    repository's extension."""
+    import torch
+
+    lib = ROOT / "oracle" / "_ref" / "libcid_engine_ref_cuda.so"
+    if not lib.exists():
+        print(json.dumps({"error": "oracle/_ref/libcid_engine_ref_cuda.so not built"}))
+        return
+    torch.ops.load_library(str(lib))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    out = {"decode": decode_suite(dev, graphs=False), "secondary": secondary_suite(dev, graphs=False)}
+    print(json.dumps(out))
+
+
+def run_ref_cuda() -> dict:
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--ref-cuda-worker"]
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+        return json.loads(res.stdout.strip().splitlines()[-1])
+    except Exception as exc:  # a secondary bar is reported, never fatal
+        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+
+
+def bench_decode_and_reference_cuda(dev) -> dict:
+    """Decode shapes and the secondary GPU bar: this repository's kernels
+    (CUDA-graph replays; statistics + refinement without a host round trip,
+    and eagerly) against the reference's own CUDA kernels on the same box,
+    shapes and inputs (eager: its refinement is a host round trip, and CUDA
+    graphs would only flatter its launch-bound kernels)."""
+    ours = decode_suite(dev, graphs=True)
+    ours_eager = decode_suite(dev, graphs=False)
+    sec = secondary_suite(dev, graphs=True)
+    ref = run_ref_cuda()
+    peak, _ = _peaks()
+    rdec = ref.get("decode", {}) if isinstance(ref, dict) else {}
+    rsec = ref.get("secondary", {}) if isinstance(ref, dict) else {}
+
+    def ratio(r, o):
+        return None if r is None or not o else round(r / o, 2)
+
+    stats = []
+    for rows in DECODE["rows"]:
+        us = ours["stats"][rows]
+        r = rdec.get("stats", {}).get(str(rows))
+        nbytes = rows * DECODE["V"] * 2 + rows * 32
+        gbps = nbytes / (us * 1e-6) / 1e9
+        stats.append({"rows": rows, "us": round(us, 2), "us_eager": round(ours_eager["stats"][rows], 2),
+                      "GBps": round(gbps, 1), "frac": round(gbps / peak, 4),
+                      "reference_cuda_us": None if r is None else round(r, 2),
+                      "speedup_vs_reference_cuda": ratio(r, us)})
+    refine = []
+    for name, _, _ in DECODE_SCENARIOS:
+        us = ours["stats_refine"][name]
+        r = rdec.get("stats_refine", {}).get(name)
+        refine.append({"scenario": name, "us": round(us, 2),
+                       "us_eager": round(ours_eager["stats_refine"][name], 2),
+                       "reference_cuda_us": None if r is None else round(r, 2),
+                       "speedup_vs_reference_cuda": ratio(r, us)})
+    secondary = {}
+    for k, v in sec.items():
+        r = rsec.get(k)
+        secondary[k] = {"ours": round(v, 3), "reference_cuda": None if r is None else round(r, 3),
+                        "speedup": ratio(r, v)}
+    return {"decode_rows": {"workload": "display statistics, logits bf16 [1, rows, 155136]; "
+                                        "statistics + refinement at 64 rows",
+                            "timing": "ours: CUDA-graph replays (us), and eager (us_eager); "
+                                      "reference: eager, separate process; inputs rotate over "
+                                      "copies totalling 2x L2",
+                            "stats": stats, "stats_refine_64": refine},
+            "reference_cuda": {"what": "the reference's csrc/cuda kernels compiled unchanged for "
+                                       "sm_100a (oracle/Makefile ref-cuda), same box, same inputs",
+                               "timing": "ours: CUDA-graph replays (eager for the 8.4 GB "
+                                         "statistics); reference: eager",
+                               "ops": secondary,
+                               "error": ref.get("error") if isinstance(ref, dict) else None}}
 
 
 def bench_lm_head(dev) -> dict:
@@ -688,12 +998,14 @@ def bench_reference(args, world: int = 1) -> dict:
     vocabulary stands for it)."""
     if world > 1:
         B, L, V = SHARDED["B"], SHARDED["L"], SHARDED["V"]
-        res = run_cpu_baseline(sample=(1, 512, V), seconds=args.cpu_seconds)
+        # 8 of the 64 sequences (10 GB), every rank's shard side by side
+        res = run_cpu_baseline(sample=(8, L, V), seconds=1.0, gen="cuda", world=world)
         workload = "vocab-parallel display stats + refine, logits bf16 [64,4096,152064]"
         scaling = "strong"
     else:
         B, L, V = STEP["B"], STEP["L"], STEP["V"]
-        res = run_cpu_baseline(seconds=args.cpu_seconds)
+        # the whole [32, 1024, 128256] step (8.4 GB), three timed reps
+        res = run_cpu_baseline(sample=(B, L, V), seconds=1.0, gen="cuda")
         workload = "display stats + refine, logits bf16 [32,1024,128256]"
         scaling = "weak"
     val = res.get("value") if res else None
@@ -728,9 +1040,8 @@ def sharded_display_inputs(B, L, V, rank, world, seed, device):
     """This rank's vocabulary shard of the [64, 4096, 152064] logits: bf16(2 N(0,1))
     with a +8 peak in 5% of rows at a column drawn once for all ranks."""
     import torch
-    from cid_engine.parallel import shard_offsets
 
-    offs = shard_offsets(V, world)
+    offs = [r * V // world for r in range(world + 1)]  # cid_engine.parallel.shard_offsets
     lo, hi = offs[rank], offs[rank + 1]
     g = torch.Generator(device=device).manual_seed(seed * 1000 + rank)
     logits = torch.randn((B, L, hi - lo), generator=g, device=device, dtype=torch.bfloat16)
@@ -755,15 +1066,16 @@ def sharded_display_inputs(B, L, V, rank, world, seed, device):
 def e2e_vocab_parallel(ids: Tensor, logits: Tensor, offs: list[int], rank: int, *, batch: int,
                        steps: int, warmup: int) -> dict:
     """End-to-end vocabulary-parallel step through the public API from pinned
-    host memory on every rank: per step the ids and this rank's logits shard
-    (the first ``batch`` sequences) go host->device, overlapped in chunks with
-    the record kernel (``HostStatisticsPipeline``), the records are
-    all-gathered and combined, the rows refined and the refined ids read
-    back.  Device time, max over ranks."""
+    host memory on every rank, on the headline path: per step the ids and
+    this rank's logits shard (the first ``batch`` sequences) go host->device,
+    overlapped in chunks with the record kernel (``HostStatisticsPipeline``
+    over ``display_shard_records``), the records go into every rank's inbox
+    through the ``PeerRecordExchange`` and are combined there, the rows are
+    refined and the refined ids read back.  Device time, max over ranks."""
     import torch
     import torch.distributed as dist
     from cid_engine.host_pipeline import HostStatisticsPipeline
-    from cid_engine.parallel import gather_records
+    from cid_engine.parallel import PeerRecordExchange
 
     dev = logits.device
     V, lo = offs[-1], offs[rank]
@@ -777,28 +1089,33 @@ def e2e_vocab_parallel(ids: Tensor, logits: Tensor, offs: list[int], rank: int, 
     ops = torch.ops.cid_engine
     pipe = HostStatisticsPipeline(*sub.shape, dtype=sub.dtype, device=dev,
                                   reduce=lambda i, x: ops.display_shard_records(i, x, lo, V))
+    ex = PeerRecordExchange(ids_h.numel())
 
     def step():
         i = ids_h.to(dev, non_blocking=True)
         rec = pipe.statistics(i, logits_h)
-        c, p, u = ops.display_combine_records(gather_records(rec), i, offs)
-        refined = ops.refine_display_from_statistics(i, c, p, u, 0, 1, 0.25, 0.1, 0.05)
+        c, p, u = ex.from_records(rec.view(-1, 4), i, shard_offsets=offs)
+        refined = ops.refine_display_from_statistics(i, c, p, u, MASK_ID, EOS_ID, REVEAL,
+                                                     REVISION, MARGIN)
         out_h.copy_(refined, non_blocking=True)
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    t = torch.tensor([a.elapsed_time(b) / steps], device=dev, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t[0])
+    try:
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    finally:
+        ex.close()
     total = batch * ids.shape[1] * V * logits.element_size()
     ids_bytes = ids_h.numel() * ids_h.element_size()
     del pipe, logits_h
@@ -807,8 +1124,96 @@ def e2e_vocab_parallel(ids: Tensor, logits: Tensor, offs: list[int], rank: int, 
             "d2h_bytes_per_step": world * ids_bytes,
             "ms_per_step": round(ms, 3), "steps": steps,
             "sample": f"first {batch} of {ids.shape[0]} sequences on every rank (bytes: all ranks)",
-            "api": "cid_engine.host_pipeline (display_shard_records) + parallel.gather_records + "
-                   "display_combine_records + refine_display_from_statistics"}
+            "api": "cid_engine.host_pipeline (display_shard_records) + "
+                   "parallel.PeerRecordExchange.from_records + refine_display_from_statistics"}
+
+
+def sharded_parity(ids: Tensor, logits: Tensor, offs: list[int], stats, rows: int = 256) -> dict:
+    """Outside the timed region: the shard slices of ``rows`` rows spread
+    over the tensor are gathered to every rank, reassembled into full
+    vocabulary rows, and the unsharded single-GPU statistics of those rows
+    are compared with the combined ones (argmax exactly; confidences within
+    a pure relative 1e-5)."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size()
+    dev = logits.device
+    n = ids.numel()
+    sel = torch.linspace(0, n - 1, rows, device=dev).long()
+    width = max(offs[r + 1] - offs[r] for r in range(world))
+    mine = torch.zeros((rows, width), dtype=logits.dtype, device=dev)
+    flat = logits.reshape(n, -1)
+    mine[:, : flat.shape[1]] = flat[sel]
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(parts, mine)
+    full = torch.cat([parts[r][:, : offs[r + 1] - offs[r]] for r in range(world)], dim=1)
+    sub_ids = ids.reshape(-1)[sel].view(1, rows)
+    e_c, e_p, e_u = torch.ops.cid_engine.display_token_statistics(sub_ids, full.view(1, rows, -1))
+    c, p, u = (t.reshape(-1)[sel] for t in stats)
+    argmax_ok = bool(torch.equal(p, e_p.view(-1)))
+    rel = max(float(((c - e_c.view(-1)).abs() / e_c.view(-1).abs()).max()),
+              float(((u - e_u.view(-1)).abs() / e_u.view(-1).abs().clamp_min(1e-30)).max()))
+    return {"rows": rows, "ok": argmax_ok and rel <= 1e-5, "argmax_exact": argmax_ok,
+            "max_rel_diff": rel,
+            "against": "display_token_statistics of the reassembled unsharded rows on one GPU"}
+
+
+def bench_sharded_loop(rank: int, world: int, dev) -> dict:
+    """Decode loop batch-sharded over the ranks: 256 / N sequences of 512
+    positions over 32000 tokens per rank, 128 slots, 64 graph-replayed
+    steps, no collective; steps/s of the whole job (max over ranks)."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+    from cid_engine.loop import DisplayRefineLoop
+
+    B = LOOP["B"]
+    per = B // world
+    lo, hi = rank * per, (rank + 1) * per
+    ring = [loop_logits(k, dev)[lo:hi].contiguous() for k in range(3)]
+    torch.cuda.empty_cache()
+    ids0, slot = loop_state(dev)
+    fields = {f.name: getattr(slot, f.name) for f in dataclasses.fields(slot)}
+    for name, val in fields.items():
+        if isinstance(val, torch.Tensor) and name != "semantic_indices":
+            fields[name] = val[lo:hi].contiguous()
+    slot = type(slot)(**fields)
+    ids0 = ids0[lo:hi].contiguous()
+    loop = DisplayRefineLoop(ids0, ring, slots=slot, host_snapshots=4, use_graphs=True,
+                             mask_token_id=MASK_ID, eos_token_id=EOS_ID, reveal_fraction=REVEAL,
+                             revision_fraction=REVISION, revision_margin=MARGIN)
+    try:
+        loop.run(3)
+        loop.drain()
+        loop.reset(ids0, slot.occupancy)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = LOOP["steps"]
+        a.record()
+        loop.run(steps)
+        b.record()
+        torch.cuda.synchronize()
+        loop.drain()
+    finally:
+        loop.close()
+    t = torch.tensor([a.elapsed_time(b) / steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0])
+    peak, _ = _peaks()
+    logits_bytes = B * LOOP["L"] * LOOP["V"] * 2
+    del ring
+    torch.cuda.empty_cache()
+    return {"workload": f"refine loop B=256 L=512 V=32000 bf16, S=128, 64 steps, "
+                        f"{per} sequences per rank",
+            "api": "cid_engine.DisplayRefineLoop (CUDA-graph replay)",
+            "graph_steps_per_s": round(1e3 / ms, 2), "graph_ms_per_step": round(ms, 4),
+            "logits_GBps": round(logits_bytes / (ms * 1e-3) / 1e9, 1),
+            "roofline_steps_per_s": round(world * peak * 1e9 / logits_bytes, 1),
+            "scaling": "strong (256 sequences in total), no collective", "timing": "max over ranks"}
 
 
 def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_baseline) -> dict:
@@ -825,21 +1230,26 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     try:
-        B, L, V = 64, 4096, 152064
+        B, L, V = SHARDED["B"], SHARDED["L"], SHARDED["V"]
         ids, logits, offs = sharded_display_inputs(B, L, V, rank, world, 3, dev)
         peers = getattr(args, "exchange", "peers") == "peers"
-        ex = PeerRecordExchange(B * L, wait_seconds=30.0) if peers else None
+        ex = PeerRecordExchange(B * L) if peers else None
+        ops = torch.ops.cid_engine
 
         def step(ev):
             if ex is None:
-                vocab_parallel_refine(ids, logits, total_vocab=V, mask_token_id=0, eos_token_id=1,
-                                      reveal_fraction=0.25, revision_fraction=0.1,
-                                      revision_margin=0.05, timing=ev)
-                return
+                vocab_parallel_refine(ids, logits, total_vocab=V, mask_token_id=MASK_ID,
+                                      eos_token_id=EOS_ID, reveal_fraction=REVEAL,
+                                      revision_fraction=REVISION, revision_margin=MARGIN,
+                                      timing=ev)
+                return None
             c, p, u = ex.statistics(ids, logits, vocab_offset=offs[rank], total_vocab=V,
                                     shard_offsets=offs, timing=ev)
-            torch.ops.cid_engine.refine_display_from_statistics(ids, c, p, u, 0, 1, 0.25, 0.1,
-                                                                0.05)
+            ops.refine_display_from_statistics(ids, c, p, u, MASK_ID, EOS_ID, REVEAL, REVISION,
+                                               MARGIN)
+            if ev is not None and len(ev) > 3:
+                ev[3].record()
+            return c, p, u
 
         K, W = args.steps, args.warmup
         for _ in range(W):
@@ -848,31 +1258,54 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
         dist.barrier()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                 for _ in range(K)]
+        nev = 4 if peers else 2
+        evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(nev)) for _ in range(K)]
         with ClockSampler(local) as clk:
             clk.mark_start()
             a.record()
             for k in range(K):
-                step(pairs[k])
+                step(evs[k])
             b.record()
             torch.cuda.synchronize()
             clk.mark_end()
         dist.barrier()
         torch.cuda.synchronize()
         ms_local = a.elapsed_time(b) / K
-        kern_local = pystats.mean(x.elapsed_time(y) for x, y in pairs)
+        kern_local = pystats.mean(e[0].elapsed_time(e[1]) for e in evs)
+        stage = [kern_local]
+        if peers:
+            stage += [pystats.mean(e[1].elapsed_time(e[2]) for e in evs),
+                      pystats.mean(e[2].elapsed_time(e[3]) for e in evs)]
         t = torch.tensor([ms_local, kern_local], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, kern_ms = float(t[0]), float(t[1])
+        st = torch.tensor([ms_local, *stage], device=dev, dtype=torch.float64)
+        st_all = [torch.empty_like(st) for _ in range(world)]
+        dist.all_gather(st_all, st)
+        stages = [{"rank": r, "step_ms": round(float(x[0]), 4), "records_ms": round(float(x[1]), 4),
+                   **({"combine_ms": round(float(x[2]), 4), "refine_ms": round(float(x[3]), 4)}
+                      if peers else {})} for r, x in enumerate(st_all)]
+        # correctness outside the timed region: one more step's statistics
+        # against the unsharded statistics of 256 reassembled rows
+        if peers:
+            stats = step(None)
+        else:
+            from cid_engine.parallel import vocab_parallel_statistics
+
+            stats = vocab_parallel_statistics(ids, logits, total_vocab=V)
+        torch.cuda.synchronize()
+        parity = sharded_parity(ids, logits, offs, stats)
         if ex is not None:
             ex.close()
         e2e = None
         if not args.no_e2e:
-            e2e = e2e_vocab_parallel(ids, logits, offs, rank, batch=4,
-                                     steps=max(3, min(K, args.e2e_steps)), warmup=2)
+            e2e = e2e_vocab_parallel(ids, logits, offs, rank, batch=16,
+                                     steps=max(20, args.e2e_steps), warmup=2)
         total_bytes = B * L * V * 2
         shard_bytes = logits.numel() * 2
+        del logits, stats
+        torch.cuda.empty_cache()
+        loop = None if args.no_loop else bench_sharded_loop(rank, world, dev)
         peak, peak_kind = peaks()
         rows = B * L
         alg = shard_bytes + rows * (8 + 16)
@@ -898,16 +1331,20 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
                            "(NCCL all-gather of 16 B row records)"),
                        "l2": f"{shard_bytes / 1e9:.1f} GB per rank per step >> 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4),
+                         "frac_of_8TBps_nominal": round(achieved / 8000.0, 4), "traffic": None,
                          "kernel": "display_stats_rows_kernel<bf16, records> (per rank, max over ranks"
                                    + ("; then pushed to the peers' inboxes)" if peers else ")"),
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
                          "algorithmic_bytes_per_launch": alg},
+            "parity": parity,
+            "stages": stages,
             "e2e": e2e,
-            # records, push, publish, combine, refine (peers); records, combine,
-            # refine (NCCL; its all-gather kernel is NCCL's)
+            # records, push, publish, combine, refine (peers); records,
+            # combine, refine (NCCL; its all-gather kernel is NCCL's)
             "gpu_launches": (5 if peers else 3) * K,
             "clocks": clk.summary(),
+            "refine_loop": loop,
         }
         if rank == 0 and not args.no_cpu_baseline:
             line["cpu_baseline"] = run_cpu_baseline(sample=(1, 512, V), seconds=args.cpu_seconds)
@@ -971,12 +1408,25 @@ def profile_case(name: str) -> None:
         print(json.dumps({"profile_case": name, "masked": int(m[1].sum()),
                           "replaced": int(d[3].sum()), "thought": float(t[0].sum())}))
         return
-    shape = {"cta": (1, 4096, 128256), "rows": (1, 10240, 128256)}[name]
+    if name == "decode64":  # decode shape: [1, 64, 155136] bf16, three launches over 16 copies
+        ids = decode_ids(64, 16, "cuda")
+        ring = [decode_logits(64, k, "cuda") for k in range(16)]
+        for k in range(3):
+            c, p, u = cid_engine.display_token_statistics(ids, ring[k * 5])
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "mean_conf": float(c.mean())}))
+        return
+    shape = {"cta": (1, 4096, 128256), "rows": (1, 10240, 128256),
+             "rows_records": (1, 10240, 128256)}[name]
     g = torch.Generator(device="cuda").manual_seed(1)
     lg = torch.randn(shape, generator=g, device="cuda", dtype=torch.bfloat16) * 2
     ids = torch.randint(0, shape[2], shape[:2], device="cuda")
     for _ in range(3):
-        c, p, u = cid_engine.display_token_statistics(ids, lg)
+        if name == "rows_records":  # the same rows reduced to shard records
+            r = cid_engine.display_shard_records(ids, lg, vocab_offset=0, total_vocab=shape[2])
+            c = r[:, 0].view(torch.float32)
+        else:
+            c, p, u = cid_engine.display_token_statistics(ids, lg)
     torch.cuda.synchronize()
     print(json.dumps({"profile_case": name, "shape": shape, "mean_conf": float(c.mean())}))
 
@@ -996,16 +1446,23 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--cpu-min-reps", type=int, default=3)
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
-    ap.add_argument("--profile-case", choices=("cta", "rows", "lm_head", "refine", "corruption"), default=None,
+    ap.add_argument("--ref-cuda-worker", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--profile-case", choices=("cta", "rows", "rows_records", "lm_head", "refine", "corruption",
+                             "decode64"), default=None,
                     help="run a small statistics case for ncu and exit")
     ap.add_argument("--sample-b", type=int, default=1)
     ap.add_argument("--sample-l", type=int, default=1024)
     ap.add_argument("--sample-v", type=int, default=128256)
+    ap.add_argument("--sample-gen", choices=("cpu", "cuda"), default="cpu")
+    ap.add_argument("--sample-world", type=int, default=0)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     if args.cpu_worker:
         cpu_reference_worker(args)
+        return
+    if args.ref_cuda_worker:
+        ref_cuda_worker(args)
         return
     if args.profile_case:
         profile_case(args.profile_case)

@@ -191,6 +191,33 @@ def rollout_slot_transition(
     )
 
 
+def rollout_slot_transition_with_live(
+    occupancy: Tensor,
+    allocation_logits: Tensor,
+    lifecycle_logits: Tensor,
+    revision_logits: Tensor,
+    input_lifecycle: Tensor,
+    *,
+    threshold: float,
+    max_allocations: int,
+    retired_index: int,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """``rollout_slot_transition`` and, from the same kernel, the live
+    occupancy of its next state: ``live_slot_occupancy(next_occupancy
+    .unsqueeze(-1).to(lifecycle_logits.dtype), lifecycle_logits,
+    retired_index)`` as a seventh output ([B, S, 1], lifecycle dtype)."""
+    return torch.ops.cid_engine.rollout_slot_transition_with_live(
+        occupancy,
+        allocation_logits,
+        lifecycle_logits,
+        revision_logits,
+        input_lifecycle,
+        threshold,
+        max_allocations,
+        retired_index,
+    )
+
+
 def materialize_cell_snapshot(
     thought_semantic: Tensor,
     role_logits: Tensor,
@@ -322,5 +349,6 @@ __all__ = [
     "refine_step",
     "refine_step_from_hidden",
     "rollout_slot_transition",
+    "rollout_slot_transition_with_live",
     "thought_corrupt_from_epsilon",
 ]

@@ -11,8 +11,9 @@ for the device-resident chain:
   occupancy -> snapshot, ``cid_engine.step.refine_step``) is captured once per
   ring position in a CUDA graph; a step is one graph replay;
 * the display ids and the slot occupancy are device state carried from one
-  step to the next (two small device copies per step); nothing is read back to
-  decide the next step;
+  step to the next (two small device copies per step inside the graph; in
+  eager mode the step's outputs simply become the state); nothing is read
+  back to decide the next step;
 * every step's snapshot is copied into a ring of pinned host buffers on a
   separate copy stream while the following steps compute; the compute stream
   waits for that copy only before the graph that rewrites the same snapshot
@@ -121,9 +122,16 @@ class DisplayRefineLoop:
                                           **self.params)
         else:
             out = refine_step(self.ids, lg, slots=slots, **self.params)
-        self.ids.copy_(out.token_ids)
-        if slots is not None:
-            self.occ.copy_(out.next_occupancy)
+        if self.use_graphs:
+            # a graph replays on fixed addresses: carry the state in place
+            self.ids.copy_(out.token_ids)
+            if slots is not None:
+                self.occ.copy_(out.next_occupancy)
+        else:
+            # eager: the step's outputs become the state (no copy kernels)
+            self.ids = out.token_ids
+            if slots is not None:
+                self.occ = out.next_occupancy
         return out
 
     def _capture(self) -> None:

@@ -162,8 +162,10 @@ class PeerRecordExchange:
         """(confidence, predicted, current) of ``display_token_statistics`` on
         the unsharded logits, from this rank's shard ``logits_shard`` [B, L, V_r]
         (columns from ``vocab_offset``) and the ranks' ``shard_offsets``.
-        ``timing`` = (start, end) CUDA events recorded around the record
-        kernel."""
+        ``timing`` = (start, end[, combined]) CUDA events recorded before the
+        record kernel, after it (its stores into the peers' inboxes and the
+        epoch's publication included) and, with a third event, after the
+        combine (its wait included)."""
         import ctypes
 
         import cid_engine
@@ -191,6 +193,8 @@ class PeerRecordExchange:
         if timing is not None:
             timing[1].record(cur_stream)
         self._combine(ids, shard_offsets, conf, pred, cur, status, stream)
+        if timing is not None and len(timing) > 2:
+            timing[2].record(cur_stream)
         return conf, pred, cur
 
     def from_records(self, records: Tensor, token_ids: Tensor, *, shard_offsets: list[int]):

@@ -4,8 +4,10 @@ The reference leaves the per-step sequencing to the external CID scheduler
 (``benchmarks/README.md:29-43`` of fwerkor/cid-engine v1.1.0): statistics, the
 refinement policy (a host round trip there), slot transition, live occupancy
 and the materialisation snapshot.  ``refine_step`` enqueues the same chain of
-operators on the current stream with no host synchronisation anywhere, so a
-caller can run many steps back to back or capture them in a CUDA graph.
+operators on the current stream with no host synchronisation anywhere (four
+kernels: statistics, refinement, slot rollout with live occupancy,
+snapshot), so a caller can run many steps back to back or capture them in a
+CUDA graph.
 """
 
 from __future__ import annotations
@@ -114,18 +116,16 @@ def step_from_statistics(
     out = StepOutputs(refined, conf, pred, cur)
     if slots is None:
         return out
-    roll = ops.rollout_slot_transition(
+    # slot rollout and the live occupancy of its next state (retired slots
+    # masked out) from one kernel
+    *roll, live = ops.rollout_slot_transition_with_live(
         slots.occupancy, slots.allocation_logits, slots.lifecycle_logits,
         slots.revision_logits, slots.input_lifecycle, slots.threshold,
         slots.max_allocations, slots.retired_index,
     )
+    roll = tuple(roll)
     next_occ = roll[0]
     live_slots = roll[5]
-    # live occupancy of the next state: retired slots masked out
-    live = ops.live_slot_occupancy(
-        next_occ.unsqueeze(-1).to(slots.lifecycle_logits.dtype),
-        slots.lifecycle_logits, slots.retired_index,
-    )
     snap = ops.materialize_cell_snapshot(
         slots.semantic, slots.role_logits, slots.uncertainty, slots.noise_delta,
         slots.lifecycle_logits, live_slots, slots.semantic_indices,

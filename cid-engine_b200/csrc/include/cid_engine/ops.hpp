@@ -24,6 +24,8 @@ using Tensor3 = std::tuple<at::Tensor, at::Tensor, at::Tensor>;
 using Tensor4 = std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor>;
 using Tensor6 =
     std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor>;
+using Tensor7 = std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
+                           at::Tensor, at::Tensor>;
 
 at::Tensor live_slot_occupancy(Backend backend, const at::Tensor& slot_occupancy,
                                const std::optional<at::Tensor>& lifecycle_features,
@@ -42,6 +44,14 @@ Tensor6 rollout_slot_transition(Backend backend, const at::Tensor& occupancy,
                                 const at::Tensor& revision_logits,
                                 const at::Tensor& input_lifecycle, double threshold,
                                 std::int64_t max_allocations, std::int64_t retired_index);
+
+Tensor7 rollout_slot_transition_with_live(Backend backend, const at::Tensor& occupancy,
+                                          const at::Tensor& allocation_logits,
+                                          const at::Tensor& lifecycle_logits,
+                                          const at::Tensor& revision_logits,
+                                          const at::Tensor& input_lifecycle, double threshold,
+                                          std::int64_t max_allocations,
+                                          std::int64_t retired_index);
 
 Tensor3 thought_corrupt_from_epsilon(Backend backend, const at::Tensor& semantic,
                                      const at::Tensor& timesteps, const at::Tensor& occupancy,

@@ -33,6 +33,7 @@
 
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -46,7 +47,7 @@ namespace {
 #define CID_STATS_THREADS 256
 #endif
 constexpr int kThreads = CID_STATS_THREADS;  // threads per CTA
-constexpr int kMaxCluster = 8;
+constexpr int kMaxCluster = 16;  // above 8: non-portable, opted into per kernel
 constexpr float kGap = 5.0f;  // natural-log units; terms stay <= e^5
 constexpr int64_t kNone = LLONG_MAX;
 constexpr int kMaxPeers = 8;  // ranks of a peer record exchange
@@ -499,33 +500,57 @@ __device__ int64_t first_column(const Acc& a, float target, const T* row, int64_
   return kNone;
 }
 
-// Block-wide merge of per-thread partials in a fixed order (result valid in
-// every thread).
+// Partial of no values: merging it changes nothing.
+__device__ __forceinline__ Partial empty_partial() { return Partial{-INFINITY, -INFINITY, 0.0f, 0.0f}; }
+
+// Merge of the `n` (<= 32) partials in lanes 0..n-1 of a warp by a fixed
+// butterfly (deterministic; the result is read from lane 0).
+__device__ __forceinline__ Partial warp_merge_n(Partial q, int n) {
+  for (int d = 1; d < n; d <<= 1) q = merge(q, shfl_xor(q, d));
+  return q;
+}
+
+// Block-wide merge of per-thread partials in a fixed order: butterflies
+// within each warp, then the warps' partials by a butterfly in warp 0
+// (result valid in every thread).
 __device__ Partial block_merge(Partial st, Partial* smem_warps, Partial* smem_out) {
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) st = merge(st, shfl_xor(st, d));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) smem_warps[warp] = st;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    Partial out = smem_warps[0];
-    for (int w = 1; w < kThreads / 32; ++w) out = merge(out, smem_warps[w]);
-    *smem_out = out;
+  if (warp == 0) {
+    Partial q = lane < kThreads / 32 ? smem_warps[lane] : empty_partial();
+    q = warp_merge_n(q, kThreads / 32);
+    if (lane == 0) *smem_out = q;
   }
   __syncthreads();
   return *smem_out;
 }
 
+// Minimum of v over the block, valid in thread 0 (the barrier on entry
+// makes `smem` reusable by consecutive calls).
 __device__ __forceinline__ int64_t block_min_i64(int64_t v, int64_t* smem) {
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, d));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
   if (lane == 0) smem[warp] = v;
   __syncthreads();
-  int64_t r = smem[0];
-  for (int w = 1; w < kThreads / 32; ++w) r = min(r, smem[w]);
-  __syncthreads();
-  return r;
+  if (warp == 0) {
+    v = lane < kThreads / 32 ? smem[lane] : kNone;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, d));
+  }
+  return v;
+}
+
+// Split cluster barrier: arrive (relaxed) early, wait later.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
 // The row's token id relative to this launch's columns, and the logit there
@@ -598,10 +623,11 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   using VT = VecTraits<T>;
   constexpr int N = 2 * VT::N;
   __shared__ Partial warp_parts[kThreads / 32];
-  __shared__ Partial cta_part;   // this CTA's merged partial
-  __shared__ Partial row_part;   // the row's merged partial (rank 0 -> all)
+  __shared__ Partial cta_part;               // this CTA's merged partial
+  __shared__ Partial parts[kMaxCluster];     // rank 0: every CTA's partial
+  __shared__ float2 heads[kMaxCluster];      // every CTA: (max, sum) of every CTA
+  __shared__ int64_t cols[kMaxCluster];      // rank 0: every CTA's first column
   __shared__ int64_t red[kThreads / 32];
-  __shared__ int64_t cta_col;    // this CTA's first column of the maximum
   __shared__ Patch patch;
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -610,6 +636,9 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   const int64_t row = static_cast<int64_t>(blockIdx.x) / nrank;
   const T* rowp = static_cast<const T*>(p.logits) + row * p.row_stride;
   const int64_t V = p.vocab;
+  // every CTA of the cluster must have started before its shared memory is
+  // written remotely: arrive now, wait once the streaming is done
+  if (nrank > 1) cluster_arrive_relaxed();
 
   if (kRep) {
     if (threadIdx.x < 32) repetition_patch(p, row, &patch);
@@ -619,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   __syncthreads();
   const Patch pt = patch;
 
-  // split the row: unaligned head, 16-byte vectors, tail
+  // split the row: unaligned head, 32-byte vectors, tail
   const uintptr_t addr = reinterpret_cast<uintptr_t>(rowp);
   int64_t head = static_cast<int64_t>(((kVecBytes - (addr & (kVecBytes - 1))) & (kVecBytes - 1)) / sizeof(T));
   if (head > V) head = V;
@@ -631,38 +660,62 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   const int64_t t_beg = rank == nrank - 1 ? tail_beg : V;
 
   Acc a{-INFINITY, -INFINITY, 0.0f, 0.0f, 0.0f, kNone};
+  // the row's writer fetches its token id now and the logit there once the
+  // streaming is done (an L2 hit by then), so that warp 0 does not wait on
+  // the dependent pair before streaming and the second load overlaps the
+  // merges below
+  const bool writer = threadIdx.x == 0 && rank == 0;
   int64_t cur_id = 0;
   float cur_x = 0.0f;
-  if (threadIdx.x == 0 && rank == 0) load_current<T, kMode>(p, row, rowp, V, cur_id, cur_x);
+  if (writer) cur_id = __ldg(p.ids + row) - (kMode == Mode::kRecord ? p.vocab_offset : 0);
   stream_row<T, kRep, kThreads, U>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
+  if (writer && cur_id >= 0 && cur_id < V) cur_x = VT::scalar(rowp, cur_id);
   Partial mine{a.m, a.om, a.off, a.s0 + a.s1};
   const Partial cta = block_merge(mine, warp_parts, &cta_part);
 
-  // the row's partial: merge the cluster's CTAs in rank order
+  // The row's maximum (every CTA: its column search needs it) and, in rank
+  // 0, the row's merged partial.  Lane k of warp 0 stores this CTA's
+  // (max, sum) into CTA k and its partial into rank 0, all in parallel; one
+  // barrier later every CTA reads them from its own shared memory.
   Partial fin = cta;
+  float target = cta.m;
+  bool special = !isfinite(cta.m) || (cta.s != cta.s);
   if (nrank > 1) {
-    cluster.sync();  // every CTA's partial is visible cluster-wide
-    if (threadIdx.x == 0) {
-      Partial r = *cluster.map_shared_rank(&cta_part, 0);
-      for (int k = 1; k < nrank; ++k) r = merge(r, *cluster.map_shared_rank(&cta_part, k));
-      row_part = r;
+    cluster_wait();
+    if (threadIdx.x < nrank) {
+      *cluster.map_shared_rank(&heads[rank], static_cast<int>(threadIdx.x)) =
+          make_float2(cta.m, cta.s);
+      if (threadIdx.x == 0) *cluster.map_shared_rank(&parts[rank], 0) = cta;
     }
-    __syncthreads();
-    fin = row_part;
+    cluster.sync();
+    float M = -INFINITY;
+    bool nan_sum = false;
+    for (int k = 0; k < nrank; ++k) {
+      M = fmaxf(M, heads[k].x);
+      nan_sum |= heads[k].y != heads[k].y;
+    }
+    target = M;
+    special = !isfinite(M) || nan_sum;
+    if (rank == 0 && threadIdx.x < 32) {
+      Partial q = static_cast<int>(threadIdx.x) < nrank ? parts[threadIdx.x] : empty_partial();
+      fin = warp_merge_n(q, nrank);  // lane 0 (thread 0) holds the row's partial
+    }
   }
-  const bool special = !isfinite(fin.m) || (fin.s != fin.s);
 
   // first column of the maximum: threads that hold it re-read their chunk
   int64_t col = kNone;
-  if (!special) col = first_column<T, kRep, kThreads, U>(a, fin.m, rowp, head, v_end, pt);
-  col = block_min_i64(col, red);
-  if (threadIdx.x == 0) cta_col = col;
+  if (!special) col = first_column<T, kRep, kThreads, U>(a, target, rowp, head, v_end, pt);
+  col = block_min_i64(col, red);  // valid in thread 0
   if (nrank > 1) {
-    cluster.sync();  // every CTA's column is visible
-    if (rank == 0 && threadIdx.x == 0)
-      for (int k = 1; k < nrank; ++k) col = min(col, *cluster.map_shared_rank(&cta_col, k));
-    cluster.sync();  // remote shared memory has been read; other CTAs may exit
+    if (threadIdx.x == 0) *cluster.map_shared_rank(&cols[rank], 0) = col;
+    cluster.sync();  // every CTA's column has landed in rank 0
     if (rank != 0) return;
+    if (threadIdx.x < 32) {
+      int64_t c = static_cast<int>(threadIdx.x) < nrank ? cols[threadIdx.x] : kNone;
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) c = min(c, __shfl_xor_sync(0xffffffffu, c, d));
+      col = c;
+    }
   }
 
   if (special) {
@@ -672,11 +725,11 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
       float x = VT::scalar(rowp, c);
       if (kRep) x = patched(pt, c, x);
       if (x != x && first_nan == kNone) first_nan = c;
-      if (x == fin.m && first_max == kNone) first_max = c;
+      if (x == target && first_max == kNone) first_max = c;
     }
     first_nan = block_min_i64(first_nan, red);
     first_max = block_min_i64(first_max, red);
-    if (threadIdx.x == 0) write_special<T, kMode>(p, row, cur_x, fin.m, first_nan, first_max);
+    if (threadIdx.x == 0) write_special<T, kMode>(p, row, cur_x, target, first_nan, first_max);
     return;
   }
   if (threadIdx.x == 0) write_normal<T, kRep, kMode>(p, row, V, cur_id, cur_x, pt, fin, col);
@@ -742,7 +795,12 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRep ? 7 : 0) display_stats_ro
     return;
   }
   const int64_t col = warp_min_i64(first_column<T, kRep, 32, U>(a, fin.m, rowp, head, nvec, pt));
-  if (lane == 0) write_normal<T, kRep, kMode>(p, row, V, cur_id, cur_x, pt, fin, col);
+  // the plain statistics re-read the token id here rather than keep it live
+  // through the streaming loop (two registers that cost the loop ~5 %)
+  if (lane == 0) {
+    const int64_t id = (kMode == Mode::kFinal && !kRep) ? __ldg(p.ids + row) : cur_id;
+    write_normal<T, kRep, kMode>(p, row, V, id, cur_x, pt, fin, col);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -952,24 +1010,56 @@ __global__ void merge_records_kernel(CombineParams p, cid_shard_record_t* out) {
 // CTA kernel to 98 registers and 2 resident CTAs per SM, which is slower).
 constexpr int kUnroll = 4;
 
-// Cluster size: split rows over P CTAs (power of two, <= 8) until the grid
-// holds at least two waves of resident CTAs, while each CTA keeps at least
-// two full iterations of 32-byte loads.
+// Largest cluster this kernel instance can be launched with: 16 where the
+// device schedules 16-CTA clusters of it (a non-portable size, opted into
+// once per instance), else the portable 8.
+template <typename T, bool kRep, Mode kMode>
+int max_cluster() {
+  static const int n = [] {  // thread-safe one-time init
+    auto* fn = display_stats_kernel<T, kRep, kMode, kUnroll>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return 8;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kMaxCluster);
+    cfg.blockDim = dim3(kThreads);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kMaxCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) != cudaSuccess || clusters < 1) {
+      cudaGetLastError();
+      return 8;
+    }
+    return kMaxCluster;
+  }();
+  return n;
+}
+
+// Cluster size: split rows over P CTAs (power of two) while the grid stays
+// within two CTAs per SM and each CTA keeps at least half a round of 32-byte
+// loads (kThreads * kUnroll / 2 vectors).  Measured on B200 over
+// [1, rows, 155136] bf16 (CUDA-graph replays): rows x P near 2 x SMs is
+// the fastest split (32 rows: P = 8, 9.5 us; 64: 4, 11.2 us; 128: 2,
+// 14.6 us; 256: 1, 21 us); larger clusters spend more in their merges than
+// the extra SMs save, smaller ones leave SMs idle.
 template <typename T, bool kRep, Mode kMode>
 int cluster_size(int64_t rows, int64_t vocab) {
-  // per template instance, from the occupancy API (thread-safe one-time init)
-  static const int resident_per_sm = [] {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, display_stats_kernel<T, kRep, kMode, kUnroll>,
-                                                      kThreads, 0) != cudaSuccess || n <= 0)
-      n = 4;
-    return n;
-  }();
-  const int64_t want = 2LL * sm_count() * resident_per_sm;
+  const int64_t target = 2LL * sm_count();
   const int64_t vecs = vocab * static_cast<int64_t>(sizeof(T)) / kVecBytes;
-  const int64_t min_vecs = 2LL * kThreads * kUnroll;
+  const int64_t min_vecs = static_cast<int64_t>(kThreads) * kUnroll / 2;
+  const int pmax = max_cluster<T, kRep, kMode>();
   int P = 1;
-  while (P < kMaxCluster && rows * P < want && vecs / (2 * P) >= min_vecs) P *= 2;
+  while (P < pmax && rows * P * 2 <= target && vecs / (2 * P) >= min_vecs) P *= 2;
+#ifdef CID_STATS_CLUSTER_FROM_ENV  // tuning builds only: force P
+  if (const char* e = getenv("CID_STATS_CLUSTER")) P = atoi(e);
+#endif
   return P;
 }
 

@@ -106,7 +106,14 @@ struct RolloutParams {
   int64_t* in_idx;
   uint8_t* present;
   uint8_t* live;
+  // optional: live occupancy of the next state (csrc/ops.cpp:12-39 applied
+  // to next_occupancy, in the lifecycle logits' dtype `live_dtype`)
+  cid_dtype_t live_dtype;
+  void* live_occ;
 };
+
+__device__ __forceinline__ float clamp01f(float x) { return x != x ? x : fminf(fmaxf(x, 0.0f), 1.0f); }
+__device__ __forceinline__ double clamp01d(double x) { return x != x ? x : fmin(fmax(x, 0.0), 1.0); }
 
 // csrc/ops.cpp:184-256 fused into one pass per row.
 __global__ void rollout_kernel(RolloutParams p) {
@@ -135,6 +142,17 @@ __global__ void rollout_kernel(RolloutParams p) {
         p.in_idx[i] = ii;
         p.present[i] = present;
         p.live[i] = nxt && !prev_retired && (!pred_retired || newly);
+        if (p.live_occ) {  // clamp(next, 0, 1) * (1 - clamp(lifecycle[..., r], 0, 1))
+          const int64_t at = i * p.F + p.retired;
+          if (p.live_dtype == CID_DTYPE_F64) {
+            const double r = clamp01d(load_double(p.dtype, p.life, at));
+            static_cast<double*>(p.live_occ)[i] = __dmul_rn(nxt ? 1.0 : 0.0, __dsub_rn(1.0, r));
+          } else {
+            const float r = clamp01f(load_float(p.dtype, p.life, at));
+            const float keep = round_to(p.live_dtype, __fsub_rn(1.0f, r));
+            store_float(p.live_dtype, p.live_occ, i, __fmul_rn(nxt ? 1.0f : 0.0f, keep));
+          }
+        }
       });
 }
 
@@ -145,9 +163,6 @@ struct LiveParams {
   int64_t rows, F, retired;
   void* out;
 };
-
-__device__ __forceinline__ float clamp01f(float x) { return x != x ? x : fminf(fmaxf(x, 0.0f), 1.0f); }
-__device__ __forceinline__ double clamp01d(double x) { return x != x ? x : fmin(fmax(x, 0.0), 1.0); }
 
 // csrc/ops.cpp:12-39: clamp(occ, 0, 1) * (1 - clamp(lifecycle[..., r], 0, 1)),
 // each op rounded to the storage dtype.
@@ -201,6 +216,27 @@ extern "C" int cid_prefix_allocation_mask(cid_dtype_t occ_dtype, const void* occ
   return launch_result();
 }
 
+namespace {
+
+int launch_rollout(const RolloutParams& p, void* stream) {
+  const int64_t blocks = (p.batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  rollout_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, as_stream(stream)>>>(p);
+  return launch_result();
+}
+
+int check_rollout(cid_dtype_t occ_dtype, cid_dtype_t dtype, int64_t batch, int64_t slots,
+                  int64_t lifecycles, int64_t revisions, double threshold,
+                  int64_t max_allocations, int64_t retired_index) {
+  if (retired_index < 0 || retired_index >= lifecycles) return CID_ERR_INVALID_ARGUMENT;
+  if (!(threshold >= 0.0 && threshold <= 1.0)) return CID_ERR_INVALID_ARGUMENT;
+  if (max_allocations <= 0 || revisions <= 0) return CID_ERR_INVALID_ARGUMENT;
+  if (!is_known_dtype(occ_dtype) || !is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || slots < 0) return CID_ERR_INVALID_ARGUMENT;
+  return CID_OK;
+}
+
+}  // namespace
+
 extern "C" int cid_rollout_slot_transition(
     cid_dtype_t occ_dtype, const void* occupancy, cid_dtype_t dtype,
     const void* allocation_logits, const void* lifecycle_logits, const void* revision_logits,
@@ -209,20 +245,38 @@ extern "C" int cid_rollout_slot_transition(
     uint8_t* next_occupancy, int64_t* lifecycle_indices, int64_t* revision_indices,
     int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present, uint8_t* live_slots,
     void* stream) {
-  if (retired_index < 0 || retired_index >= lifecycles) return CID_ERR_INVALID_ARGUMENT;
-  if (!(threshold >= 0.0 && threshold <= 1.0)) return CID_ERR_INVALID_ARGUMENT;
-  if (max_allocations <= 0 || revisions <= 0) return CID_ERR_INVALID_ARGUMENT;
-  if (!is_known_dtype(occ_dtype) || !is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
-  if (batch < 0 || slots < 0) return CID_ERR_INVALID_ARGUMENT;
+  int rc = check_rollout(occ_dtype, dtype, batch, slots, lifecycles, revisions, threshold,
+                         max_allocations, retired_index);
+  if (rc != CID_OK) return rc;
   if (batch == 0 || slots == 0) return CID_OK;
   RolloutParams p{occ_dtype, occupancy, dtype, allocation_logits, lifecycle_logits,
                   revision_logits, input_lifecycle, batch, slots, lifecycles, revisions,
                   static_cast<float>(threshold), max_allocations, retired_index,
                   next_occupancy, lifecycle_indices, revision_indices, input_lifecycle_indices,
-                  input_lifecycle_present, live_slots};
-  const int64_t blocks = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  rollout_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, as_stream(stream)>>>(p);
-  return launch_result();
+                  input_lifecycle_present, live_slots, dtype, nullptr};
+  return launch_rollout(p, stream);
+}
+
+extern "C" int cid_rollout_slot_transition_live(
+    cid_dtype_t occ_dtype, const void* occupancy, cid_dtype_t dtype,
+    const void* allocation_logits, const void* lifecycle_logits, const void* revision_logits,
+    const void* input_lifecycle, int64_t batch, int64_t slots, int64_t lifecycles,
+    int64_t revisions, double threshold, int64_t max_allocations, int64_t retired_index,
+    uint8_t* next_occupancy, int64_t* lifecycle_indices, int64_t* revision_indices,
+    int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present, uint8_t* live_slots,
+    cid_dtype_t live_dtype, void* live_occupancy, void* stream) {
+  int rc = check_rollout(occ_dtype, dtype, batch, slots, lifecycles, revisions, threshold,
+                         max_allocations, retired_index);
+  if (rc != CID_OK) return rc;
+  if (!is_float_dtype(live_dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
+  if (batch == 0 || slots == 0) return CID_OK;
+  if (!live_occupancy) return CID_ERR_INVALID_ARGUMENT;
+  RolloutParams p{occ_dtype, occupancy, dtype, allocation_logits, lifecycle_logits,
+                  revision_logits, input_lifecycle, batch, slots, lifecycles, revisions,
+                  static_cast<float>(threshold), max_allocations, retired_index,
+                  next_occupancy, lifecycle_indices, revision_indices, input_lifecycle_indices,
+                  input_lifecycle_present, live_slots, live_dtype, live_occupancy};
+  return launch_rollout(p, stream);
 }
 
 extern "C" int cid_live_slot_occupancy(cid_dtype_t dtype, const void* occupancy,

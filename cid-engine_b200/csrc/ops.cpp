@@ -444,12 +444,15 @@ at::Tensor batched_linear_assignment(Backend backend, const at::Tensor& costs,
 // rollout_slot_transition — csrc/ops.cpp:184-256
 // ---------------------------------------------------------------------------
 
-Tensor6 rollout_slot_transition(Backend backend, const at::Tensor& occupancy_input,
-                                const at::Tensor& allocation_logits,
-                                const at::Tensor& lifecycle_logits,
-                                const at::Tensor& revision_logits,
-                                const at::Tensor& input_lifecycle, double threshold,
-                                std::int64_t max_allocations, std::int64_t retired_index) {
+namespace {
+
+// rollout_slot_transition; with `live_out` also the live occupancy of the
+// next state (one kernel, cid_rollout_slot_transition_live).
+Tensor6 rollout_common(Backend backend, const at::Tensor& occupancy_input,
+                       const at::Tensor& allocation_logits, const at::Tensor& lifecycle_logits,
+                       const at::Tensor& revision_logits, const at::Tensor& input_lifecycle,
+                       double threshold, std::int64_t max_allocations,
+                       std::int64_t retired_index, at::Tensor* live_out) {
   TORCH_CHECK(occupancy_input.dim() == 2 ||
                   (occupancy_input.dim() == 3 && occupancy_input.size(-1) == 1),
               "occupancy must have shape [batch, slots] or [batch, slots, 1]");  // :193-196
@@ -484,6 +487,10 @@ Tensor6 rollout_slot_transition(Backend backend, const at::Tensor& occupancy_inp
   auto ii = at::empty({batch, slots}, o.dtype(at::kLong));
   auto present = at::empty({batch, slots}, o.dtype(at::kBool));
   auto live = at::empty({batch, slots}, o.dtype(at::kBool));
+  if (live_out) {
+    TORCH_CHECK(lifecycle_logits.is_floating_point(), "lifecycle_logits must use a floating dtype");
+    *live_out = at::empty({batch, slots, 1}, lifecycle_logits.options());
+  }
   if (backend == Backend::kMeta) return {next, li, ri, ii, present, live};
   if (backend == Backend::kCpu) detail::no_cpu_backend("rollout_slot_transition");
   if (batch == 0 || slots == 0) return {next, li, ri, ii, present, live};
@@ -501,6 +508,17 @@ Tensor6 rollout_slot_transition(Backend backend, const at::Tensor& occupancy_inp
   at::Tensor occ = occupancy.contiguous();
   if (dtype_code(occ.scalar_type()) < 0) occ = occ.to(at::kBool);
   auto u8 = [](at::Tensor& t) { return reinterpret_cast<std::uint8_t*>(t.data_ptr<bool>()); };
+  if (live_out) {
+    check_result(cid_rollout_slot_transition_live(
+                     dt(occ), occ.data_ptr(), dt(al), al.data_ptr(), lc.data_ptr(),
+                     rv.data_ptr(), il.data_ptr(), batch, slots, lc.size(-1), rv.size(-1),
+                     threshold, max_allocations, retired_index, u8(next),
+                     li.data_ptr<std::int64_t>(), ri.data_ptr<std::int64_t>(),
+                     ii.data_ptr<std::int64_t>(), u8(present), u8(live), dt(*live_out),
+                     live_out->data_ptr(), stream_of(occ)),
+                 "rollout_slot_transition_with_live");
+    return {next, li, ri, ii, present, live};
+  }
   check_result(cid_rollout_slot_transition(
                    dt(occ), occ.data_ptr(), dt(al), al.data_ptr(), lc.data_ptr(), rv.data_ptr(),
                    il.data_ptr(), batch, slots, lc.size(-1), rv.size(-1), threshold,
@@ -509,6 +527,36 @@ Tensor6 rollout_slot_transition(Backend backend, const at::Tensor& occupancy_inp
                    u8(live), stream_of(occ)),
                "rollout_slot_transition");
   return {next, li, ri, ii, present, live};
+}
+
+}  // namespace
+
+Tensor6 rollout_slot_transition(Backend backend, const at::Tensor& occupancy,
+                                const at::Tensor& allocation_logits,
+                                const at::Tensor& lifecycle_logits,
+                                const at::Tensor& revision_logits,
+                                const at::Tensor& input_lifecycle, double threshold,
+                                std::int64_t max_allocations, std::int64_t retired_index) {
+  return rollout_common(backend, occupancy, allocation_logits, lifecycle_logits, revision_logits,
+                        input_lifecycle, threshold, max_allocations, retired_index, nullptr);
+}
+
+// Additive: the decode step's rollout and the live occupancy of its next
+// state (live_slot_occupancy(next.unsqueeze(-1).to(lifecycle dtype),
+// lifecycle_logits, retired_index)) from one kernel.
+Tensor7 rollout_slot_transition_with_live(Backend backend, const at::Tensor& occupancy,
+                                          const at::Tensor& allocation_logits,
+                                          const at::Tensor& lifecycle_logits,
+                                          const at::Tensor& revision_logits,
+                                          const at::Tensor& input_lifecycle, double threshold,
+                                          std::int64_t max_allocations,
+                                          std::int64_t retired_index) {
+  at::Tensor live_occ;
+  auto r = rollout_common(backend, occupancy, allocation_logits, lifecycle_logits,
+                          revision_logits, input_lifecycle, threshold, max_allocations,
+                          retired_index, &live_occ);
+  return {std::get<0>(r), std::get<1>(r), std::get<2>(r), std::get<3>(r), std::get<4>(r),
+          std::get<5>(r), live_occ};
 }
 
 // ---------------------------------------------------------------------------
@@ -627,6 +675,7 @@ Tensor4 display_corrupt_from_random(Backend backend, const at::Tensor& token_ids
 // ---------------------------------------------------------------------------
 // masked_diffusion_corrupt_from_random — csrc/ops.cpp:394-444
 // ---------------------------------------------------------------------------
+
 
 Tensor4 masked_diffusion_corrupt_from_random(Backend backend, const at::Tensor& clean_ids,
                                              const at::Tensor& ratio_random,

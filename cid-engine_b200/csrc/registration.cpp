@@ -34,6 +34,12 @@ Tensor6 rollout_impl(const at::Tensor& occ, const at::Tensor& al, const at::Tens
   return rollout_slot_transition(B, occ, al, lc, rv, il, thr, n, r);
 }
 template <Backend B>
+Tensor7 rollout_live_impl(const at::Tensor& occ, const at::Tensor& al, const at::Tensor& lc,
+                          const at::Tensor& rv, const at::Tensor& il, double thr, std::int64_t n,
+                          std::int64_t r) {
+  return rollout_slot_transition_with_live(B, occ, al, lc, rv, il, thr, n, r);
+}
+template <Backend B>
 Tensor3 thought_impl(const at::Tensor& s, const at::Tensor& t, const at::Tensor& o,
                      const at::Tensor& e) {
   return thought_corrupt_from_epsilon(B, s, t, o, e);
@@ -101,6 +107,7 @@ void register_all(torch::Library& m) {
   m.impl("prefix_allocation_mask", TORCH_FN(prefix_impl<B>));
   m.impl("batched_linear_assignment", TORCH_FN(assignment_impl<B>));
   m.impl("rollout_slot_transition", TORCH_FN(rollout_impl<B>));
+  m.impl("rollout_slot_transition_with_live", TORCH_FN(rollout_live_impl<B>));
   m.impl("thought_corrupt_from_epsilon", TORCH_FN(thought_impl<B>));
   m.impl("display_corrupt_from_random", TORCH_FN(display_corrupt_impl<B>));
   m.impl("masked_diffusion_corrupt_from_random", TORCH_FN(masked_impl<B>));
@@ -160,6 +167,13 @@ TORCH_LIBRARY(cid_engine, m) {
       "materialize_cell_snapshot(Tensor thought_semantic, Tensor role_logits, "
       "Tensor uncertainty, Tensor noise_delta, Tensor lifecycle_logits, "
       "Tensor selected, Tensor semantic_indices) -> Tensor");
+  // additive: the decode step's slot rollout with the live occupancy of the
+  // next state, one kernel
+  m.def(
+      "rollout_slot_transition_with_live(Tensor occupancy, Tensor allocation_logits, "
+      "Tensor lifecycle_logits, Tensor revision_logits, Tensor input_lifecycle, "
+      "float threshold, int max_allocations, int retired_index) "
+      "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)");
   // additive: vocabulary-parallel statistics
   m.def(
       "display_shard_records(Tensor token_ids, Tensor logits_shard, int vocab_offset, "

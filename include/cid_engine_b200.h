@@ -200,6 +200,21 @@ CID_API int cid_rollout_slot_transition(
     int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present,
     uint8_t* live_slots, void* stream);
 
+/* cid_rollout_slot_transition plus, in the same launch, the live occupancy
+ * of the next state: live_slot_occupancy (csrc/ops.cpp:12-39) of
+ * next_occupancy (as a 0/1 value of live_dtype, the lifecycle logits'
+ * dtype) with lifecycle_logits and retired_index, into live_occupancy
+ * (batch x slots of live_dtype).  The decode step's slot rollout followed by
+ * its live occupancy (csrc/ops.cpp:184-256 then :12-39) in one kernel. */
+CID_API int cid_rollout_slot_transition_live(
+    cid_dtype_t occ_dtype, const void* occupancy, cid_dtype_t dtype,
+    const void* allocation_logits, const void* lifecycle_logits, const void* revision_logits,
+    const void* input_lifecycle, int64_t batch, int64_t slots, int64_t lifecycles,
+    int64_t revisions, double threshold, int64_t max_allocations, int64_t retired_index,
+    uint8_t* next_occupancy, int64_t* lifecycle_indices, int64_t* revision_indices,
+    int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present, uint8_t* live_slots,
+    cid_dtype_t live_dtype, void* live_occupancy, void* stream);
+
 /* live_slot_occupancy — replaces csrc/registration.cpp:6-8 and
  * csrc/ops.cpp:12-39.  occupancy: rows (= batch*slots) of `dtype`;
  * lifecycle: rows x features of `dtype` or NULL; out: rows of `dtype`. */

@@ -62,6 +62,24 @@ def test_full_size_32x1024x128256_rows_match_oracle() -> None:
     assert bool((cur <= conf * (1 + 1e-6)).all())
 
 
+@pytest.mark.parametrize("rows", [1, 3, 32, 64, 128, 256, 512])
+@pytest.mark.parametrize("dtype,vocab", [(torch.bfloat16, 155136), (torch.float32, 32000),
+                                         (torch.float16, 50021)])
+def test_decode_rows_match_oracle(rows: int, dtype: torch.dtype, vocab: int) -> None:
+    """Few-row (decode) launches, which split each row over a cluster of up
+    to 16 CTAs, on the published decode widths; a planted peak and an exact
+    tie in a few rows."""
+    g = torch.Generator().manual_seed(rows * 7 + vocab)
+    logits = (torch.randn(1, rows, vocab, generator=g) * 2).to(dtype)
+    ids = torch.randint(vocab, (1, rows), generator=g)
+    logits[0, 0, vocab - 1] = 30.0
+    if rows > 2:
+        logits[0, 2, [5, vocab // 2]] = 40.0
+    out = torch.ops.cid_engine.display_token_statistics(ids.cuda(), logits.cuda())
+    torch.cuda.synchronize()
+    _check_stats(out, ids, logits, f"decode [1,{rows},{vocab}] {dtype}")
+
+
 def test_chain_4x256x32000_matches_oracle() -> None:
     """fp32 [4, 256, 32000] stats -> refine, S=32 slots, thought t=0.3."""
     ids, logits = cases.display_f32_4x256x32000()
@@ -94,6 +112,28 @@ def test_masked_diffusion_64x2048_deterministic() -> None:
     compare.assert_matches("masked_diffusion_corrupt_from_random", out1,
                            oracle.masked_diffusion_corrupt_from_random(*args), "64x2048")
     assert bool(out1[1].any(dim=1).all())  # zero-ratio rows took the fallback
+
+
+@pytest.mark.parametrize("batch,tokens", [(3000, 100), (1, 9000), (7, 33)])
+def test_masked_diffusion_row_shapes_match_oracle(batch: int, tokens: int) -> None:
+    """Masked diffusion with many short rows (3000 rows: more CTAs than the
+    device holds at once, and the metrics kernel's loop over rows), one long
+    row (several loads batches per thread) and rows shorter than a CTA; a
+    third of the rows take the empty-row fallback."""
+    g = torch.Generator().manual_seed(batch + tokens)
+    clean = torch.randint(0, 50257, (batch, tokens), generator=g)
+    rr = torch.rand(batch, 1, generator=g)
+    rr[::3] = 0.0
+    mr = torch.rand(batch, tokens, generator=g)
+    args = (clean, rr, mr, 50256, 1e-6, 1.0)
+    dev = [a.cuda() if isinstance(a, torch.Tensor) else a for a in args]
+    out1 = torch.ops.cid_engine.masked_diffusion_corrupt_from_random(*dev)
+    out2 = torch.ops.cid_engine.masked_diffusion_corrupt_from_random(*dev)
+    for a, b in zip(out1, out2):
+        assert torch.equal(a, b)
+    compare.assert_matches("masked_diffusion_corrupt_from_random", out1,
+                           oracle.masked_diffusion_corrupt_from_random(*args),
+                           f"masked diffusion [{batch},{tokens}]")
 
 
 @pytest.mark.parametrize("tokens", [512, 4096, 8192])

@@ -145,6 +145,36 @@ def test_fuzz_rollout(batch, slots, F, Rv, seed, dtype, threshold, max_alloc) ->
 
 
 @SETTINGS
+@given(batch=st.integers(1, 5), slots=st.integers(1, 150), F=st.integers(1, 6),
+       Rv=st.integers(1, 5), seed=st.integers(0, 2**31 - 1), dtype=DTYPES,
+       threshold=UNIT, max_alloc=st.integers(1, 10), special=st.booleans())
+def test_fuzz_rollout_with_live(batch, slots, F, Rv, seed, dtype, threshold, max_alloc,
+                                special) -> None:
+    """The fused rollout + live occupancy equals rollout_slot_transition
+    followed by live_slot_occupancy of its next occupancy (csrc/ops.cpp:184-256
+    then :12-39); lifecycle values outside [0, 1] and NaN exercise the clamps."""
+    g = torch.Generator().manual_seed(seed)
+    occ = torch.randint(0, 2, (batch, slots), generator=g).bool()
+    al = torch.randn(batch, slots, generator=g).to(dtype)
+    lc = (torch.rand(batch, slots, F, generator=g) * 3 - 1).to(dtype)
+    if special:
+        lc.view(-1)[:: 7] = float("nan")
+    rv = torch.randn(batch, slots, Rv, generator=g).to(dtype)
+    il = torch.randint(-1, 2, (batch, slots, F), generator=g).to(dtype)
+    r = seed % F
+    got = torch.ops.cid_engine.rollout_slot_transition_with_live(
+        occ.cuda(), al.cuda(), lc.cuda(), rv.cuda(), il.cuda(), threshold, max_alloc, r)
+    exp = oracle.rollout_slot_transition(occ, al, lc, rv, il, threshold, max_alloc, r)
+    if bool(compare.sigmoid_ambiguous(al, threshold).any()):
+        return  # the reference's own decision is position-dependent there
+    for a, e in zip(got[:6], exp):
+        assert torch.equal(a.cpu(), e)
+    live = oracle.live_slot_occupancy(exp[0].unsqueeze(-1).to(dtype), lc, r)
+    assert got[6].dtype == dtype and got[6].shape == (batch, slots, 1)
+    torch.testing.assert_close(got[6].cpu(), live, rtol=0, atol=0, equal_nan=True)
+
+
+@SETTINGS
 @given(batch=st.integers(1, 12), tokens=st.integers(1, 3000), seed=st.integers(0, 2**31 - 1),
        lo=st.floats(1e-6, 1.0), span=st.floats(0.0, 1.0), zero_rows=st.booleans())
 def test_fuzz_masked_diffusion(batch, tokens, seed, lo, span, zero_rows) -> None:

@@ -59,6 +59,40 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
             assert torch.equal(pred, e_pred)
             torch.testing.assert_close(conf, e_conf, rtol=compare.STATS_RTOL, atol=compare.STATS_ATOL, equal_nan=True)
             torch.testing.assert_close(cur, e_cur, rtol=compare.STATS_RTOL, atol=compare.STATS_ATOL, equal_nan=True)
+        # the vocabulary-parallel workload's row width, 4096 rows: records
+        # through the peer exchange == the unsharded statistics, and rank 0's
+        # rows against the oracle
+        V = 152064
+        g = torch.Generator(device=dev).manual_seed(3)
+        logits = (torch.randn(4, 1024, V, generator=g, device=dev) * 2).to(torch.bfloat16)
+        flat = logits.view(-1, V)
+        peak = torch.nonzero(torch.rand(4096, generator=g, device=dev) < 0.05).flatten()
+        col = torch.randint(V, (peak.numel(),), generator=g, device=dev)
+        flat[peak, col] = (flat[peak, col].float() + 8.0).to(torch.bfloat16)
+        ids = torch.randint(V, (4, 1024), generator=g, device=dev)
+        offs = parallel.shard_offsets(V, world)
+        shard = logits[..., offs[rank]:offs[rank + 1]].contiguous()
+        ex = parallel.PeerRecordExchange(4 * 1024)
+        try:
+            conf, pred, cur = ex.statistics(ids, shard, vocab_offset=offs[rank], total_vocab=V,
+                                            shard_offsets=offs)
+        finally:
+            ex.close()
+        e_conf, e_pred, e_cur = cid_engine.display_token_statistics(ids, logits)
+        assert torch.equal(pred, e_pred)
+        compare.assert_stats_close(conf, e_conf, "sharded [4,1024,152064] conf")
+        compare.assert_stats_close(cur, e_cur, "sharded [4,1024,152064] cur")
+        if rank == 0:
+            from oracle import oracle
+
+            sel = torch.arange(0, 4096, 64, device=dev)
+            o_conf, o_pred, o_cur = oracle.display_token_statistics(
+                ids.view(-1)[sel].view(1, -1), flat[sel].view(1, -1, V))
+            assert torch.equal(pred.view(-1)[sel].cpu(), o_pred.view(-1))
+            compare.assert_stats_close(conf.view(-1)[sel], o_conf.view(-1), "vs oracle conf")
+            compare.assert_stats_close(cur.view(-1)[sel], o_cur.view(-1), "vs oracle cur")
+        del logits, flat, shard
+        torch.cuda.empty_cache()
         # the fused vocabulary-parallel step == statistics then refinement
         V = 50021
         g = torch.Generator(device=dev).manual_seed(7)
@@ -153,7 +187,7 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
 def test_vocab_parallel_statistics_over_nccl(tmp_path) -> None:
     import torch.multiprocessing as mp
 
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")
     assert sorted(p.name for p in tmp_path.iterdir()) == [f"ok{r}" for r in range(world)]
