@@ -53,9 +53,35 @@ inline int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// Programmatic dependent launch (sm_90 and later).  A kernel launched with
+// launch_pdl may be scheduled while the kernel before it in the stream is
+// still running, so its launch latency hides under that kernel's tail.  Such
+// a kernel calls pdl_wait() before its first global memory access, read or
+// write (the wait returns once the previous kernel has completed and its
+// writes are visible), and pdl_trigger() once its own dependents may be
+// scheduled.  In a kernel launched without the attribute both are no-ops.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return record_cuda_error(cudaLaunchKernelEx(&cfg, kernel, args...));
+}
+
 // ---------------------------------------------------------------------------
 // Device-side helpers
 // ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 // 2^x with the SFU (ex2.approx.ftz.f32: a few ulp of relative error).
 __device__ __forceinline__ float ex2(float x) {

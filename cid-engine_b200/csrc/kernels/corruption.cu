@@ -56,6 +56,8 @@ constexpr int kRowBatch = 4;  // tokens per thread whose loads are issued togeth
 // token a thread handles.
 template <int kBT>
 __global__ void __launch_bounds__(kBT) masked_diffusion_kernel(MaskedParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int kW = kBT / 32;
   constexpr int U = kRowBatch;
   __shared__ int64_t s_cnt[kW];
@@ -132,19 +134,20 @@ __global__ void __launch_bounds__(kBT) masked_diffusion_kernel(MaskedParams p) {
 
 // Row kernel at the block size that covers a row in one batch of loads
 // where the row allows it.
-void launch_masked_rows(const MaskedParams& p, cudaStream_t s) {
-  const unsigned grid = static_cast<unsigned>(p.batch);
+int launch_masked_rows(const MaskedParams& p, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>(p.batch));
   if (p.tokens <= 256 * kRowBatch)
-    masked_diffusion_kernel<256><<<grid, 256, 0, s>>>(p);
-  else if (p.tokens <= 512 * kRowBatch)
-    masked_diffusion_kernel<512><<<grid, 512, 0, s>>>(p);
-  else
-    masked_diffusion_kernel<1024><<<grid, 1024, 0, s>>>(p);
+    return launch_pdl(masked_diffusion_kernel<256>, grid, dim3(256), 0, s, p);
+  if (p.tokens <= 512 * kRowBatch)
+    return launch_pdl(masked_diffusion_kernel<512>, grid, dim3(512), 0, s, p);
+  return launch_pdl(masked_diffusion_kernel<1024>, grid, dim3(1024), 0, s, p);
 }
 
 __global__ void __launch_bounds__(kT) masked_metrics_kernel(const int64_t* counts,
                                                             const float* ratio, int64_t batch,
                                                             int64_t tokens, float* metrics) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int64_t s_c[kWarps];
   __shared__ double s_r[kWarps];
   int64_t c = 0;
@@ -209,6 +212,8 @@ __device__ double thought_alpha(cid_dtype_t tdt, const void* ts, int64_t row) {
 }
 
 __global__ void __launch_bounds__(kT) thought_kernel(ThoughtParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const bool occ = load_truthy(p.odt, p.occ, row);
   const int64_t base = row * p.hidden;
@@ -297,6 +302,8 @@ constexpr int kCorruptBatch = 4;  // tokens per thread whose loads are issued to
 // (kBT apart, so every load instruction is coalesced) before it uses them.
 template <int kBT>
 __global__ void __launch_bounds__(kBT) display_corrupt_kernel(DisplayCorruptParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int kW = kBT / 32;
   constexpr int U = kCorruptBatch;
   __shared__ int64_t s_first[kW];
@@ -409,11 +416,11 @@ extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const floa
   p.metrics = metrics;
   p.counts = static_cast<int64_t*>(workspace);
   cudaStream_t s = as_stream(stream);
-  launch_masked_rows(p, s);
-  int rc = launch_result();
+  int rc = launch_masked_rows(p, s);
   if (rc != CID_OK) return rc;
-  masked_metrics_kernel<<<1, kT, 0, s>>>(p.counts, ratio, batch, tokens, metrics);
-  return launch_result();
+  return launch_pdl(masked_metrics_kernel, dim3(1), dim3(kT), 0, s,
+                    static_cast<const int64_t*>(p.counts), static_cast<const float*>(ratio), batch,
+                    tokens, metrics);
 }
 
 // ---------------------------------------------------------------------------
@@ -492,11 +499,11 @@ extern "C" int cid_masked_diffusion_corrupt_no_alloc(
   p.metrics = metrics;
   p.counts = scratch;
   cudaStream_t s = as_stream(stream);
-  launch_masked_rows(p, s);
-  rc = launch_result();
+  rc = launch_masked_rows(p, s);
   if (rc != CID_OK) return rc;
-  masked_metrics_kernel<<<1, kT, 0, s>>>(p.counts, ratio, batch, tokens, metrics);
-  return launch_result();
+  return launch_pdl(masked_metrics_kernel, dim3(1), dim3(kT), 0, s,
+                    static_cast<const int64_t*>(p.counts), static_cast<const float*>(ratio), batch,
+                    tokens, metrics);
 }
 
 extern "C" int cid_thought_corrupt(cid_dtype_t sem_dtype, const void* semantic,
@@ -511,8 +518,8 @@ extern "C" int cid_thought_corrupt(cid_dtype_t sem_dtype, const void* semantic,
   if (rows == 0) return CID_OK;
   ThoughtParams p{sem_dtype, semantic, t_dtype, timesteps, occ_dtype, occupancy, epsilon,
                   rows, hidden, corrupted, local_noise, masked_epsilon};
-  thought_kernel<<<static_cast<unsigned>(rows), kT, 0, as_stream(stream)>>>(p);
-  return launch_result();
+  return launch_pdl(thought_kernel, dim3(static_cast<unsigned>(rows)), dim3(kT), 0,
+                    as_stream(stream), p);
 }
 
 extern "C" int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype,
@@ -546,10 +553,8 @@ extern "C" int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype
   const unsigned grid = static_cast<unsigned>(batch);
   cudaStream_t s = as_stream(stream);
   if (tokens <= 256 * kCorruptBatch)
-    display_corrupt_kernel<256><<<grid, 256, 0, s>>>(p);
-  else if (tokens <= 512 * kCorruptBatch)
-    display_corrupt_kernel<512><<<grid, 512, 0, s>>>(p);
-  else
-    display_corrupt_kernel<1024><<<grid, 1024, 0, s>>>(p);
-  return launch_result();
+    return launch_pdl(display_corrupt_kernel<256>, dim3(grid), dim3(256), 0, s, p);
+  if (tokens <= 512 * kCorruptBatch)
+    return launch_pdl(display_corrupt_kernel<512>, dim3(grid), dim3(512), 0, s, p);
+  return launch_pdl(display_corrupt_kernel<1024>, dim3(grid), dim3(1024), 0, s, p);
 }

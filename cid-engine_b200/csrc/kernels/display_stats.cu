@@ -33,7 +33,6 @@
 
 #include <climits>
 #include <cmath>
-#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -466,6 +465,20 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
     consume_scalar<kRep>(a, VT::scalar(row, c), c, pt);
 }
 
+// Pulls the chunk recorded in `where` into L1 ahead of first_column, so the
+// re-read after the merges hits L1 instead of L2 (no registers held).
+template <typename T, int kStride, int U>
+__device__ __forceinline__ void prefetch_chunk(const Acc& a, const T* row, int64_t head,
+                                               int64_t v_end) {
+  if (a.where < 0 || !(a.m > -INFINITY)) return;
+  const Vec32* vrow = reinterpret_cast<const Vec32*>(row + head);
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const int64_t vi = a.where + static_cast<int64_t>(k) * kStride;
+    if (vi < v_end) asm volatile("prefetch.global.L1 [%0];" ::"l"(vrow + vi));
+  }
+}
+
 // First column holding `target` among this thread's elements, from the chunk
 // recorded in `where` (re-read from memory); kNone when the thread's maximum
 // is not `target`.
@@ -620,6 +633,7 @@ __device__ void write_normal(const StatsParams& p, int64_t row, int64_t V, int64
 // the default cap and raise the plain kernels to 92-124 registers.
 template <typename T, bool kRep, Mode kMode, int U>
 __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(StatsParams p) {
+  pdl_wait();
   using VT = VecTraits<T>;
   constexpr int N = 2 * VT::N;
   __shared__ Partial warp_parts[kThreads / 32];
@@ -669,6 +683,7 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   float cur_x = 0.0f;
   if (writer) cur_id = __ldg(p.ids + row) - (kMode == Mode::kRecord ? p.vocab_offset : 0);
   stream_row<T, kRep, kThreads, U>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
+  prefetch_chunk<T, kThreads, U>(a, rowp, head, v_end);  // under the merges below
   if (writer && cur_id >= 0 && cur_id < V) cur_x = VT::scalar(rowp, cur_id);
   Partial mine{a.m, a.om, a.off, a.s0 + a.s1};
   const Partial cta = block_merge(mine, warp_parts, &cta_part);
@@ -718,6 +733,13 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
     }
   }
 
+  // The next kernel may be scheduled from here on.  Measured on B200 with
+  // CUDA graphs: this late point keeps back-to-back statistics launches as
+  // fast as without programmatic launch (an early trigger placed the next
+  // launch's CTAs unevenly: +15 % at 64 rows) and still hides most of the
+  // refinement kernel's launch after the statistics (64 rows: 17.3 against
+  // 17.7 us for the pair).
+  pdl_trigger();
   if (special) {
     // Rare path: first NaN column, else first column equal to the maximum.
     int64_t first_nan = kNone, first_max = kNone;
@@ -751,6 +773,7 @@ __device__ __forceinline__ int64_t warp_min_i64(int64_t v) {
 // faster than its natural 80 on bf16 [32768, 128256]).
 template <typename T, bool kRep, Mode kMode, int U>
 __global__ void __launch_bounds__(kRowWarps * 32, kRep ? 7 : 0) display_stats_rows_kernel(StatsParams p) {
+  pdl_wait();
   using VT = VecTraits<T>;
   constexpr int N = 2 * VT::N;
   __shared__ Patch patches[kRowWarps];
@@ -777,6 +800,8 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRep ? 7 : 0) display_stats_ro
   float cur_x = 0.0f;
   if (lane == 0) load_current<T, kMode>(p, row, rowp, V, cur_id, cur_x);
   stream_row<T, kRep, 32, U>(rowp, head, 0, nvec, head, tail_beg, V, pt, a, lane);
+  pdl_trigger();
+  prefetch_chunk<T, 32, U>(a, rowp, head, nvec);
   Partial fin{a.m, a.om, a.off, a.s0 + a.s1};
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) fin = merge(fin, shfl_xor(fin, d));
@@ -1057,9 +1082,6 @@ int cluster_size(int64_t rows, int64_t vocab) {
   const int pmax = max_cluster<T, kRep, kMode>();
   int P = 1;
   while (P < pmax && rows * P * 2 <= target && vecs / (2 * P) >= min_vecs) P *= 2;
-#ifdef CID_STATS_CLUSTER_FROM_ENV  // tuning builds only: force P
-  if (const char* e = getenv("CID_STATS_CLUSTER")) P = atoi(e);
-#endif
   return P;
 }
 
@@ -1093,13 +1115,15 @@ int launch_cta_kernel(const StatsParams& prm, int P, cudaStream_t stream) {
   cfg.gridDim = dim3(static_cast<unsigned>(blocks));
   cfg.blockDim = dim3(kThreads);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = P;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return record_cuda_error(cudaLaunchKernelEx(&cfg, display_stats_kernel<T, kRep, kMode, U>, prm));
 }
 
@@ -1108,9 +1132,8 @@ int launch_stats(const StatsParams& prm, cudaStream_t stream) {
   if (use_row_warps<T, kRep, kMode>(prm.rows)) {
     const int64_t blocks = (prm.rows + kRowWarps - 1) / kRowWarps;
     if (blocks > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
-    display_stats_rows_kernel<T, kRep, kMode, kUnroll>
-        <<<static_cast<unsigned>(blocks), kRowWarps * 32, 0, stream>>>(prm);
-    return launch_result();
+    return launch_pdl(display_stats_rows_kernel<T, kRep, kMode, kUnroll>,
+                      dim3(static_cast<unsigned>(blocks)), dim3(kRowWarps * 32), 0, stream, prm);
   }
   const int P = cluster_size<T, kRep, kMode>(prm.rows, prm.vocab);
   return launch_cta_kernel<T, kRep, kMode, kUnroll>(prm, P, stream);

@@ -280,6 +280,8 @@ __device__ __forceinline__ bool cand_better(const Candidate& a, const Candidate&
 
 template <int kT>
 __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int kWarps = kT / 32;
   constexpr int kChunk = 8;
   extern __shared__ __align__(16) unsigned char dyn[];
@@ -599,8 +601,8 @@ extern "C" int cid_refine_display(const int64_t* token_ids, const float* confide
     if (e != cudaSuccess) return record_cuda_error(e);
   }
   if (wide)
-    refine_kernel<512><<<static_cast<unsigned>(batch), 512, dyn, as_stream(stream)>>>(p);
-  else
-    refine_kernel<256><<<static_cast<unsigned>(batch), 256, dyn, as_stream(stream)>>>(p);
-  return launch_result();
+    return launch_pdl(refine_kernel<512>, dim3(static_cast<unsigned>(batch)), dim3(512), dyn,
+                      as_stream(stream), p);
+  return launch_pdl(refine_kernel<256>, dim3(static_cast<unsigned>(batch)), dim3(256), dyn,
+                    as_stream(stream), p);
 }

@@ -80,6 +80,8 @@ struct PrefixParams {
 };
 
 __global__ void prefix_allocation_kernel(PrefixParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= p.batch) return;
   warp_prefix_allocation(
@@ -117,6 +119,8 @@ __device__ __forceinline__ double clamp01d(double x) { return x != x ? x : fmin(
 
 // csrc/ops.cpp:184-256 fused into one pass per row.
 __global__ void rollout_kernel(RolloutParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= p.batch) return;
   const int64_t base = row * p.slots;
@@ -167,6 +171,8 @@ struct LiveParams {
 // csrc/ops.cpp:12-39: clamp(occ, 0, 1) * (1 - clamp(lifecycle[..., r], 0, 1)),
 // each op rounded to the storage dtype.
 __global__ void live_kernel(LiveParams p) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < p.rows;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     if (p.dtype == CID_DTYPE_F64) {
@@ -211,17 +217,16 @@ extern "C" int cid_prefix_allocation_mask(cid_dtype_t occ_dtype, const void* occ
                  logit_row_stride, logit_col_stride, batch, slots,
                  static_cast<float>(threshold), max_allocations, out};
   const int64_t blocks = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  prefix_allocation_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0,
-                             as_stream(stream)>>>(p);
-  return launch_result();
+  return launch_pdl(prefix_allocation_kernel, dim3(static_cast<unsigned>(blocks)),
+                    dim3(kWarpsPerBlock * 32), 0, as_stream(stream), p);
 }
 
 namespace {
 
 int launch_rollout(const RolloutParams& p, void* stream) {
   const int64_t blocks = (p.batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  rollout_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, as_stream(stream)>>>(p);
-  return launch_result();
+  return launch_pdl(rollout_kernel, dim3(static_cast<unsigned>(blocks)), dim3(kWarpsPerBlock * 32),
+                    0, as_stream(stream), p);
 }
 
 int check_rollout(cid_dtype_t occ_dtype, cid_dtype_t dtype, int64_t batch, int64_t slots,
@@ -292,6 +297,6 @@ extern "C" int cid_live_slot_occupancy(cid_dtype_t dtype, const void* occupancy,
   const int threads = 256;
   int64_t blocks = (rows + threads - 1) / threads;
   if (blocks > 4096) blocks = 4096;
-  live_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(p);
-  return launch_result();
+  return launch_pdl(live_kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0,
+                    as_stream(stream), p);
 }

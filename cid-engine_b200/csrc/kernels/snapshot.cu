@@ -38,6 +38,8 @@ struct SnapshotParams {
 };
 
 __global__ void snapshot_kernel(SnapshotParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   if (row >= p.rows) return;
   const int lane = threadIdx.x & 31;
@@ -101,6 +103,6 @@ extern "C" int cid_materialize_cell_snapshot(
                    uncertainty, noise_dtype, noise_delta, life_dtype, lifecycle, lifecycles,
                    selected, indices, nindices, rows, out, status};
   const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  snapshot_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, as_stream(stream)>>>(p);
-  return launch_result();
+  return launch_pdl(snapshot_kernel, dim3(static_cast<unsigned>(blocks)), dim3(kWarpsPerBlock * 32),
+                    0, as_stream(stream), p);
 }
