@@ -18,7 +18,7 @@
 //   vocabulary tiles); each unit ends in one 16-byte shard record per row
 //   (the same record as the vocabulary-parallel statistics), and the record
 //   combine kernel merges the groups of a row into its statistics;
-// * units are ordered in groups of 16 row blocks, so the CTAs running at a
+// * units are ordered in groups of 32 row blocks, so the CTAs running at a
 //   time share their hidden blocks and weight tiles in L2;
 // * every mbarrier wait is bounded (2 s of %globaltimer); a wait that runs
 //   out sets CID_STATUS_LM_HEAD_TIMEOUT and a shared abort flag, every role
@@ -43,7 +43,12 @@ constexpr int kUmmaK = 16;
 constexpr int kStages = 4;
 constexpr int kAccBufs = 2;
 constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 512: all of TMEM
-constexpr int kRowGroup = 16;                   // row blocks per raster group
+// Row blocks per raster group.  The CTAs running at once cover about
+// 148 / kRowGroup vocabulary groups (each 16 MB of weight at G = 8 tiles)
+// and kRowGroup hidden blocks (1 MB each); 32 keeps that set under the
+// 126 MB L2 (16 did not: ~150 MB), measured 1-2 % faster at 32768 x 128256
+// x 4096; 64 and 128 were slower.
+constexpr int kRowGroup = 32;
 constexpr int kMaxGroups = 64;                  // record combine limit
 constexpr int kThreads = 192;                   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t kStageA = kBM * kBK * 2;     // 16 KiB
