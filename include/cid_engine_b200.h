@@ -289,9 +289,14 @@ CID_API int cid_masked_diffusion_corrupt(const int64_t* clean_ids,
  * exits; batch > CID_NO_ALLOC_MAX_BATCH returns CID_ERR_SCRATCH_LIMIT.  The
  * first call on a device looks up the array's device address (a
  * cudaGetSymbolAddress with that device current), so make that first call
- * before any stream capture.  Calls on one device share the array: calls
- * that overlap on the GPU (on different streams) race on it.  Nothing in it
- * needs clearing between calls. */
+ * before any stream capture.  The address is cached per device for the
+ * device's primary context (the one the CUDA runtime uses by default): a
+ * caller that runs the library in a context of its own (cuCtxCreate), or
+ * calls it after cudaDeviceReset in the same process, would be handed a
+ * stale address and must use cid_masked_diffusion_corrupt instead.  Calls
+ * on one device share the array: calls that overlap on the GPU (on
+ * different streams) race on it.  Nothing in it needs clearing between
+ * calls. */
 #define CID_NO_ALLOC_MAX_BATCH 65536
 CID_API int cid_masked_diffusion_corrupt_no_alloc(
     const int64_t* clean_ids, const float* ratio_random,

@@ -7,7 +7,9 @@ its request path, an FFI binding with no device allocator): its scratch is a
 fixed array inside the library.  Both entry points are called here through
 the C ABI with the same inputs, twice in a row with different inputs, and
 must produce identical outputs (the kernels are deterministic, so the
-tolerance is zero).  This file is collected last on purpose.
+tolerance is zero), on device 0 and, when a second GPU is visible, on device
+1 too (the array's address is looked up per device).  This file is collected
+last on purpose.
 """
 
 from __future__ import annotations
@@ -60,8 +62,16 @@ def _call(lib, fn_name: str, inputs, outputs, lo: float, hi: float, workspace=No
     return getattr(lib, fn_name)(*args, stream)
 
 
-def test_no_alloc_entry_point_matches_workspace_entry_point() -> None:
+def _devices() -> list[int]:
+    """Device 0, and device 1 when a second GPU is visible (the scratch
+    address is looked up and cached per device)."""
+    return [0, 1] if torch.cuda.device_count() > 1 else [0]
+
+
+@pytest.mark.parametrize("device", _devices())
+def test_no_alloc_entry_point_matches_workspace_entry_point(device: int) -> None:
     assert torch.cuda.is_available()
+    torch.cuda.set_device(device)
     lib = ctypes.CDLL(str(LIB))
     lib.cid_masked_diffusion_workspace_bytes.restype = ctypes.c_size_t
     for k, (batch, tokens) in enumerate(((64, 2048), (37, 333))):
@@ -78,6 +88,7 @@ def test_no_alloc_entry_point_matches_workspace_entry_point() -> None:
         for a, b in zip(no_alloc_out, ref_out):
             torch.testing.assert_close(a, b, rtol=0, atol=0)
         assert bool(no_alloc_out[1].any(dim=1).all())  # fallback rows got one mask
+    torch.cuda.set_device(0)
 
 
 def test_no_alloc_entry_point_rejects_batches_beyond_its_scratch() -> None:
