@@ -465,20 +465,6 @@ __device__ void stream_row(const T* row, int64_t head, int64_t v_beg, int64_t v_
     consume_scalar<kRep>(a, VT::scalar(row, c), c, pt);
 }
 
-// Pulls the chunk recorded in `where` into L1 ahead of first_column, so the
-// re-read after the merges hits L1 instead of L2 (no registers held).
-template <typename T, int kStride, int U>
-__device__ __forceinline__ void prefetch_chunk(const Acc& a, const T* row, int64_t head,
-                                               int64_t v_end) {
-  if (a.where < 0 || !(a.m > -INFINITY)) return;
-  const Vec32* vrow = reinterpret_cast<const Vec32*>(row + head);
-#pragma unroll
-  for (int k = 0; k < U; ++k) {
-    const int64_t vi = a.where + static_cast<int64_t>(k) * kStride;
-    if (vi < v_end) asm volatile("prefetch.global.L1 [%0];" ::"l"(vrow + vi));
-  }
-}
-
 // First column holding `target` among this thread's elements, from the chunk
 // recorded in `where` (re-read from memory); kNone when the thread's maximum
 // is not `target`.
@@ -683,7 +669,6 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   float cur_x = 0.0f;
   if (writer) cur_id = __ldg(p.ids + row) - (kMode == Mode::kRecord ? p.vocab_offset : 0);
   stream_row<T, kRep, kThreads, U>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
-  prefetch_chunk<T, kThreads, U>(a, rowp, head, v_end);  // under the merges below
   if (writer && cur_id >= 0 && cur_id < V) cur_x = VT::scalar(rowp, cur_id);
   Partial mine{a.m, a.om, a.off, a.s0 + a.s1};
   const Partial cta = block_merge(mine, warp_parts, &cta_part);
@@ -801,7 +786,6 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRep ? 7 : 0) display_stats_ro
   if (lane == 0) load_current<T, kMode>(p, row, rowp, V, cur_id, cur_x);
   stream_row<T, kRep, 32, U>(rowp, head, 0, nvec, head, tail_beg, V, pt, a, lane);
   pdl_trigger();
-  prefetch_chunk<T, 32, U>(a, rowp, head, nvec);
   Partial fin{a.m, a.om, a.off, a.s0 + a.s1};
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) fin = merge(fin, shfl_xor(fin, d));
