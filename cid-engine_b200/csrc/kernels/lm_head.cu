@@ -536,349 +536,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// The CTA-pair kernel: tcgen05.mma.cta_group::2, a 256 x 256 tile per pair
-// ---------------------------------------------------------------------------
-//
-// A cluster of two CTAs computes one 256-row x 256-column tile: CTA r stages
-// its own 128 hidden rows and weight rows [128 r, 128 r + 128) of the tile
-// (16 KiB each per 64-wide K slice), the leader (rank 0) issues
-// tcgen05.mma.cta_group::2 (M = 256, N = 256), which reads A and B from both
-// CTAs' shared memory at the same offsets and leaves each CTA's 128 rows x 256
-// columns in its own TMEM.  Per FLOP that is a third less shared-memory fill
-// than the single-CTA 128 x 256 tile.  No load uses cluster multicast: each
-// CTA's TMA names the leader's full barrier (.cta_group::2 completes the
-// transaction bytes there), MMA completion is committed to both CTAs'
-// barriers (tcgen05.commit .multicast::cluster), and the peer's epilogue
-// warps release an accumulator to the leader with remote mbarrier arrives.
-
-constexpr int kPairStages = 6;
-constexpr uint32_t kPairStageA = kBM * kBK * 2;         // 16 KiB: this CTA's hidden rows
-constexpr uint32_t kPairStageB = (kBN / 2) * kBK * 2;   // 16 KiB: this CTA's half of the tile
-constexpr uint32_t kPairStageBytes = kPairStageA + kPairStageB;
-constexpr size_t kPairSmemBytes = kPairStages * size_t{kPairStageBytes} + 1024 + 256;
-constexpr int kPairRowGroup = 16;  // 256-row blocks per raster group (as 32 single blocks)
-// tcgen05.mma kind::f16, D f32, A/B bf16 K-major, N = 256, M = 256 (the pair)
-constexpr uint32_t kPairIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
-                                (uint32_t((2 * kBM) >> 4) << 24);
-// shared::cluster address bit of the CTA rank in a two-CTA cluster: cleared,
-// an address names the leader's copy of the same variable
-constexpr uint32_t kPeerBitMask = 0xFEFFFFFFu;
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void pair_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" :::
-                   "memory");
-}
-
-// try_wait with cluster-scope acquire (arrivals may come from the peer CTA)
-__device__ __forceinline__ bool mbar_try_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
-                                                  volatile int* abort,
-                                                  unsigned long long limit_ns) {
-  if (mbar_try_cluster(bar, parity)) return true;
-  const unsigned long long t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_cluster(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (abort != nullptr && *abort) return false;
-      if (global_ns() - t0 > limit_ns) return false;
-    }
-  }
-}
-
-// Arrival on the leader's copy of `bar` (release at cluster scope).
-__device__ __forceinline__ void mbar_arrive_leader(uint64_t* bar) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(smem_u32(bar)));
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote)
-               : "memory");
-}
-
-// 2-D TMA load into this CTA's shared memory whose transaction bytes
-// complete on the leader's barrier.
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int32_t x,
-                                                 int32_t y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar) & kPeerBitMask)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a, uint64_t b,
-                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(kPairIdesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrives on `bar` in both CTAs of the pair once the MMAs issued so far are done.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
-  const uint16_t mask = 0x3;
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(smem_u32(bar)),
-      "h"(mask)
-      : "memory");
-}
-
-__device__ __forceinline__ void pair_unit_coords(const LmParams& p, int64_t u, int64_t& rb,
-                                                 int64_t& vg) {
-  const int64_t per_group = int64_t{kPairRowGroup} * p.groups;
-  const int64_t gi = u / per_group;
-  const int64_t first = gi * kPairRowGroup;
-  const int64_t rows_in = p.row_blocks - first < kPairRowGroup ? p.row_blocks - first : kPairRowGroup;
-  const int64_t local = u - gi * per_group;
-  rb = first + local % rows_in;
-  vg = local / rows_in;
-}
-
-__global__ void __launch_bounds__(kThreads, 1)
-    lm_head_pair_kernel(const __grid_constant__ CUtensorMap map_a,
-                        const __grid_constant__ CUtensorMap map_b, LmParams p) {
-  extern __shared__ unsigned char smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-byte aligned
-  unsigned char* stage_a = smem;
-  unsigned char* stage_b = smem + kPairStages * kPairStageA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
-  uint64_t* empty = full + kPairStages;
-  uint64_t* acc_full = empty + kPairStages;
-  uint64_t* acc_empty = acc_full + kAccBufs;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + kAccBufs);
-  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const bool leader = rank == 0;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairStages; ++s) {
-      mbar_init(&full[s], 1);   // the leader's expect_tx arrival (leader only)
-      mbar_init(&empty[s], 1);  // one MMA commit per use
-    }
-    for (int b = 0; b < kAccBufs; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);  // four epilogue warps of each CTA (leader only)
-    }
-    *abort = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  }
-  __syncthreads();
-  pair_sync();  // both CTAs' barriers are initialised before any remote use
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const int64_t cid = cluster_id_x(), ncl = nclusters_x();
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer (both CTAs) ----------------
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
-      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
-      int s = 0;
-      uint32_t ph = 0;
-      uint32_t issued = 0, issue_par = 0;
-      bool ok = true;
-      for (int64_t u = cid; ok && u < p.units; u += ncl) {
-        int64_t rb, vg;
-        pair_unit_coords(p, u, rb, vg);
-        const int64_t t0 = vg * p.group_tiles;
-        const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
-        for (int64_t t = t0; ok && t < t1; ++t) {
-          for (int64_t kt = 0; kt < p.ktiles; ++kt) {
-            if (!mbar_wait_cluster(&empty[s], ph ^ 1u, abort, kWaitNs)) {
-              if (!*abort) raise_abort(abort, p.status);
-              ok = false;
-              break;
-            }
-            if (leader) mbar_expect_tx(&full[s], 2 * kPairStageBytes);
-            tma_load_2d_pair(stage_a + s * kPairStageA, &map_a, static_cast<int32_t>(kt * kBK),
-                             static_cast<int32_t>(rb * 2 * kBM + rank * kBM), &full[s]);
-            tma_load_2d_pair(stage_b + s * kPairStageB, &map_b, static_cast<int32_t>(kt * kBK),
-                             static_cast<int32_t>(t * kBN + rank * (kBN / 2)), &full[s]);
-            issued |= 1u << s;
-            issue_par = (issue_par & ~(1u << s)) | (ph << s);
-            if (++s == kPairStages) {
-              s = 0;
-              ph ^= 1u;
-            }
-          }
-        }
-      }
-      // the leader's full barriers complete only once both CTAs' copies landed
-      if (leader)
-        for (int i = 0; i < kPairStages; ++i)
-          if (issued & (1u << i)) mbar_wait_cluster(&full[i], (issue_par >> i) & 1u, nullptr, kDrainNs);
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && leader) {
-      // ---------------- MMA issuer (leader) ----------------
-      int s = 0, buf = 0;
-      uint32_t ph = 0, aph = 0;
-      uint64_t* last_bar = nullptr;
-      uint32_t last_par = 0;
-      bool ok = true;
-      for (int64_t u = cid; ok && u < p.units; u += ncl) {
-        int64_t rb, vg;
-        pair_unit_coords(p, u, rb, vg);
-        const int64_t t0 = vg * p.group_tiles;
-        const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
-        for (int64_t t = t0; ok && t < t1; ++t) {
-          if (!mbar_wait_cluster(&acc_empty[buf], aph ^ 1u, abort, kWaitNs)) {
-            if (!*abort) raise_abort(abort, p.status);
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kBN);
-          for (int64_t kt = 0; kt < p.ktiles; ++kt) {
-            if (!mbar_wait_cluster(&full[s], ph, abort, kWaitNs)) {
-              if (!*abort) raise_abort(abort, p.status);
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t a0 = smem_u32(stage_a + s * kPairStageA);
-            const uint32_t b0 = smem_u32(stage_b + s * kPairStageB);
-#pragma unroll
-            for (int kk = 0; kk < kBK / kUmmaK; ++kk)
-              umma_bf16_pair(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32),
-                             (kt | kk) != 0 ? 1u : 0u);
-            umma_commit_pair(&empty[s]);  // frees the stage in both CTAs
-            last_bar = &empty[s];
-            last_par = ph;
-            if (++s == kPairStages) {
-              s = 0;
-              ph ^= 1u;
-            }
-          }
-          if (!ok) break;
-          umma_commit_pair(&acc_full[buf]);  // both CTAs' halves of the tile are complete
-          last_bar = &acc_full[buf];
-          last_par = aph;
-          if (++buf == kAccBufs) {
-            buf = 0;
-            aph ^= 1u;
-          }
-        }
-      }
-      if (last_bar != nullptr) mbar_wait_cluster(last_bar, last_par, nullptr, kDrainNs);
-    }
-  } else {
-    // ---------------- epilogue: thread = row, TMEM lane = row ----------------
-    const int quarter = warp & 3;
-    const int row_in_block = quarter * 32 + lane;
-    int buf = 0;
-    uint32_t aph = 0;
-    bool ok = true;
-    for (int64_t u = cid; ok && u < p.units; u += ncl) {
-      int64_t rb, vg;
-      pair_unit_coords(p, u, rb, vg);
-      const int64_t t0 = vg * p.group_tiles;
-      const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
-      const int64_t row = rb * 2 * kBM + static_cast<int64_t>(rank) * kBM + row_in_block;
-      const bool valid = row < p.rows;
-      const int64_t c_lo = t0 * kBN;
-      const int64_t c_hi = t1 * kBN < p.vocab ? t1 * kBN : p.vocab;
-      const int64_t id = valid ? p.ids[row] - p.vocab_offset : -1;
-      const int64_t local_id = (id >= c_lo && id < c_hi) ? id : INT64_MIN / 2;
-      RowState st{-INFINITY, -INFINITY, 0.0f, 0.0f, -1, -1, 0.0f};
-      for (int64_t t = t0; t < t1; ++t) {
-        bool got = mbar_wait_cluster(&acc_full[buf], aph, abort, kWaitNs);
-        got = __all_sync(0xffffffffu, got);
-        if (!got) {
-          if (lane == 0 && !*abort) raise_abort(abort, p.status);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t taddr =
-            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * kBN);
-        uint32_t ra[32], rb2[32];
-        tmem_issue32(taddr, ra);
-        tmem_wait32(ra);
-#pragma unroll
-        for (int c = 0; c < kBN / 32; c += 2) {
-          tmem_issue32(taddr + static_cast<uint32_t>((c + 1) * 32), rb2);
-          fold32(st, ra, t * kBN + c * 32, p.vocab, local_id, p.round_bf16);
-          tmem_wait32(rb2);
-          if (c + 2 < kBN / 32) tmem_issue32(taddr + static_cast<uint32_t>((c + 2) * 32), ra);
-          fold32(st, rb2, t * kBN + (c + 1) * 32, p.vocab, local_id, p.round_bf16);
-          if (c + 2 < kBN / 32) tmem_wait32(ra);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_leader(&acc_empty[buf]);  // local arrive in the leader
-        if (++buf == kAccBufs) {
-          buf = 0;
-          aph ^= 1u;
-        }
-      }
-      if (!ok) break;
-      if (valid) {
-        cid_shard_record_t rec;
-        rec.max_logit = st.m;
-        const bool special = !(st.m > -INFINITY && st.m < INFINITY) || st.s != st.s;
-        if (special) {
-          const int64_t local = st.first_nan >= 0 ? st.first_nan : (st.where >= 0 ? st.where : c_lo);
-          rec.sum_exp = st.m == -INFINITY ? 0.0f : __int_as_float(0x7fffffff);
-          rec.index = static_cast<int32_t>(p.vocab_offset + local) |
-                      (st.first_nan >= 0 ? static_cast<int32_t>(0x80000000u) : 0);
-        } else {
-          const float top = ex2(fmaf(st.m, kLog2e, -st.off));
-          rec.sum_exp = __fdiv_rn(st.s, top);
-          rec.index = static_cast<int32_t>(p.vocab_offset + st.where);
-        }
-        rec.current = local_id >= 0 ? st.cur : 0.0f;
-        p.records[vg * p.rows + row] = rec;
-      }
-    }
-  }
-
-  __syncthreads();
-  pair_sync();  // no remote arrive or copy targets a CTA that has left
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kTmemCols)
-                 : "memory");
-  }
-}
-
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {  // thread-safe one-time init
     void* ptr = nullptr;
@@ -911,17 +568,13 @@ struct Plan {
   int64_t tiles, group_tiles, groups, row_blocks, units;
 };
 
-// The CTA-pair kernel serves launches of at least one full 256-row block.
-bool use_pair(int64_t rows) { return rows >= 2 * kBM; }
-
 Plan plan(int64_t rows, int64_t vocab) {
   Plan pl;
   pl.tiles = (vocab + kBN - 1) / kBN;
   pl.group_tiles = (pl.tiles + kMaxGroups - 1) / kMaxGroups;
   if (pl.group_tiles < 4) pl.group_tiles = 4;
   pl.groups = (pl.tiles + pl.group_tiles - 1) / pl.group_tiles;
-  const int64_t block = use_pair(rows) ? 2 * kBM : kBM;
-  pl.row_blocks = (rows + block - 1) / block;
+  pl.row_blocks = (rows + kBM - 1) / kBM;
   pl.units = pl.row_blocks * pl.groups;
   return pl;
 }
@@ -953,10 +606,9 @@ int launch_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const v
   if (rows > INT32_MAX - kBM) return CID_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < cid_lm_head_workspace_bytes(rows, vocab)) return CID_ERR_SCRATCH_LIMIT;
   const Plan pl = plan(rows, vocab);
-  const bool pair = use_pair(rows);
   CUtensorMap map_a, map_b;
   if (!make_map(&map_a, hidden, hidden_dim, rows, kBM) ||
-      !make_map(&map_b, weight, hidden_dim, vocab, pair ? kBN / 2 : kBN))
+      !make_map(&map_b, weight, hidden_dim, vocab, kBN))
     return CID_ERR_INVALID_ARGUMENT;
   LmParams p = {};
   p.rows = rows;
@@ -972,37 +624,14 @@ int launch_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const v
   p.records = static_cast<cid_shard_record_t*>(workspace);
   p.status = status;
   p.round_bf16 = round_bf16 ? 1 : 0;
-  int rc = CID_OK;
-  if (pair) {
-    cudaError_t e = cudaFuncSetAttribute(lm_head_pair_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kPairSmemBytes));
-    if (e != cudaSuccess) return record_cuda_error(e);
-    const int64_t pairs = sm_count() / 2;
-    const int64_t clusters = pl.units < pairs ? pl.units : pairs;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters));
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kPairSmemBytes;
-    cfg.stream = as_stream(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    rc = record_cuda_error(cudaLaunchKernelEx(&cfg, lm_head_pair_kernel, map_a, map_b, p));
-  } else {
-    cudaError_t e = cudaFuncSetAttribute(lm_head_stats_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kSmemBytes));
-    if (e != cudaSuccess) return record_cuda_error(e);
-    const int64_t grid = pl.units < sm_count() ? pl.units : sm_count();
-    lm_head_stats_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, as_stream(stream)>>>(
-        map_a, map_b, p);
-    rc = launch_result();
-  }
+  cudaError_t e = cudaFuncSetAttribute(lm_head_stats_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kSmemBytes));
+  if (e != cudaSuccess) return record_cuda_error(e);
+  const int64_t grid = pl.units < sm_count() ? pl.units : sm_count();
+  lm_head_stats_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, as_stream(stream)>>>(
+      map_a, map_b, p);
+  const int rc = launch_result();
   if (rc != CID_OK) return rc;
   groups = static_cast<int>(pl.groups);
   for (int64_t g = 0; g < pl.groups; ++g) offsets[g] = vocab_offset + g * pl.group_tiles * kBN;

@@ -9,7 +9,9 @@ logits — as f32 for ``round_bf16=False``, rounded to bf16 for
 reference GEMM's, so: confidences within rtol 1e-4 (f32) / 1e-2 (bf16: a
 logit can round to the neighbouring bf16 value); the predicted column must
 hold the row maximum of the reference logits within the accumulation error
-(f32: 1e-3 absolute; bf16: one bf16 ulp of the maximum).  Exact structure
+(f32: 1e-3 absolute; bf16: one bf16 ulp of the maximum), and must equal the
+reference argmax exactly on every row whose maximum is unique by more than
+that band.  Exact structure
 is checked exactly: duplicated weight rows give bit-identical columns, and
 the lower column must win.
 """
@@ -59,8 +61,13 @@ def _check(ids, h, w, round_bf16):
     got = lf.gather(1, pred.view(-1, 1)).view(-1)
     tol = (rowmax.abs() * 2.0**-7 + 1e-6) if round_bf16 else torch.full_like(rowmax, 1e-3)
     assert bool(((rowmax - got) <= tol).all()), "predicted column does not hold the row maximum"
-    agree = (pred == e_pred).float().mean().item()
-    assert agree > 0.95, f"argmax agreement {agree}"
+    # exact argmax wherever the reference logits' maximum is unique by more
+    # than the accumulation-order band (bf16: one ulp of the maximum; f32:
+    # 1e-3): only there can the tensor-core sum not reorder the top two
+    second = lf.topk(2, dim=1).values[:, 1]
+    clear = (rowmax - second) > tol
+    assert bool(clear.any())
+    assert torch.equal(pred[clear], e_pred[clear]), "argmax differs on a clear maximum"
     return conf, pred, cur
 
 
