@@ -59,7 +59,15 @@ LOOP = dict(B=256, L=512, V=32000, S=128, F=4, Rv=3, Rr=6, H=512, K=12, steps=64
 # [32, 1024, 128256] step (warp per row), measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on a [1, 10240, 128256] bf16 launch and divided by
 # its 10240 rows; traffic grows in proportion to rows.
-NCU_TRAFFIC_PER_ROW = (2_631_003_000 + 4_521_216) / 10240
+NCU_TRAFFIC_PER_ROW = (2_632_891_000 + 4_414_848) / 10240
+# The same for the record kernel on a rank's shard rows at N ranks of the
+# [64, 4096, 152064] workload (152064 / N columns), from ncu captures of
+# `bench.py --profile-case shard<N>` (8192 N rows each, 2.5 GB), per row.
+NCU_SHARD_TRAFFIC_PER_ROW: dict[int, float] = {
+    2: (2_499_850_240 + 3_524_608) / 16384,
+    4: (2_504_554_496 + 3_683_072) / 32768,
+    8: (2_505_670_912 + 4_321_280) / 65536,
+}
 
 
 def _peaks() -> tuple[float, str]:
@@ -414,7 +422,8 @@ def bench_single(args) -> dict:
                    "batch": B, "tokens": L, "vocab": V, "parallelism": "single GPU",
                    "l2": "inputs 8.4 GB per step >> 126 MB L2; no flush needed"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "frac_of_8TBps_nominal": round(achieved / 8000.0, 4), "traffic": traffic,
                      "kernel": "display_stats_rows_kernel<bf16> (warp per row)", "peak_kind": peak_kind,
                      "kernel_ms": round(kern_ms, 4),
                      "algorithmic_bytes_per_launch": alg_bytes},
@@ -1332,7 +1341,9 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
                        "l2": f"{shard_bytes / 1e9:.1f} GB per rank per step >> 126 MB L2"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
-                         "frac_of_8TBps_nominal": round(achieved / 8000.0, 4), "traffic": None,
+                         "frac_of_8TBps_nominal": round(achieved / 8000.0, 4),
+                         "traffic": (round(NCU_SHARD_TRAFFIC_PER_ROW[world] * rows)
+                                     if world in NCU_SHARD_TRAFFIC_PER_ROW else None),
                          "kernel": "display_stats_rows_kernel<bf16, records> (per rank, max over ranks"
                                    + ("; then pushed to the peers' inboxes)" if peers else ")"),
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
@@ -1416,6 +1427,18 @@ def profile_case(name: str) -> None:
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": name, "mean_conf": float(c.mean())}))
         return
+    if name.startswith("shard"):  # a rank's record kernel at N ranks: rows of 152064 / N, 2.5 GB
+        world = int(name[5:])
+        V = SHARDED["V"] // world
+        n = 8192 * world
+        g = torch.Generator(device="cuda").manual_seed(world)
+        lg = torch.randn((1, n, V), generator=g, device="cuda", dtype=torch.bfloat16) * 2
+        ids = torch.randint(0, SHARDED["V"], (1, n), device="cuda")
+        for _ in range(3):
+            r = cid_engine.display_shard_records(ids, lg, vocab_offset=0, total_vocab=SHARDED["V"])
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "checksum": int(r[:, 2].sum())}))
+        return
     shape = {"cta": (1, 4096, 128256), "rows": (1, 10240, 128256),
              "rows_records": (1, 10240, 128256)}[name]
     g = torch.Generator(device="cuda").manual_seed(1)
@@ -1448,7 +1471,7 @@ def main() -> None:
     ap.add_argument("--cpu-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--ref-cuda-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--profile-case", choices=("cta", "rows", "rows_records", "lm_head", "refine", "corruption",
-                             "decode64"), default=None,
+                             "decode64", "shard2", "shard4", "shard8"), default=None,
                     help="run a small statistics case for ncu and exit")
     ap.add_argument("--sample-b", type=int, default=1)
     ap.add_argument("--sample-l", type=int, default=1024)
