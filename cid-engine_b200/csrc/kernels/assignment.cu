@@ -153,10 +153,14 @@ extern "C" int cid_batched_linear_assignment(cid_dtype_t cost_dtype, const void*
                                              int64_t rows, int64_t columns, int64_t* out,
                                              uint32_t* status, void* stream) {
   if (!is_float_dtype(cost_dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
-  if (batch < 0 || rows < 0 || columns < 0 || rows > columns || columns > kMaxColumns)
+  if (batch < 0 || batch > kMaxRows || rows < 0 || columns < 0 || rows > columns ||
+      columns > kMaxColumns)
     return CID_ERR_INVALID_ARGUMENT;  // csrc/ops.cpp:71-86
+  if (misaligned({{costs, static_cast<size_t>(dtype_size(cost_dtype))}, {row_counts, 8},
+                  {out, 8}, {status, 4}}))
+    return CID_ERR_MISALIGNED;
   if (batch == 0 || rows == 0) return CID_OK;
-  if (!costs || !row_counts || !out) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({costs, row_counts, out})) return CID_ERR_INVALID_ARGUMENT;
   AssignParams p{cost_dtype, costs, row_counts, batch, rows, columns, out, status};
   const int64_t blocks = (batch + kWarpsPerBlock - 1) / kWarpsPerBlock;
   assignment_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, as_stream(stream)>>>(p);

@@ -5,7 +5,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstdint>
+#include <initializer_list>
 
 #include "cid_engine_b200.h"
 
@@ -41,6 +43,55 @@ inline int dtype_size(cid_dtype_t dt) {
     case CID_DTYPE_I16: return 2;
     default: return 1;
   }
+}
+
+// Argument checks shared by the entry points.  Each entry point checks, in
+// this order and before any CUDA call: its dtype codes
+// (CID_ERR_UNSUPPORTED_DTYPE); its scalar arguments and extents
+// (CID_ERR_INVALID_ARGUMENT: negative extents, element counts that overflow
+// int64, row counts above kMaxRows); the alignment of every non-NULL pointer
+// to its element size (CID_ERR_MISALIGNED); then it returns CID_OK when there
+// is no work, and otherwise requires every array of non-zero extent to be
+// non-NULL (CID_ERR_INVALID_ARGUMENT).
+
+// Largest row (or batch) count of any entry point: grid dimensions and the
+// kernels' 32-bit row indexes stay in range.
+constexpr int64_t kMaxRows = INT32_MAX;
+// Largest element count of any array argument (2^58): byte offsets of
+// elements up to 16 bytes wide stay within int64.
+constexpr int64_t kMaxCount = int64_t{1} << 58;
+
+// a * b as an element count: false when either is negative or the product
+// does not fit in int64 (callers compare the product with kMaxCount).
+inline bool count_ok(int64_t a, int64_t b, int64_t* product = nullptr) {
+  int64_t r = 0;
+  if (a < 0 || b < 0 || __builtin_mul_overflow(a, b, &r)) return false;
+  if (product) *product = r;
+  return true;
+}
+
+// a * b * c likewise.
+inline bool count_ok(int64_t a, int64_t b, int64_t c, int64_t* product = nullptr) {
+  int64_t ab = 0;
+  return count_ok(a, b, &ab) && count_ok(ab, c, product);
+}
+
+struct Aligned {
+  const void* ptr;
+  size_t bytes;
+};
+
+// True when a non-NULL pointer of the list is not a multiple of its bytes.
+inline bool misaligned(std::initializer_list<Aligned> ptrs) {
+  for (const Aligned& a : ptrs)
+    if (a.ptr != nullptr && reinterpret_cast<uintptr_t>(a.ptr) % a.bytes != 0) return true;
+  return false;
+}
+
+inline bool any_null(std::initializer_list<const void*> ptrs) {
+  for (const void* p : ptrs)
+    if (p == nullptr) return true;
+  return false;
 }
 
 // Checks the launch that was just enqueued.

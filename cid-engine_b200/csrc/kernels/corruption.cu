@@ -384,8 +384,33 @@ __global__ void __launch_bounds__(kBT) display_corrupt_kernel(DisplayCorruptPara
 
 using namespace cid;
 
+namespace {
+
+// The arguments both masked-diffusion entry points share (csrc/ops.cpp:406,
+// :416-420): a non-empty batch x tokens, 0 < min <= max <= 1, aligned and
+// non-NULL arrays.
+int check_masked(const int64_t* clean_ids, const float* ratio_random, const float* mask_random,
+                 int64_t batch, int64_t tokens, double min_mask_ratio, double max_mask_ratio,
+                 const int64_t* corrupted, const uint8_t* masked, const float* ratio,
+                 const float* metrics) {
+  int64_t count = 0;
+  if (batch <= 0 || tokens <= 0 || batch > kMaxRows || !count_ok(batch, tokens, &count) ||
+      count > kMaxCount)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (!(min_mask_ratio > 0.0 && min_mask_ratio <= max_mask_ratio && max_mask_ratio <= 1.0))
+    return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{clean_ids, 8}, {ratio_random, 4}, {mask_random, 4}, {corrupted, 8},
+                  {ratio, 4}, {metrics, 4}}))
+    return CID_ERR_MISALIGNED;
+  if (any_null({clean_ids, ratio_random, mask_random, corrupted, masked, ratio, metrics}))
+    return CID_ERR_INVALID_ARGUMENT;
+  return CID_OK;
+}
+
+}  // namespace
+
 extern "C" size_t cid_masked_diffusion_workspace_bytes(int64_t batch) {
-  return batch > 0 ? static_cast<size_t>(batch) * sizeof(int64_t) : 0;
+  return batch > 0 && batch <= kMaxRows ? static_cast<size_t>(batch) * sizeof(int64_t) : 0;
 }
 
 extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const float* ratio_random,
@@ -394,13 +419,11 @@ extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const floa
                                             double min_mask_ratio, double max_mask_ratio,
                                             int64_t* corrupted, uint8_t* masked, float* ratio,
                                             float* metrics, void* workspace, void* stream) {
-  if (batch <= 0 || tokens <= 0 || batch > INT_MAX) return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:406
-  if (!(min_mask_ratio > 0.0 && min_mask_ratio <= max_mask_ratio && max_mask_ratio <= 1.0))
-    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:416-420
-  if (!clean_ids || !ratio_random || !mask_random || !corrupted || !masked || !ratio ||
-      !metrics || !workspace)
-    return CID_ERR_INVALID_ARGUMENT;
-  if (reinterpret_cast<uintptr_t>(workspace) % 16 != 0) return CID_ERR_MISALIGNED;
+  int rc = check_masked(clean_ids, ratio_random, mask_random, batch, tokens, min_mask_ratio,
+                        max_mask_ratio, corrupted, masked, ratio, metrics);
+  if (rc != CID_OK) return rc;
+  if (misaligned({{workspace, 16}})) return CID_ERR_MISALIGNED;
+  if (workspace == nullptr) return CID_ERR_INVALID_ARGUMENT;
   MaskedParams p;
   p.clean = clean_ids;
   p.ratio_random = ratio_random;
@@ -416,7 +439,7 @@ extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const floa
   p.metrics = metrics;
   p.counts = static_cast<int64_t*>(workspace);
   cudaStream_t s = as_stream(stream);
-  int rc = launch_masked_rows(p, s);
+  rc = launch_masked_rows(p, s);
   if (rc != CID_OK) return rc;
   return launch_pdl(masked_metrics_kernel, dim3(1), dim3(kT), 0, s,
                     static_cast<const int64_t*>(p.counts), static_cast<const float*>(ratio), batch,
@@ -475,14 +498,12 @@ extern "C" int cid_masked_diffusion_corrupt_no_alloc(
     int64_t batch, int64_t tokens, int64_t mask_token_id, double min_mask_ratio,
     double max_mask_ratio, int64_t* corrupted, uint8_t* masked, float* ratio, float* metrics,
     void* stream) {
-  if (batch <= 0 || tokens <= 0) return CID_ERR_INVALID_ARGUMENT;
   if (batch > CID_NO_ALLOC_MAX_BATCH) return CID_ERR_SCRATCH_LIMIT;
-  if (!(min_mask_ratio > 0.0 && min_mask_ratio <= max_mask_ratio && max_mask_ratio <= 1.0))
-    return CID_ERR_INVALID_ARGUMENT;
-  if (!clean_ids || !ratio_random || !mask_random || !corrupted || !masked || !ratio || !metrics)
-    return CID_ERR_INVALID_ARGUMENT;
+  int rc = check_masked(clean_ids, ratio_random, mask_random, batch, tokens, min_mask_ratio,
+                        max_mask_ratio, corrupted, masked, ratio, metrics);
+  if (rc != CID_OK) return rc;
   int64_t* scratch = nullptr;
-  int rc = no_alloc_scratch(&scratch);
+  rc = no_alloc_scratch(&scratch);
   if (rc != CID_OK) return rc;
   MaskedParams p;
   p.clean = clean_ids;
@@ -514,8 +535,19 @@ extern "C" int cid_thought_corrupt(cid_dtype_t sem_dtype, const void* semantic,
                                    void* stream) {
   if (!is_float_dtype(sem_dtype) || !is_float_dtype(t_dtype) || !is_known_dtype(occ_dtype))
     return CID_ERR_UNSUPPORTED_DTYPE;
-  if (rows < 0 || hidden < 0 || rows > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+  int64_t count = 0;
+  if (!count_ok(rows, hidden, &count) || rows > kMaxRows || count > kMaxCount)
+    return CID_ERR_INVALID_ARGUMENT;
+  const size_t es = static_cast<size_t>(dtype_size(sem_dtype));
+  if (misaligned({{semantic, es}, {epsilon, es}, {corrupted, es}, {local_noise, es},
+                  {masked_epsilon, es}, {timesteps, static_cast<size_t>(dtype_size(t_dtype))},
+                  {occupancy, static_cast<size_t>(dtype_size(occ_dtype))}}))
+    return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
+  // rows x hidden arrays may be NULL when hidden == 0
+  if (any_null({timesteps, occupancy, local_noise}) ||
+      (hidden > 0 && any_null({semantic, epsilon, corrupted, masked_epsilon})))
+    return CID_ERR_INVALID_ARGUMENT;
   ThoughtParams p{sem_dtype, semantic, t_dtype, timesteps, occ_dtype, occupancy, epsilon,
                   rows, hidden, corrupted, local_noise, masked_epsilon};
   return launch_pdl(thought_kernel, dim3(static_cast<unsigned>(rows)), dim3(kT), 0,
@@ -533,16 +565,29 @@ extern "C" int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype
                                    double replacement_fraction, int64_t* corrupted,
                                    int64_t* labels, uint8_t* masked, uint8_t* replaced,
                                    void* stream) {
-  if (!(replacement_fraction >= 0.0 && replacement_fraction <= 1.0))
-    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:320-322
   const int replace = replacement_fraction > 0.0;
-  if (replace && (vocab_size < 3 || !replacement_random || !replacement_offsets))
-    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:343-348
   if (!is_float_dtype(t_dtype) || !is_known_dtype(elig_dtype) || !is_float_dtype(rand_dtype) ||
       (replace && !is_float_dtype(repl_dtype)))
     return CID_ERR_UNSUPPORTED_DTYPE;
-  if (batch < 0 || tokens < 0 || batch > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+  if (!(replacement_fraction >= 0.0 && replacement_fraction <= 1.0))
+    return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:320-322
+  if (replace && vocab_size < 3) return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:343-345
+  int64_t count = 0;
+  if (!count_ok(batch, tokens, &count) || batch > kMaxRows || count > kMaxCount)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{token_ids, 8}, {timesteps, static_cast<size_t>(dtype_size(t_dtype))},
+                  {eligible, static_cast<size_t>(dtype_size(elig_dtype))},
+                  {corruption_random, static_cast<size_t>(dtype_size(rand_dtype))},
+                  {corrupted, 8}, {labels, 8}}) ||
+      (replace && misaligned({{replacement_random, static_cast<size_t>(dtype_size(repl_dtype))},
+                              {replacement_offsets, 8}})))
+    return CID_ERR_MISALIGNED;
   if (batch == 0 || tokens == 0) return CID_OK;
+  // the replacement inputs are read only when replacement_fraction > 0 (ops.cpp:346-348)
+  if (any_null({token_ids, timesteps, eligible, corruption_random, corrupted, labels, masked,
+                replaced}) ||
+      (replace && any_null({replacement_random, replacement_offsets})))
+    return CID_ERR_INVALID_ARGUMENT;
   DisplayCorruptParams p{token_ids, t_dtype, timesteps, elig_dtype, eligible, rand_dtype,
                          corruption_random, repl_dtype, replacement_random,
                          replacement_offsets, batch, tokens, mask_token_id, eos_token_id,

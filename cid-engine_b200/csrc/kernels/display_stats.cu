@@ -1134,13 +1134,46 @@ int dispatch_stats(cid_dtype_t dtype, const StatsParams& prm, cudaStream_t strea
   }
 }
 
+// The dtype, extents and alignment of a logits argument: rows x vocab with
+// row r at logits + r*row_stride (row_stride >= vocab), the whole span
+// (rows-1)*row_stride + vocab within kMaxCount elements.
 int check_logits(cid_dtype_t dtype, const void* logits, int64_t row_stride, int64_t rows,
                  int64_t vocab) {
   if (!is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
-  if (rows < 0 || vocab <= 0 || vocab > INT_MAX - 16) return CID_ERR_INVALID_ARGUMENT;
-  if (rows > 0 && (logits == nullptr || row_stride < vocab)) return CID_ERR_INVALID_ARGUMENT;
-  if (reinterpret_cast<uintptr_t>(logits) % dtype_size(dtype) != 0) return CID_ERR_MISALIGNED;
+  if (rows < 0 || rows > kMaxRows || vocab <= 0 || vocab > INT_MAX - 16)
+    return CID_ERR_INVALID_ARGUMENT;
+  int64_t span = 0;
+  if (rows > 0 && (row_stride < vocab || !count_ok(rows - 1, row_stride, &span) ||
+                   span > kMaxCount - vocab))
+    return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{logits, static_cast<size_t>(dtype_size(dtype))}})) return CID_ERR_MISALIGNED;
   return CID_OK;
+}
+
+// Host shard offsets of a record merge: world + 1 ascending column offsets
+// within [0, INT_MAX] (the records hold 32-bit global columns).
+int check_offsets(const int64_t* offsets, int world, int max_world, int64_t (&out)[kMaxWorld + 1]) {
+  if (world < 1 || world > max_world || offsets == nullptr) return CID_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r <= world; ++r) {
+    out[r] = offsets[r];
+    if (r > 0 && out[r] < out[r - 1]) return CID_ERR_INVALID_ARGUMENT;
+  }
+  if (out[0] < 0 || out[world] > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+  return CID_OK;
+}
+
+// The vocabulary range of a shard: [vocab_offset, vocab_offset + shard_vocab)
+// inside [0, total_vocab), total_vocab <= INT_MAX.
+bool shard_range_ok(int64_t shard_vocab, int64_t vocab_offset, int64_t total_vocab) {
+  return shard_vocab > 0 && vocab_offset >= 0 && total_vocab <= INT_MAX &&
+         total_vocab >= shard_vocab && vocab_offset <= total_vocab - shard_vocab;
+}
+
+// The statistics outputs of one call.
+bool stats_outputs_misaligned(const int64_t* ids, const float* confidence,
+                              const int64_t* predicted, const float* current,
+                              const uint32_t* status) {
+  return misaligned({{ids, 8}, {confidence, 4}, {predicted, 8}, {current, 4}, {status, 4}});
 }
 
 }  // namespace
@@ -1155,8 +1188,11 @@ extern "C" int cid_display_token_statistics(cid_dtype_t dtype, const void* logit
                                             uint32_t* status, void* stream) {
   int rc = check_logits(dtype, logits, row_stride, rows, vocab);
   if (rc != CID_OK) return rc;
+  if (stats_outputs_misaligned(token_ids, confidence, predicted, current_confidence, status))
+    return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
-  if (!token_ids || !confidence || !predicted || !current_confidence) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({logits, token_ids, confidence, predicted, current_confidence}))
+    return CID_ERR_INVALID_ARGUMENT;
   StatsParams prm = {};
   prm.logits = logits;
   prm.row_stride = row_stride;
@@ -1176,17 +1212,21 @@ extern "C" int cid_display_token_statistics_with_repetition(
     int64_t batch, int64_t tokens, int64_t vocab, int64_t mask_token_id, int has_eos,
     int64_t eos_token_id, double multiplier, float* confidence, int64_t* predicted,
     float* current_confidence, uint32_t* status, void* stream) {
+  if (!is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
   if (!(multiplier > 0.0 && multiplier <= 1.0)) return CID_ERR_INVALID_ARGUMENT;
-  if (batch < 0 || tokens < 0) return CID_ERR_INVALID_ARGUMENT;
-  const int64_t rows = batch * tokens;
+  int64_t rows = 0;
+  if (!count_ok(batch, tokens, &rows) || rows > kMaxRows) return CID_ERR_INVALID_ARGUMENT;
   if (multiplier == 1.0 || tokens <= 1)  // csrc/ops.cpp:494-496
     return cid_display_token_statistics(dtype, logits, row_stride, token_ids, rows, vocab,
                                         confidence, predicted, current_confidence, status,
                                         stream);
   int rc = check_logits(dtype, logits, row_stride, rows, vocab);
   if (rc != CID_OK) return rc;
+  if (stats_outputs_misaligned(token_ids, confidence, predicted, current_confidence, status))
+    return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
-  if (!token_ids || !confidence || !predicted || !current_confidence) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({logits, token_ids, confidence, predicted, current_confidence}))
+    return CID_ERR_INVALID_ARGUMENT;
   StatsParams prm = {};
   prm.logits = logits;
   prm.row_stride = row_stride;
@@ -1213,10 +1253,10 @@ extern "C" int cid_display_shard_records(cid_dtype_t dtype, const void* logits,
                                          void* stream) {
   int rc = check_logits(dtype, logits, row_stride, rows, shard_vocab);
   if (rc != CID_OK) return rc;
-  if (vocab_offset < 0 || vocab_offset + shard_vocab > total_vocab || total_vocab > INT_MAX)
-    return CID_ERR_INVALID_ARGUMENT;
+  if (!shard_range_ok(shard_vocab, vocab_offset, total_vocab)) return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{token_ids, 8}, {records, 4}, {status, 4}})) return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
-  if (!token_ids || !records) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({logits, token_ids, records})) return CID_ERR_INVALID_ARGUMENT;
   StatsParams prm = {};
   prm.logits = logits;
   prm.row_stride = row_stride;
@@ -1235,17 +1275,15 @@ extern "C" int cid_display_merge_records(const cid_shard_record_t* records, int 
                                          const int64_t* shard_offsets_host,
                                          const int64_t* token_ids, int64_t rows,
                                          cid_shard_record_t* merged, void* stream) {
-  if (world < 1 || world > kMaxWorld || rows < 0 || !shard_offsets_host)
-    return CID_ERR_INVALID_ARGUMENT;
-  if (rows == 0) return CID_OK;
-  if (!records || !token_ids || !merged) return CID_ERR_INVALID_ARGUMENT;
   CombineParams prm = {};
+  int rc = check_offsets(shard_offsets_host, world, kMaxWorld, prm.offsets);
+  if (rc != CID_OK) return rc;
+  if (rows < 0 || rows > kMaxRows) return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{records, 4}, {token_ids, 8}, {merged, 4}})) return CID_ERR_MISALIGNED;
+  if (rows == 0) return CID_OK;
+  if (any_null({records, token_ids, merged})) return CID_ERR_INVALID_ARGUMENT;
   prm.records = records;
   prm.world = world;
-  for (int r = 0; r <= world; ++r) {
-    prm.offsets[r] = shard_offsets_host[r];
-    if (r > 0 && prm.offsets[r] < prm.offsets[r - 1]) return CID_ERR_INVALID_ARGUMENT;
-  }
   prm.ids = token_ids;
   prm.rows = rows;
   prm.stride = rows;
@@ -1262,18 +1300,18 @@ extern "C" int cid_display_combine_records(const cid_shard_record_t* records, in
                                            float* confidence, int64_t* predicted,
                                            float* current_confidence, uint32_t* status,
                                            void* stream) {
-  if (world < 1 || world > kMaxWorld || rows < 0 || !shard_offsets_host)
-    return CID_ERR_INVALID_ARGUMENT;
-  if (rows == 0) return CID_OK;
-  if (!records || !token_ids || !confidence || !predicted || !current_confidence)
-    return CID_ERR_INVALID_ARGUMENT;
   CombineParams prm = {};
+  int rc = check_offsets(shard_offsets_host, world, kMaxWorld, prm.offsets);
+  if (rc != CID_OK) return rc;
+  if (rows < 0 || rows > kMaxRows) return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{records, 4}}) ||
+      stats_outputs_misaligned(token_ids, confidence, predicted, current_confidence, status))
+    return CID_ERR_MISALIGNED;
+  if (rows == 0) return CID_OK;
+  if (any_null({records, token_ids, confidence, predicted, current_confidence}))
+    return CID_ERR_INVALID_ARGUMENT;
   prm.records = records;
   prm.world = world;
-  for (int r = 0; r <= world; ++r) {
-    prm.offsets[r] = shard_offsets_host[r];
-    if (r > 0 && prm.offsets[r] < prm.offsets[r - 1]) return CID_ERR_INVALID_ARGUMENT;
-  }
   prm.ids = token_ids;
   prm.rows = rows;
   prm.stride = rows;
@@ -1344,11 +1382,27 @@ uint32_t* inbox_flags(void* inbox, int world, int64_t capacity) {
                                      inbox_record_bytes(world, capacity));
 }
 
+// The rank arguments of a peer exchange call: 1 <= world <= kMaxPeers,
+// 0 <= rank < world, 1 <= rows <= rows_capacity <= kMaxRows, and `world`
+// non-NULL inbox pointers (4-byte aligned: they hold the flag words).
+int check_peers(int64_t rows, int rank, int world, void* const* inboxes, int64_t rows_capacity) {
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || inboxes == nullptr)
+    return CID_ERR_INVALID_ARGUMENT;
+  // every rank publishes each epoch, so rows == 0 is not a call
+  if (rows < 1 || rows > rows_capacity || rows_capacity > kMaxRows) return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{inboxes, alignof(void*)}})) return CID_ERR_MISALIGNED;
+  for (int q = 0; q < world; ++q) {
+    if (inboxes[q] == nullptr) return CID_ERR_INVALID_ARGUMENT;
+    if (misaligned({{inboxes[q], 4}})) return CID_ERR_MISALIGNED;
+  }
+  return CID_OK;
+}
+
 }  // namespace
 }  // namespace cid
 
 extern "C" size_t cid_peer_inbox_bytes(int world, int64_t rows_capacity) {
-  if (world < 1 || world > kMaxPeers || rows_capacity < 0) return 0;
+  if (world < 1 || world > kMaxPeers || rows_capacity < 0 || rows_capacity > kMaxRows) return 0;
   return inbox_record_bytes(world, rows_capacity) + kInboxTail;
 }
 
@@ -1403,14 +1457,11 @@ extern "C" int cid_display_shard_records_to_peers(
     void* stream) {
   int rc = check_logits(dtype, logits, row_stride, rows, shard_vocab);
   if (rc != CID_OK) return rc;
-  if (vocab_offset < 0 || vocab_offset + shard_vocab > total_vocab || total_vocab > INT_MAX)
-    return CID_ERR_INVALID_ARGUMENT;
-  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !inboxes)
-    return CID_ERR_INVALID_ARGUMENT;
-  if (rows < 1 || rows > rows_capacity || rows > UINT32_MAX || !token_ids)
-    return CID_ERR_INVALID_ARGUMENT;  // every rank publishes, so rows == 0 is not a call
-  for (int q = 0; q < world; ++q)
-    if (!inboxes[q]) return CID_ERR_INVALID_ARGUMENT;
+  if (!shard_range_ok(shard_vocab, vocab_offset, total_vocab)) return CID_ERR_INVALID_ARGUMENT;
+  rc = check_peers(rows, rank, world, inboxes, rows_capacity);
+  if (rc != CID_OK) return rc;
+  if (misaligned({{token_ids, 8}, {status, 4}})) return CID_ERR_MISALIGNED;
+  if (any_null({logits, token_ids})) return CID_ERR_INVALID_ARGUMENT;
   StatsParams prm = {};
   prm.logits = logits;
   prm.row_stride = row_stride;
@@ -1451,20 +1502,20 @@ extern "C" int cid_display_combine_inbox(void* inbox, int world,
                                          double wait_seconds, float* confidence,
                                          int64_t* predicted, float* current_confidence,
                                          uint32_t* status, void* stream) {
-  if (world < 1 || world > kMaxPeers || !shard_offsets_host || !inbox)
-    return CID_ERR_INVALID_ARGUMENT;
-  if (rows < 1 || rows > rows_capacity || !(wait_seconds > 0.0 && wait_seconds <= 60.0))
-    return CID_ERR_INVALID_ARGUMENT;
-  if (!token_ids || !confidence || !predicted || !current_confidence)
-    return CID_ERR_INVALID_ARGUMENT;
   CombineParams prm = {};
+  int rc = check_offsets(shard_offsets_host, world, kMaxPeers, prm.offsets);
+  if (rc != CID_OK) return rc;
+  if (rows < 1 || rows > rows_capacity || rows_capacity > kMaxRows ||
+      !(wait_seconds > 0.0 && wait_seconds <= 60.0))
+    return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{inbox, 4}}) ||
+      stats_outputs_misaligned(token_ids, confidence, predicted, current_confidence, status))
+    return CID_ERR_MISALIGNED;
+  if (any_null({inbox, token_ids, confidence, predicted, current_confidence}))
+    return CID_ERR_INVALID_ARGUMENT;
   prm.records = inbox_records(inbox, world, rows_capacity, epoch & 1u, 0);
   prm.stride = rows_capacity;
   prm.world = world;
-  for (int r = 0; r <= world; ++r) {
-    prm.offsets[r] = shard_offsets_host[r];
-    if (r > 0 && prm.offsets[r] < prm.offsets[r - 1]) return CID_ERR_INVALID_ARGUMENT;
-  }
   prm.ids = token_ids;
   prm.rows = rows;
   prm.confidence = confidence;
@@ -1482,11 +1533,10 @@ extern "C" int cid_display_combine_inbox(void* inbox, int world,
 extern "C" int cid_peer_push_records(const cid_shard_record_t* records, int64_t rows, int rank,
                                      int world, void* const* inboxes, int64_t rows_capacity,
                                      uint32_t epoch, void* stream) {
-  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || !inboxes || !records)
-    return CID_ERR_INVALID_ARGUMENT;
-  if (rows < 1 || rows > rows_capacity) return CID_ERR_INVALID_ARGUMENT;
-  for (int q = 0; q < world; ++q)
-    if (!inboxes[q]) return CID_ERR_INVALID_ARGUMENT;
+  int rc = check_peers(rows, rank, world, inboxes, rows_capacity);
+  if (rc != CID_OK) return rc;
+  if (misaligned({{records, 4}})) return CID_ERR_MISALIGNED;
+  if (any_null({records})) return CID_ERR_INVALID_ARGUMENT;
   PeerSlots slots = {};
   for (int q = 0; q < world; ++q) {
     slots.dst[q] = inbox_records(inboxes[q], world, rows_capacity, epoch & 1u, rank);
@@ -1496,7 +1546,7 @@ extern "C" int cid_peer_push_records(const cid_shard_record_t* records, int64_t 
   const int64_t blocks = (rows + threads - 1) / threads;
   push_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(
       records, slots, world, rows);
-  int rc = launch_result();
+  rc = launch_result();
   if (rc != CID_OK) return rc;
   publish_epoch_kernel<<<1, 32, 0, as_stream(stream)>>>(slots, world, epoch);
   return launch_result();

@@ -551,9 +551,9 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // 2-D bf16 tensor map over a row-major [outer, inner] matrix, box
 // [box_outer, 64] with the 128-byte swizzle.
-bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_outer) {
+int make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int box_outer) {
   auto encode = tensor_map_encoder();
-  if (encode == nullptr) return false;
+  if (encode == nullptr) return record_cuda_error(cudaErrorNotSupported);
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_outer)};
@@ -561,7 +561,9 @@ bool make_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, 
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+             ? CID_OK
+             : CID_ERR_INVALID_ARGUMENT;
 }
 
 struct Plan {
@@ -584,8 +586,32 @@ Plan plan(int64_t rows, int64_t vocab) {
 
 using namespace cid;
 
+namespace {
+
+// Row limit of the fused LM head (the last row tile's index stays in int32).
+constexpr int64_t kMaxLmRows = INT32_MAX - kBM;
+
+// The operands every LM-head call shares: rows x hidden_dim and
+// vocab x hidden_dim bf16, hidden_dim a positive multiple of 8 (16-byte TMA
+// rows) up to INT32_MAX - kBK, 16-byte-aligned operands and workspace.
+int check_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const void* weight,
+                  int64_t vocab, const int64_t* token_ids, const void* workspace,
+                  const uint32_t* status) {
+  int64_t n = 0;
+  if (rows < 0 || rows > kMaxLmRows || hidden_dim <= 0 || hidden_dim % 8 != 0 ||
+      hidden_dim > INT32_MAX - kBK || vocab <= 0 || vocab > INT32_MAX ||
+      !count_ok(rows, hidden_dim, &n) || n > kMaxCount || !count_ok(vocab, hidden_dim, &n) ||
+      n > kMaxCount)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{hidden, 16}, {weight, 16}, {token_ids, 8}, {workspace, 16}, {status, 4}}))
+    return CID_ERR_MISALIGNED;
+  return CID_OK;
+}
+
+}  // namespace
+
 extern "C" size_t cid_lm_head_workspace_bytes(int64_t rows, int64_t vocab) {
-  if (rows <= 0 || vocab <= 0) return 0;
+  if (rows <= 0 || rows > kMaxLmRows || vocab <= 0 || vocab > INT32_MAX) return 0;
   const Plan pl = plan(rows, vocab);
   return static_cast<size_t>(pl.groups) * static_cast<size_t>(rows) * sizeof(cid_shard_record_t);
 }
@@ -598,18 +624,13 @@ int launch_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const v
                    int64_t vocab, int64_t vocab_offset, const int64_t* token_ids, int round_bf16,
                    void* workspace, size_t workspace_bytes, uint32_t* status, void* stream,
                    int64_t (&offsets)[kMaxGroups + 1], int& groups) {
-  if (!hidden || !weight || !token_ids || !workspace) return CID_ERR_INVALID_ARGUMENT;
   // TMA: row strides and base addresses 16-byte aligned
-  if (hidden_dim % 8 != 0 || (reinterpret_cast<uintptr_t>(hidden) & 15u) ||
-      (reinterpret_cast<uintptr_t>(weight) & 15u))
-    return CID_ERR_INVALID_ARGUMENT;
-  if (rows > INT32_MAX - kBM) return CID_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < cid_lm_head_workspace_bytes(rows, vocab)) return CID_ERR_SCRATCH_LIMIT;
   const Plan pl = plan(rows, vocab);
   CUtensorMap map_a, map_b;
-  if (!make_map(&map_a, hidden, hidden_dim, rows, kBM) ||
-      !make_map(&map_b, weight, hidden_dim, vocab, kBN))
-    return CID_ERR_INVALID_ARGUMENT;
+  int rc = make_map(&map_a, hidden, hidden_dim, rows, kBM);
+  if (rc == CID_OK) rc = make_map(&map_b, weight, hidden_dim, vocab, kBN);
+  if (rc != CID_OK) return rc;
   LmParams p = {};
   p.rows = rows;
   p.vocab = vocab;
@@ -631,7 +652,7 @@ int launch_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const v
   const int64_t grid = pl.units < sm_count() ? pl.units : sm_count();
   lm_head_stats_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, as_stream(stream)>>>(
       map_a, map_b, p);
-  const int rc = launch_result();
+  rc = launch_result();
   if (rc != CID_OK) return rc;
   groups = static_cast<int>(pl.groups);
   for (int64_t g = 0; g < pl.groups; ++g) offsets[g] = vocab_offset + g * pl.group_tiles * kBN;
@@ -648,13 +669,17 @@ extern "C" int cid_lm_head_display_statistics(const void* hidden, int64_t rows, 
                                               float* current_confidence, void* workspace,
                                               size_t workspace_bytes, uint32_t* status,
                                               void* stream) {
-  if (rows < 0 || hidden_dim <= 0 || vocab <= 0 || vocab > INT32_MAX) return CID_ERR_INVALID_ARGUMENT;
+  int rc = check_lm_head(hidden, rows, hidden_dim, weight, vocab, token_ids, workspace, status);
+  if (rc != CID_OK) return rc;
+  if (misaligned({{confidence, 4}, {predicted, 8}, {current_confidence, 4}}))
+    return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
-  if (!confidence || !predicted || !current_confidence) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({hidden, weight, token_ids, workspace, confidence, predicted, current_confidence}))
+    return CID_ERR_INVALID_ARGUMENT;
   int64_t offsets[kMaxGroups + 1];
   int groups = 0;
-  int rc = launch_lm_head(hidden, rows, hidden_dim, weight, vocab, 0, token_ids, round_bf16,
-                          workspace, workspace_bytes, status, stream, offsets, groups);
+  rc = launch_lm_head(hidden, rows, hidden_dim, weight, vocab, 0, token_ids, round_bf16,
+                      workspace, workspace_bytes, status, stream, offsets, groups);
   if (rc != CID_OK) return rc;
   // merge the groups of every row (ascending column ranges) into its statistics
   return cid_display_combine_records(static_cast<const cid_shard_record_t*>(workspace), groups,
@@ -668,16 +693,21 @@ extern "C" int cid_lm_head_shard_records(const void* hidden, int64_t rows, int64
                                          const int64_t* token_ids, int round_bf16,
                                          cid_shard_record_t* records, void* workspace,
                                          size_t workspace_bytes, uint32_t* status, void* stream) {
-  if (rows < 0 || hidden_dim <= 0 || vocab_shard <= 0 || vocab_offset < 0 ||
-      total_vocab > INT32_MAX || vocab_offset + vocab_shard > total_vocab)
+  int rc = check_lm_head(hidden, rows, hidden_dim, weight_shard, vocab_shard, token_ids,
+                         workspace, status);
+  if (rc != CID_OK) return rc;
+  if (vocab_offset < 0 || total_vocab > INT32_MAX || total_vocab < vocab_shard ||
+      vocab_offset > total_vocab - vocab_shard)
     return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{records, 4}})) return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
-  if (!records) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({hidden, weight_shard, token_ids, workspace, records}))
+    return CID_ERR_INVALID_ARGUMENT;
   int64_t offsets[kMaxGroups + 1];
   int groups = 0;
-  int rc = launch_lm_head(hidden, rows, hidden_dim, weight_shard, vocab_shard, vocab_offset,
-                          token_ids, round_bf16, workspace, workspace_bytes, status, stream,
-                          offsets, groups);
+  rc = launch_lm_head(hidden, rows, hidden_dim, weight_shard, vocab_shard, vocab_offset,
+                      token_ids, round_bf16, workspace, workspace_bytes, status, stream, offsets,
+                      groups);
   if (rc != CID_OK) return rc;
   // one record per row over the whole shard
   return cid_display_merge_records(static_cast<const cid_shard_record_t*>(workspace), groups,

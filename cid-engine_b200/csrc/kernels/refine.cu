@@ -569,9 +569,14 @@ extern "C" int cid_refine_display(const int64_t* token_ids, const float* confide
   if (!(reveal_fraction >= 0.0 && reveal_fraction <= 1.0)) return CID_ERR_INVALID_ARGUMENT;
   if (!(revision_fraction >= 0.0 && revision_fraction <= 1.0)) return CID_ERR_INVALID_ARGUMENT;
   if (!(revision_margin >= 0.0)) return CID_ERR_INVALID_ARGUMENT;
-  if (batch < 0 || tokens < 0 || batch > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
+  int64_t count = 0;
+  if (!count_ok(batch, tokens, &count) || batch > kMaxRows || count > kMaxCount)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{token_ids, 8}, {confidence, 4}, {predicted, 8}, {current_confidence, 4},
+                  {out, 8}}))
+    return CID_ERR_MISALIGNED;
   if (batch == 0 || tokens == 0) return CID_OK;
-  if (!token_ids || !confidence || !predicted || !current_confidence || !out)
+  if (any_null({token_ids, confidence, predicted, current_confidence, out}))
     return CID_ERR_INVALID_ARGUMENT;
   RefineParams p;
   p.ids = token_ids;
@@ -586,8 +591,9 @@ extern "C" int cid_refine_display(const int64_t* token_ids, const float* confide
   p.revision = revision_fraction;
   p.margin = revision_margin;
   p.out = out;
-  const int64_t smem = tokens * (3 * 8 + 2 * 4);
-  p.use_smem = smem <= kSmemLimit;
+  constexpr int64_t kRowBytes = 3 * 8 + 2 * 4;  // shared bytes per position
+  p.use_smem = tokens <= kSmemLimit / kRowBytes;
+  const int64_t smem = p.use_smem ? tokens * kRowBytes : 0;
   const size_t dyn = p.use_smem ? static_cast<size_t>(smem) : 0;
   // 512 threads per row when rows are long and too few to fill the SMs
   const bool wide = tokens >= 1024 && batch < 2LL * sm_count();

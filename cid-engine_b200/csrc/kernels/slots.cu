@@ -196,6 +196,14 @@ __global__ void live_kernel(LiveParams p) {
   }
 }
 
+// A batch x slots strided view: non-negative strides whose largest element
+// offset stays within kMaxCount.
+bool strided_span_ok(int64_t batch, int64_t slots, int64_t row_stride, int64_t col_stride) {
+  int64_t a = 0, b = 0;
+  return row_stride >= 0 && col_stride >= 0 && count_ok(batch - 1, row_stride, &a) &&
+         count_ok(slots - 1, col_stride, &b) && a <= kMaxCount && b <= kMaxCount - a;
+}
+
 }  // namespace
 }  // namespace cid
 
@@ -207,12 +215,21 @@ extern "C" int cid_prefix_allocation_mask(cid_dtype_t occ_dtype, const void* occ
                                           int64_t logit_row_stride, int64_t logit_col_stride,
                                           int64_t batch, int64_t slots, double threshold,
                                           int64_t max_allocations, uint8_t* out, void* stream) {
+  if (!is_known_dtype(occ_dtype) || !is_float_dtype(logit_dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
   if (!(threshold >= 0.0 && threshold <= 1.0)) return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:50
   if (max_allocations <= 0) return CID_ERR_INVALID_ARGUMENT;                      // ops.cpp:51
-  if (!is_known_dtype(occ_dtype) || !is_float_dtype(logit_dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
-  if (batch < 0 || slots < 0) return CID_ERR_INVALID_ARGUMENT;
+  int64_t count = 0;
+  if (!count_ok(batch, slots, &count) || batch > kMaxRows || count > kMaxCount)
+    return CID_ERR_INVALID_ARGUMENT;
+  if (batch > 0 && slots > 0 &&
+      (!strided_span_ok(batch, slots, occ_row_stride, occ_col_stride) ||
+       !strided_span_ok(batch, slots, logit_row_stride, logit_col_stride)))
+    return CID_ERR_INVALID_ARGUMENT;
+  if (misaligned({{occupancy, static_cast<size_t>(dtype_size(occ_dtype))},
+                  {logits, static_cast<size_t>(dtype_size(logit_dtype))}}))
+    return CID_ERR_MISALIGNED;
   if (batch == 0 || slots == 0) return CID_OK;
-  if (!occupancy || !logits || !out) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({occupancy, logits, out})) return CID_ERR_INVALID_ARGUMENT;
   PrefixParams p{occ_dtype, occupancy, occ_row_stride, occ_col_stride, logit_dtype, logits,
                  logit_row_stride, logit_col_stride, batch, slots,
                  static_cast<float>(threshold), max_allocations, out};
@@ -229,14 +246,30 @@ int launch_rollout(const RolloutParams& p, void* stream) {
                     0, as_stream(stream), p);
 }
 
-int check_rollout(cid_dtype_t occ_dtype, cid_dtype_t dtype, int64_t batch, int64_t slots,
-                  int64_t lifecycles, int64_t revisions, double threshold,
-                  int64_t max_allocations, int64_t retired_index) {
-  if (retired_index < 0 || retired_index >= lifecycles) return CID_ERR_INVALID_ARGUMENT;
+// The arguments of a rollout call (with its live-occupancy output when
+// `with_live`): dtypes, scalars (threshold as the caller passed it), extents,
+// alignment, and (when there is work) non-NULL arrays.
+int check_rollout(const RolloutParams& p, double threshold, bool with_live) {
+  if (!is_known_dtype(p.occ_dtype) || !is_float_dtype(p.dtype) ||
+      (with_live && !is_float_dtype(p.live_dtype)))
+    return CID_ERR_UNSUPPORTED_DTYPE;
+  if (p.retired < 0 || p.retired >= p.F) return CID_ERR_INVALID_ARGUMENT;
   if (!(threshold >= 0.0 && threshold <= 1.0)) return CID_ERR_INVALID_ARGUMENT;
-  if (max_allocations <= 0 || revisions <= 0) return CID_ERR_INVALID_ARGUMENT;
-  if (!is_known_dtype(occ_dtype) || !is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
-  if (batch < 0 || slots < 0) return CID_ERR_INVALID_ARGUMENT;
+  if (p.max_alloc <= 0 || p.Rv <= 0) return CID_ERR_INVALID_ARGUMENT;
+  const int64_t widest = p.F > p.Rv ? p.F : p.Rv;
+  int64_t count = 0;
+  if (!count_ok(p.batch, p.slots, widest, &count) || p.batch > kMaxRows || count > kMaxCount)
+    return CID_ERR_INVALID_ARGUMENT;
+  const size_t es = static_cast<size_t>(dtype_size(p.dtype));
+  if (misaligned({{p.occ, static_cast<size_t>(dtype_size(p.occ_dtype))}, {p.alloc, es},
+                  {p.life, es}, {p.rev, es}, {p.in_life, es}, {p.life_idx, 8}, {p.rev_idx, 8},
+                  {p.in_idx, 8}, {p.live_occ, static_cast<size_t>(dtype_size(p.live_dtype))}}))
+    return CID_ERR_MISALIGNED;
+  if (p.batch == 0 || p.slots == 0) return CID_OK;
+  if (any_null({p.occ, p.alloc, p.life, p.rev, p.in_life, p.next, p.life_idx, p.rev_idx,
+                p.in_idx, p.present, p.live}) ||
+      (with_live && p.live_occ == nullptr))
+    return CID_ERR_INVALID_ARGUMENT;
   return CID_OK;
 }
 
@@ -250,15 +283,13 @@ extern "C" int cid_rollout_slot_transition(
     uint8_t* next_occupancy, int64_t* lifecycle_indices, int64_t* revision_indices,
     int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present, uint8_t* live_slots,
     void* stream) {
-  int rc = check_rollout(occ_dtype, dtype, batch, slots, lifecycles, revisions, threshold,
-                         max_allocations, retired_index);
-  if (rc != CID_OK) return rc;
-  if (batch == 0 || slots == 0) return CID_OK;
   RolloutParams p{occ_dtype, occupancy, dtype, allocation_logits, lifecycle_logits,
                   revision_logits, input_lifecycle, batch, slots, lifecycles, revisions,
                   static_cast<float>(threshold), max_allocations, retired_index,
                   next_occupancy, lifecycle_indices, revision_indices, input_lifecycle_indices,
                   input_lifecycle_present, live_slots, dtype, nullptr};
+  const int rc = check_rollout(p, threshold, false);
+  if (rc != CID_OK || batch == 0 || slots == 0) return rc;
   return launch_rollout(p, stream);
 }
 
@@ -270,17 +301,13 @@ extern "C" int cid_rollout_slot_transition_live(
     uint8_t* next_occupancy, int64_t* lifecycle_indices, int64_t* revision_indices,
     int64_t* input_lifecycle_indices, uint8_t* input_lifecycle_present, uint8_t* live_slots,
     cid_dtype_t live_dtype, void* live_occupancy, void* stream) {
-  int rc = check_rollout(occ_dtype, dtype, batch, slots, lifecycles, revisions, threshold,
-                         max_allocations, retired_index);
-  if (rc != CID_OK) return rc;
-  if (!is_float_dtype(live_dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
-  if (batch == 0 || slots == 0) return CID_OK;
-  if (!live_occupancy) return CID_ERR_INVALID_ARGUMENT;
   RolloutParams p{occ_dtype, occupancy, dtype, allocation_logits, lifecycle_logits,
                   revision_logits, input_lifecycle, batch, slots, lifecycles, revisions,
                   static_cast<float>(threshold), max_allocations, retired_index,
                   next_occupancy, lifecycle_indices, revision_indices, input_lifecycle_indices,
                   input_lifecycle_present, live_slots, live_dtype, live_occupancy};
+  const int rc = check_rollout(p, threshold, true);
+  if (rc != CID_OK || batch == 0 || slots == 0) return rc;
   return launch_rollout(p, stream);
 }
 
@@ -290,9 +317,14 @@ extern "C" int cid_live_slot_occupancy(cid_dtype_t dtype, const void* occupancy,
   if (!is_float_dtype(dtype)) return CID_ERR_UNSUPPORTED_DTYPE;
   if (lifecycle && (retired_index < 0 || retired_index >= features))
     return CID_ERR_INVALID_ARGUMENT;  // ops.cpp:31-33
-  if (rows < 0) return CID_ERR_INVALID_ARGUMENT;
+  int64_t count = 0;
+  if (rows < 0 || rows > kMaxRows ||
+      (lifecycle && (!count_ok(rows, features, &count) || count > kMaxCount)))
+    return CID_ERR_INVALID_ARGUMENT;
+  const size_t es = static_cast<size_t>(dtype_size(dtype));
+  if (misaligned({{occupancy, es}, {lifecycle, es}, {out, es}})) return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
-  if (!occupancy || !out) return CID_ERR_INVALID_ARGUMENT;
+  if (any_null({occupancy, out})) return CID_ERR_INVALID_ARGUMENT;
   LiveParams p{dtype, occupancy, lifecycle, rows, features, retired_index, out};
   const int threads = 256;
   int64_t blocks = (rows + threads - 1) / threads;

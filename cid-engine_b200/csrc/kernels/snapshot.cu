@@ -95,10 +95,25 @@ extern "C" int cid_materialize_cell_snapshot(
   if (!is_float_dtype(sem_dtype) || !is_float_dtype(role_dtype) || !is_float_dtype(unc_dtype) ||
       !is_float_dtype(noise_dtype) || !is_float_dtype(life_dtype))
     return CID_ERR_UNSUPPORTED_DTYPE;
-  if (rows < 0 || hidden < 0 || nroles < 0 || nindices < 0 || lifecycles <= 0)
+  // rows x hidden, roles and lifecycles inputs; rows x (4 + roles + indices) output
+  int64_t n = 0;
+  if (rows < 0 || rows > kMaxRows || lifecycles <= 0 || nroles < 0 || nroles > kMaxCount ||
+      nindices < 0 || nindices > kMaxCount || !count_ok(rows, hidden, &n) || n > kMaxCount ||
+      !count_ok(rows, nroles, &n) || n > kMaxCount || !count_ok(rows, lifecycles, &n) ||
+      n > kMaxCount || !count_ok(rows, 4 + nroles + nindices, &n) || n > kMaxCount)
     return CID_ERR_INVALID_ARGUMENT;
+  auto es = [](cid_dtype_t dt) { return static_cast<size_t>(dtype_size(dt)); };
+  if (misaligned({{semantic, es(sem_dtype)}, {roles, es(role_dtype)},
+                  {uncertainty, es(unc_dtype)}, {noise_delta, es(noise_dtype)},
+                  {lifecycle, es(life_dtype)}, {indices, 8}, {out, 4}, {status, 4}}))
+    return CID_ERR_MISALIGNED;
   if (rows == 0) return CID_OK;
-  if (!out || !selected || (nindices > 0 && !indices)) return CID_ERR_INVALID_ARGUMENT;
+  // the semantic values are read only at the indices, and only when the
+  // width is non-zero (every index is out of range otherwise)
+  if (any_null({out, selected, uncertainty, noise_delta, lifecycle}) ||
+      (nroles > 0 && roles == nullptr) || (nindices > 0 && indices == nullptr) ||
+      (nindices > 0 && hidden > 0 && semantic == nullptr))
+    return CID_ERR_INVALID_ARGUMENT;
   SnapshotParams p{sem_dtype, semantic, hidden, role_dtype, roles, nroles, unc_dtype,
                    uncertainty, noise_dtype, noise_delta, life_dtype, lifecycle, lifecycles,
                    selected, indices, nindices, rows, out, status};

@@ -11,6 +11,18 @@
  * v1.1.0); the reference interface is cited beside it.  Argument meaning and
  * output semantics are those of the reference CPU backend.
  *
+ * Host-side validation.  Before its first CUDA call every entry point checks,
+ * in this order: its dtype codes (CID_ERR_UNSUPPORTED_DTYPE); its scalar
+ * arguments and extents (CID_ERR_INVALID_ARGUMENT) — negative extents, row
+ * or batch counts above 2^31 - 1, arrays of more than 2^58 elements, element
+ * counts that overflow int64; the alignment of every non-NULL pointer to its
+ * element size, or to 16 bytes where an entry point says so
+ * (CID_ERR_MISALIGNED); then it returns CID_OK when there is no work, and
+ * otherwise rejects a NULL pointer for any array of non-zero extent that it
+ * reads or writes (CID_ERR_INVALID_ARGUMENT; `status` may always be NULL).
+ * Host arrays (shard offsets, inbox lists, IPC handles) are read only within
+ * their documented extents, after the extent itself has been checked.
+ *
  * Device-side status.  Conditions that the reference CPU backend turns into
  * exceptions but that a device kernel cannot raise without a host sync (an
  * out-of-range token id, a snapshot index outside the semantic width) are
@@ -46,7 +58,12 @@ typedef enum cid_dtype {
   CID_DTYPE_I32 = 6,
   CID_DTYPE_U8 = 7,
   CID_DTYPE_I8 = 8,
-  CID_DTYPE_I16 = 9
+  CID_DTYPE_I16 = 9,
+  /* Not dtypes: these two make every 32-bit int a value of the type, so an
+   * unknown code from a caller is a defined value that the entry points
+   * reject with CID_ERR_UNSUPPORTED_DTYPE. */
+  CID_DTYPE_RANGE_MIN_ = -0x7fffffff - 1,
+  CID_DTYPE_RANGE_MAX_ = 0x7fffffff
 } cid_dtype_t;
 
 typedef enum cid_result {
@@ -132,8 +149,9 @@ CID_API int cid_display_shard_records(cid_dtype_t dtype, const void* logits,
                               cid_shard_record_t* records, uint32_t* status,
                               void* stream);
 
-/* records: world x rows (rank-major).  shard_offsets: world+1 ascending
- * column offsets on the HOST (shard r owns [offsets[r], offsets[r+1])). */
+/* records: world x rows (rank-major), world <= 64.  shard_offsets: world+1
+ * ascending column offsets within [0, 2^31 - 1] on the HOST (shard r owns
+ * [offsets[r], offsets[r+1])). */
 /* Merges records [world][rows] of ascending column ranges shard_offsets_host
  * (world + 1 host values) into one record per row of their union, as
  * cid_display_shard_records would produce for the concatenated range (no
@@ -347,7 +365,8 @@ CID_API size_t cid_lm_head_workspace_bytes(int64_t rows, int64_t vocab);
 /* display_token_statistics(token_ids, logits) of logits = hidden @ weight^T
  * without writing the logits: hidden rows x hidden_dim bf16 and weight
  * vocab x hidden_dim bf16, both row-major with hidden_dim % 8 == 0 and
- * 16-byte aligned bases; f32 accumulation on the tcgen05 tensor cores,
+ * 16-byte aligned bases (workspace too), rows <= 2^31 - 129; f32
+ * accumulation on the tcgen05 tensor cores,
  * each logit rounded to bf16 first when round_bf16 != 0 (the statistics of
  * a bf16 LM head's stored output).  token_ids rows int64; outputs as
  * cid_display_token_statistics.  workspace: device memory of at least
@@ -378,7 +397,8 @@ CID_API int cid_lm_head_shard_records(const void* hidden, int64_t rows, int64_t 
 /* ---------------------------------------------------------------------- */
 
 /* Bytes of one rank's inbox for `world` ranks (<= 8) and up to rows_capacity
- * rows: records [2][world][rows_capacity] then a 256-byte tail (flag words). */
+ * (<= 2^31 - 1) rows: records [2][world][rows_capacity] then a 256-byte tail
+ * (flag words); 0 for arguments outside those ranges. */
 CID_API size_t cid_peer_inbox_bytes(int world, int64_t rows_capacity);
 /* cudaMalloc'd, zeroed inbox on the current device (set-up, not per step). */
 CID_API int cid_peer_inbox_alloc(size_t bytes, void** inbox);

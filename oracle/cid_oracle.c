@@ -858,8 +858,11 @@ int cid_oracle_display_corrupt(const int64_t* ids, int t_dtype,
   if (!(replacement_fraction >= 0.0 && replacement_fraction <= 1.0))
     return -1; /* :320-322 */
   const int replace = replacement_fraction > 0.0;
-  if (replace && (vocab < 3 || !replacement_random || !replacement_offsets))
-    return -1; /* :343-360 */
+  /* :343-360; an empty replacement tensor has a null data pointer, so the
+     presence check on empty inputs is left to the caller */
+  if (replace && (vocab < 3 || (batch * tokens > 0 &&
+                                (!replacement_random || !replacement_offsets))))
+    return -1;
   const float repl_thr = (float)replacement_fraction;
   for (int64_t b = 0; b < batch; ++b) {
     const float t = (float)load(t_dtype, timesteps, b); /* :325 */

@@ -294,6 +294,9 @@ def display_corrupt_from_random(
     rr = None if replacement_random is None else _host(replacement_random)
     ro = None if replacement_offsets is None else _host(replacement_offsets)
     b, t = ids.shape
+    if replacement_fraction > 0.0 and (rr is None or ro is None):
+        raise RuntimeError("replacement random tensors are required when "
+                           "replacement_fraction > 0")  # csrc/ops.cpp:347-349
     corrupted = torch.empty_like(ids)
     labels = torch.empty_like(ids)
     masked = torch.empty((b, t), dtype=torch.bool)

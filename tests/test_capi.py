@@ -164,7 +164,7 @@ def test_host_validation_of_the_other_entry_points(lib: ctypes.CDLL) -> None:
             p(0x4000), p(0x5000), p(0x6000), p(0x7000), ctypes.c_size_t(ws_bytes), null, null)
 
     assert lm_head(12, 0x1000, ws_need) == CID_ERR_INVALID_ARGUMENT
-    assert lm_head(64, 0x1008, ws_need) == CID_ERR_INVALID_ARGUMENT
+    assert lm_head(64, 0x1008, ws_need) == 4  # CID_ERR_MISALIGNED
     assert lm_head(64, 0x1000, ws_need - 1) == 6  # CID_ERR_SCRATCH_LIMIT
 
 

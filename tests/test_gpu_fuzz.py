@@ -220,3 +220,97 @@ def test_fuzz_linear_assignment(batch, columns, seed, integer_costs) -> None:
     counts = torch.randint(0, rows + 1, (batch,), generator=g)
     got = torch.ops.cid_engine.batched_linear_assignment(costs.cuda(), counts.cuda())
     assert torch.equal(got.cpu(), oracle.batched_linear_assignment(costs, counts))
+
+
+@SETTINGS
+@given(batch=st.integers(0, 5), slots=st.integers(0, 48), features=st.integers(1, 8),
+       seed=st.integers(0, 2**31 - 1), dtype=DTYPES, with_lifecycle=st.booleans(),
+       special=st.booleans())
+def test_fuzz_live_slot_occupancy(batch, slots, features, seed, dtype, with_lifecycle,
+                                  special) -> None:
+    """tests/test_fuzz.py:50-81 of the reference: occupancy and lifecycle
+    drawn as N(0, 1.5^2) so both clamps of csrc/ops.cpp:12-39 are hit, the
+    retired index from the seed; ``special`` adds NaN and infinities."""
+    g = torch.Generator().manual_seed(seed)
+    occ = (torch.randn(batch, slots, 1, generator=g) * 1.5).to(dtype)
+    lc = None
+    r = 0
+    if with_lifecycle:
+        lc = (torch.randn(batch, slots, features, generator=g) * 1.5).to(dtype)
+        r = seed % features
+        if special and lc.numel():
+            lc.view(-1)[::5] = float("nan")
+            lc.view(-1)[1::7] = float("inf")
+            occ.view(-1)[::3] = float("-inf")
+    got = torch.ops.cid_engine.live_slot_occupancy(occ.cuda(), None if lc is None else lc.cuda(),
+                                                   r)
+    exp = oracle.live_slot_occupancy(occ, lc, r)
+    assert got.dtype == dtype and got.shape == occ.shape
+    torch.testing.assert_close(got.cpu(), exp, rtol=0, atol=0, equal_nan=True)
+
+
+@SETTINGS
+@given(batch=st.integers(0, 4), slots=st.integers(0, 40), hidden=st.integers(1, 300),
+       roles=st.integers(0, 8), lifecycles=st.integers(1, 6), picks=st.integers(0, 24),
+       seed=st.integers(0, 2**31 - 1), dtypes=st.lists(DTYPES, min_size=5, max_size=5),
+       ties=st.booleans(), host_indices=st.booleans())
+def test_fuzz_materialize_cell_snapshot(batch, slots, hidden, roles, lifecycles, picks, seed,
+                                        dtypes, ties, host_indices) -> None:
+    """csrc/ops.cpp:556-615 of the reference with every input in its own
+    dtype, repeated semantic indices, role counts down to zero, and (with
+    ``ties``) integer-valued lifecycle logits with NaN so the argmax meets
+    ties and NaN; indices resident on the host or on the device."""
+    g = torch.Generator().manual_seed(seed)
+    sem = torch.randn(batch, slots, hidden, generator=g).to(dtypes[0])
+    rl = (torch.randn(batch, slots, roles, generator=g) * 8).to(dtypes[1])
+    unc = torch.rand(batch, slots, 1, generator=g).to(dtypes[2])
+    noise = torch.randn(batch, slots, 1, generator=g).to(dtypes[3])
+    life = torch.randn(batch, slots, lifecycles, generator=g)
+    if ties:
+        life = (life * 1.5).round()
+        if life.numel():
+            life.view(-1)[::9] = float("nan")
+    life = life.to(dtypes[4])
+    sel = torch.rand(batch, slots, generator=g) > 0.5
+    idx = torch.randint(0, hidden, (picks,), generator=g)
+    got = torch.ops.cid_engine.materialize_cell_snapshot(
+        sem.cuda(), rl.cuda(), unc.cuda(), noise.cuda(), life.cuda(), sel.cuda(),
+        idx if host_indices else idx.cuda())
+    exp = oracle.materialize_cell_snapshot(sem, rl, unc, noise, life, sel, idx)
+    assert got.shape == (batch, slots, 4 + roles + picks)
+    compare.assert_matches("materialize_cell_snapshot", got, exp, "fuzz snapshot")
+
+
+@SETTINGS
+@given(batch=st.integers(0, 6), tokens=st.integers(0, 3000),
+       vocab=st.sampled_from([3, 4, 7, 50, 32000, 50257, (1 << 32) + 5]),
+       seed=st.integers(0, 2**31 - 1), fraction=UNIT, density=UNIT,
+       eos=st.sampled_from([None, 0, 1, 2]), mask_at_end=st.booleans(),
+       el_dtype=st.sampled_from([torch.bool, torch.uint8, torch.int64, torch.float32]),
+       r_dtype=DTYPES, t_dtype=DTYPES)
+def test_fuzz_display_corruption(batch, tokens, vocab, seed, fraction, density, eos,
+                                 mask_at_end, el_dtype, r_dtype, t_dtype) -> None:
+    """csrc/ops.cpp:292-391 of the reference (the CUDA differential test of
+    tests/test_cuda.py:155-195 over random shapes): timesteps at 0 and 1
+    included, eligibility masks of every density in several dtypes, random
+    dtypes for the uniform draws, offsets that wrap the vocabulary, EOS and
+    mask ids that collide with the replacement candidates."""
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, min(vocab, 1 << 40), (batch, tokens), generator=g)
+    ts = torch.rand(batch, generator=g)
+    if batch:
+        ts[torch.rand(batch, generator=g) < 0.25] = 0.0
+        ts[torch.rand(batch, generator=g) < 0.15] = 1.0
+    ts = ts.to(t_dtype)
+    el = (torch.rand(batch, tokens, generator=g) < density).to(el_dtype)
+    cr = torch.rand(batch, tokens, generator=g).to(r_dtype)
+    rr = torch.rand(batch, tokens, generator=g).to(r_dtype)
+    ro = torch.randint(-3 * min(vocab, 1 << 40), 3 * min(vocab, 1 << 40), (batch, tokens),
+                       generator=g)
+    mask_id = vocab - 1 if mask_at_end else 0
+    got = torch.ops.cid_engine.display_corrupt_from_random(
+        ids.cuda(), ts.cuda(), el.cuda(), cr.cuda(), rr.cuda(), ro.cuda(), mask_id, eos, vocab,
+        fraction)
+    exp = oracle.display_corrupt_from_random(ids, ts, el, cr, rr, ro, mask_id, eos, vocab,
+                                             fraction)
+    compare.assert_matches("display_corrupt_from_random", got, exp, "fuzz display corruption")
