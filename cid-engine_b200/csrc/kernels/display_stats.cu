@@ -231,6 +231,11 @@ struct StatsParams {
   cid_shard_record_t* records;
   int64_t vocab_offset;
   int64_t total_vocab;
+  int records_v4;  // records (and peer_records) 16-byte aligned: one vector store each
+  // peer exchange: this rank's slot in the other ranks' inboxes, where each
+  // record is stored too, over NVLink, while the kernel streams its logits
+  int peers;
+  cid_shard_record_t* peer_records[kMaxPeers - 1];
 };
 
 enum class Mode { kFinal, kRecord };
@@ -562,6 +567,22 @@ __device__ __forceinline__ void load_current(const StatsParams& p, int64_t row, 
   x = (id >= 0 && id < V) ? VecTraits<T>::scalar(rowp, id) : 0.0f;
 }
 
+// The record of one row, into this launch's records and, in a peer exchange,
+// into this rank's slot of every other rank's inbox (remote stores that
+// overlap the streaming of later rows; the publish kernel that follows the
+// launch orders them before the epoch flag).
+__device__ __forceinline__ void store_record(const StatsParams& p, int64_t row,
+                                             const cid_shard_record_t& rec) {
+  if (p.records_v4) {
+    const uint4 v = make_uint4(__float_as_uint(rec.max_logit), __float_as_uint(rec.sum_exp),
+                               static_cast<uint32_t>(rec.index), __float_as_uint(rec.current));
+    *reinterpret_cast<uint4*>(p.records + row) = v;
+    for (int q = 0; q < p.peers; ++q) *reinterpret_cast<uint4*>(p.peer_records[q] + row) = v;
+  } else {
+    p.records[row] = rec;
+  }
+}
+
 // Outputs of one row whose maximum is not finite or whose sum is NaN:
 // predicted = first NaN, else first maximum; statistics NaN.
 template <typename T, Mode kMode>
@@ -580,7 +601,7 @@ __device__ void write_special(const StatsParams& p, int64_t row, float cur_x, fl
     rec.index = static_cast<int32_t>(p.vocab_offset + local) |
                 (first_nan != kNone ? static_cast<int32_t>(0x80000000u) : 0);
     rec.current = cur_x;
-    p.records[row] = rec;
+    store_record(p, row, rec);
   }
 }
 
@@ -608,7 +629,7 @@ __device__ void write_normal(const StatsParams& p, int64_t row, int64_t V, int64
     rec.sum_exp = __fdiv_rn(fin.s, top);  // sum of exp(x - max) over the shard
     rec.index = static_cast<int32_t>(p.vocab_offset + col);
     rec.current = cur_x;
-    p.records[row] = rec;
+    store_record(p, row, rec);
   }
 }
 
@@ -1258,6 +1279,7 @@ extern "C" int cid_display_shard_records(cid_dtype_t dtype, const void* logits,
   if (rows == 0) return CID_OK;
   if (any_null({logits, token_ids, records})) return CID_ERR_INVALID_ARGUMENT;
   StatsParams prm = {};
+  prm.records_v4 = reinterpret_cast<uintptr_t>(records) % 16 == 0;
   prm.logits = logits;
   prm.row_stride = row_stride;
   prm.ids = token_ids;
@@ -1384,7 +1406,8 @@ uint32_t* inbox_flags(void* inbox, int world, int64_t capacity) {
 
 // The rank arguments of a peer exchange call: 1 <= world <= kMaxPeers,
 // 0 <= rank < world, 1 <= rows <= rows_capacity <= kMaxRows, and `world`
-// non-NULL inbox pointers (4-byte aligned: they hold the flag words).
+// non-NULL inbox pointers, 16-byte aligned (records are stored as one
+// 16-byte vector each; cudaMalloc and IPC mappings are 256-byte aligned).
 int check_peers(int64_t rows, int rank, int world, void* const* inboxes, int64_t rows_capacity) {
   if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || inboxes == nullptr)
     return CID_ERR_INVALID_ARGUMENT;
@@ -1393,7 +1416,7 @@ int check_peers(int64_t rows, int rank, int world, void* const* inboxes, int64_t
   if (misaligned({{inboxes, alignof(void*)}})) return CID_ERR_MISALIGNED;
   for (int q = 0; q < world; ++q) {
     if (inboxes[q] == nullptr) return CID_ERR_INVALID_ARGUMENT;
-    if (misaligned({{inboxes[q], 4}})) return CID_ERR_MISALIGNED;
+    if (misaligned({{inboxes[q], 16}})) return CID_ERR_MISALIGNED;
   }
   return CID_OK;
 }
@@ -1472,25 +1495,20 @@ extern "C" int cid_display_shard_records_to_peers(
   prm.tokens = 1;
   prm.vocab_offset = vocab_offset;
   prm.total_vocab = total_vocab;
-  cid_shard_record_t* own = inbox_records(inboxes[rank], world, rows_capacity, epoch & 1u, rank);
-  prm.records = own;
+  // the statistics kernel stores each record into this rank's slot of every
+  // inbox, its own and (over NVLink) the other ranks', as it finishes the row
+  prm.records = inbox_records(inboxes[rank], world, rows_capacity, epoch & 1u, rank);
+  prm.records_v4 = 1;  // inbox slots are 16-byte aligned (check_peers)
   PeerSlots slots = {};
-  int others = 0;
   for (int q = 0; q < world; ++q) {
     slots.flags[q] = inbox_flags(inboxes[q], world, rows_capacity) + rank;
     if (q != rank)
-      slots.dst[others++] = inbox_records(inboxes[q], world, rows_capacity, epoch & 1u, rank);
+      prm.peer_records[prm.peers++] =
+          inbox_records(inboxes[q], world, rows_capacity, epoch & 1u, rank);
   }
   rc = dispatch_stats<false, Mode::kRecord>(dtype, prm, as_stream(stream));
   if (rc != CID_OK) return rc;
-  if (others > 0) {
-    const int threads = 256;
-    const int64_t blocks = (rows + threads - 1) / threads;
-    push_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(
-        own, slots, others, rows);
-    rc = launch_result();
-    if (rc != CID_OK) return rc;
-  }
+  // a plain launch: it starts once every record store above has completed
   publish_epoch_kernel<<<1, 32, 0, as_stream(stream)>>>(slots, world, epoch);
   return launch_result();
 }
@@ -1508,7 +1526,7 @@ extern "C" int cid_display_combine_inbox(void* inbox, int world,
   if (rows < 1 || rows > rows_capacity || rows_capacity > kMaxRows ||
       !(wait_seconds > 0.0 && wait_seconds <= 60.0))
     return CID_ERR_INVALID_ARGUMENT;
-  if (misaligned({{inbox, 4}}) ||
+  if (misaligned({{inbox, 16}}) ||
       stats_outputs_misaligned(token_ids, confidence, predicted, current_confidence, status))
     return CID_ERR_MISALIGNED;
   if (any_null({inbox, token_ids, confidence, predicted, current_confidence}))

@@ -409,13 +409,14 @@ CID_API int cid_peer_inbox_export(void* inbox, unsigned char handle[64]);
 CID_API int cid_peer_inbox_import(const unsigned char handle[64], void** peer_inbox);
 CID_API int cid_peer_inbox_release(void* peer_inbox);
 
-/* The shard records of cid_display_shard_records written into this rank's
- * slot (of the epoch's parity) of its own inbox, copied into the same slot of
- * every other rank's inbox over peer memory (inboxes: `world` device pointers
- * as this process maps them, inboxes[rank] its own), then `epoch` published in
- * this rank's flag word of every inbox (system fence, then release).
- * 1 <= rows <= rows_capacity; `epoch` increases by one per step on every
- * rank. */
+/* The shard records of cid_display_shard_records, each stored by the
+ * statistics kernel as it finishes the row into this rank's slot (of the
+ * epoch's parity) of every inbox: its own and, over peer memory, the other
+ * ranks' (inboxes: `world` 16-byte-aligned device pointers as this process
+ * maps them, inboxes[rank] its own); then `epoch` published in this rank's
+ * flag word of every inbox (system fence, then release) by a kernel that
+ * starts after the statistics kernel has completed.  1 <= rows <=
+ * rows_capacity; `epoch` increases by one per step on every rank. */
 CID_API int cid_display_shard_records_to_peers(cid_dtype_t dtype, const void* logits,
                         int64_t row_stride, const int64_t* token_ids, int64_t rows,
                         int64_t shard_vocab, int64_t vocab_offset, int64_t total_vocab,

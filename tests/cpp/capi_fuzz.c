@@ -233,7 +233,8 @@ static int64_t* offsets_of(input_t* in, int world, int max_world, int* bad) {
   return o;
 }
 
-/* An inbox list of `world` pointers (exact size when in range), or NULL. */
+/* An inbox list of `world` pointers (exact size when in range; each must be
+ * non-NULL and 16-byte aligned), or NULL. */
 static void** inboxes_of(input_t* in, int world, int* bad) {
   if (take(in) % 10 == 0) {
     *bad = 1;
@@ -245,7 +246,7 @@ static void** inboxes_of(input_t* in, int world, int* bad) {
   int b = 0;
   for (int q = 0; q < n; ++q) {
     list[q] = take(in) % 6 == 0 ? ptr_of(in, 20 + q) : g_arena + 64 * (20 + q);
-    b |= list[q] == NULL || mis(list[q], 4);
+    b |= list[q] == NULL || mis(list[q], 16);
   }
   *bad = b;
   return list;
@@ -736,7 +737,7 @@ static void fuzz_combine_inbox(input_t* in) {
   float* cur = ptr_of(in, 4);
   uint32_t* st = ptr_of(in, 5);
   const int bad = offsets_bad || rows < 1 || rows > cap || cap > MAX_ROWS ||
-                  !(wait > 0.0 && wait <= 60.0) || mis(inbox, 4) ||
+                  !(wait > 0.0 && wait <= 60.0) || mis(inbox, 16) ||
                   outputs_mis(ids, conf, pred, cur, st) || !inbox || !ids || !conf || !pred ||
                   !cur;
   expect(cid_display_combine_inbox(inbox, world, offs, ids, rows, cap, take(in), wait, conf, pred,

@@ -178,3 +178,67 @@ def test_one_rank_exchange_from_lm_head_records() -> None:
         torch.testing.assert_close(u, e_u, rtol=1e-5, atol=1e-30)
     finally:
         ex.close()
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_emulated_ranks_store_records_into_every_inbox(world: int) -> None:
+    """``world`` ranks emulated on one GPU: one inbox each, every rank's
+    record launch (``cid_display_shard_records_to_peers``) stores each record
+    into every inbox as it finishes the row, then publishes; every rank's
+    combine must equal the records + combine path bit for bit, over three
+    steps (both epoch parities).  All launches go to one stream in rank
+    order, so every flag is published before any combine reads it (no kernel
+    waits on another that runs at the same time)."""
+    import cid_engine
+    from cid_engine import parallel
+
+    lib = parallel._capi()
+    dev = torch.device("cuda", 0)
+    B, L, V = 2, 150, 20011
+    rows = B * L
+    offs = parallel.shard_offsets(V, world)
+    stream = torch.cuda.current_stream().cuda_stream
+    status = cid_engine._C.status_word_ptr(0)
+    cid_engine.device_status(0, reset=True)
+    nbytes = lib.cid_peer_inbox_bytes(world, rows)
+    inboxes = []
+    try:
+        for _ in range(world):
+            p = ctypes.c_void_p()
+            assert lib.cid_peer_inbox_alloc(nbytes, ctypes.byref(p)) == 0
+            inboxes.append(p.value)
+        table = (ctypes.c_void_p * world)(*inboxes)
+        c_offs = (ctypes.c_int64 * (world + 1))(*offs)
+        for epoch in (1, 2, 3):
+            g = torch.Generator(device=dev).manual_seed(40 + epoch)
+            logits = (torch.randn(B, L, V, generator=g, device=dev) * 3).to(torch.bfloat16)
+            logits[0, 7, [offs[1] - 1, offs[1]]] = 40.0  # tie across a shard edge: the lower
+            logits[1, 3, offs[-2] + 5] = float("nan")
+            ids = torch.randint(V, (B, L), generator=g, device=dev)
+            shards = [logits[..., offs[r]:offs[r + 1]].contiguous() for r in range(world)]
+            for r in range(world):
+                rc = lib.cid_display_shard_records_to_peers(
+                    3, shards[r].data_ptr(), offs[r + 1] - offs[r], ids.data_ptr(), rows,
+                    offs[r + 1] - offs[r], offs[r], V, r, world, table, rows, epoch, status,
+                    stream)
+                assert rc == 0
+            rec = torch.stack([cid_engine.display_shard_records(ids, shards[r], vocab_offset=offs[r],
+                                                               total_vocab=V)
+                               for r in range(world)])
+            exp = cid_engine.display_combine_records(rec, ids, offs)
+            for r in range(world):
+                got = [torch.empty(B, L, device=dev), torch.empty(B, L, dtype=torch.int64, device=dev),
+                       torch.empty(B, L, device=dev)]
+                rc = lib.cid_display_combine_inbox(
+                    inboxes[r], world, c_offs, ids.data_ptr(), rows, rows, epoch, 1.0,
+                    got[0].data_ptr(), got[1].data_ptr(), got[2].data_ptr(), status, stream)
+                assert rc == 0
+                for a, e in zip(got, exp):
+                    _same(a, e)
+            assert int(exp[1][0, 7]) == offs[1] - 1 and int(exp[1][1, 3]) == offs[-2] + 5
+        torch.cuda.synchronize()
+        assert cid_engine.device_status(0) == 0
+    finally:
+        torch.cuda.synchronize()
+        for p in inboxes:
+            lib.cid_peer_inbox_free(p)
