@@ -4,7 +4,19 @@
 // [rows, vocab] logits to memory.
 //
 // The reference has no LM head (its statistics operator takes materialised
-// logits); this is the producer side of the display path on B200:
+// logits); this is the producer side of the display path on B200.  Two
+// kernels share the work-unit, record and bounded-wait scheme below:
+//
+// * wide tiles (bf16-rounded logits, launches of at least kWideMinRows
+//   rows): one persistent CTA per SM computes 256 rows x 256 columns, two
+//   M=128 MMAs per K step sharing the weight slice (a third less operand
+//   traffic from L2 into shared memory per FLOP than 128 x 256); the tile
+//   fills all of TMEM, so eight epilogue warps drain it into registers as
+//   bf16 pairs (128 registers a thread, after a setmaxnreg split that moves
+//   registers from the TMA/MMA warpgroup to the two epilogue warpgroups),
+//   release it at once and fold the 256 columns while the next tile
+//   accumulates;
+// * 128-row tiles (every other launch), described next.
 //
 // * one persistent CTA per SM, warp-specialised: warp 0 issues TMA loads of
 //   128 x 64 hidden tiles and 256 x 64 weight tiles (128-byte swizzle) into a
@@ -50,6 +62,28 @@ constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 512: all of TMEM
 // x 4096; 64 and 128 were slower.
 constexpr int kRowGroup = 32;
 constexpr int kMaxGroups = 64;                  // record combine limit
+// Wide tiles: 256 rows, 3 stages of 64 KiB (32 KiB hidden + 32 KiB weight).
+// Raster groups of 16 row blocks (4096 rows, the hidden set of kRowGroup
+// 128-row blocks): measured at 32768 x 128256 x 4096, DRAM reads 18.7 GB
+// with 16, 24.8 GB with 8, 34.6 GB with 4.
+constexpr int kWRows = 256;
+constexpr int kWStages = 3;
+constexpr int kWRowGroup = 16;
+constexpr uint32_t kWStageA = kWRows * kBK * 2;  // 32 KiB
+constexpr uint32_t kWStageB = kBN * kBK * 2;     // 32 KiB
+constexpr uint32_t kWStageBytes = kWStageA + kWStageB;
+constexpr size_t kWSmemBytes = kWStages * size_t{kWStageBytes} + 1024 + 256;
+// Warpgroup 0: warp 0 TMA, warp 1 MMA, warps 2-3 idle; warpgroups 1-2: the
+// epilogue.  The register file is split per SM sub-partition (16384 each),
+// and warp w runs on sub-partition w % 4: at launch 3 warps x 168 registers
+// fit one; after the split each holds one control warp at 56 and two
+// epilogue warps at 224 (32 x (56 + 2 x 224) = 16128).
+constexpr int kWThreads = 384;
+constexpr int kWLaunchRegs = 168;
+constexpr int kWCtrlRegs = 56;
+constexpr int kWEpiRegs = 224;
+static_assert(128 * kWCtrlRegs + 256 * kWEpiRegs <= kWThreads * kWLaunchRegs,
+              "setmaxnreg.inc draws only on the registers the CTA was launched with");
 constexpr int kThreads = 192;                   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr uint32_t kStageA = kBM * kBK * 2;     // 16 KiB
 constexpr uint32_t kStageB = kBN * kBK * 2;     // 32 KiB
@@ -74,8 +108,9 @@ struct LmParams {
   int64_t tiles;        // ceil(vocab / kBN)
   int64_t group_tiles;  // vocabulary tiles per work unit
   int64_t groups;       // ceil(tiles / group_tiles)
-  int64_t row_blocks;   // ceil(rows / kBM)
+  int64_t row_blocks;   // ceil(rows / rows per tile)
   int64_t units;        // row_blocks * groups
+  int64_t row_group;    // row blocks per raster group
   const int64_t* ids;
   cid_shard_record_t* records;  // [groups][rows]
   uint32_t* status;
@@ -224,10 +259,10 @@ __device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
 
 __device__ __forceinline__ void unit_coords(const LmParams& p, int64_t u, int64_t& rb,
                                             int64_t& vg) {
-  const int64_t per_group = int64_t{kRowGroup} * p.groups;
+  const int64_t per_group = p.row_group * p.groups;
   const int64_t gi = u / per_group;
-  const int64_t first = gi * kRowGroup;
-  const int64_t rows_in = p.row_blocks - first < kRowGroup ? p.row_blocks - first : kRowGroup;
+  const int64_t first = gi * p.row_group;
+  const int64_t rows_in = p.row_blocks - first < p.row_group ? p.row_blocks - first : p.row_group;
   const int64_t local = u - gi * per_group;
   rb = first + local % rows_in;
   vg = local / rows_in;
@@ -246,26 +281,11 @@ struct RowState {
   float cur;          // logit at the row's token id (when in the unit)
 };
 
-// Folds 32 consecutive columns (weight columns c0..c0+31, raw f32 bits from
-// TMEM) into the state: logits rounded to bf16 in pairs (one cvt per two),
-// exponent arguments and sums in packed f32 pairs.
-__device__ __forceinline__ void fold32(RowState& st, const uint32_t (&r)[32], int64_t c0,
-                                       int64_t vocab, int64_t local_id, int round_bf16) {
-  float x[32];
-  if (round_bf16) {
-#pragma unroll
-    for (int j = 0; j < 32; j += 2) {
-      uint32_t pk;  // upper half: column j + 1, lower half: column j
-      asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
-          : "=r"(pk)
-          : "f"(__uint_as_float(r[j + 1])), "f"(__uint_as_float(r[j])));
-      x[j] = __uint_as_float(pk << 16);
-      x[j + 1] = __uint_as_float(pk & 0xffff0000u);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r[j]);
-  }
+// Folds 32 consecutive logits (weight columns c0..c0+31, already rounded as
+// the launch asks) into the state: exponent arguments and sums in packed f32
+// pairs.
+__device__ __forceinline__ void fold32v(RowState& st, float (&x)[32], int64_t c0, int64_t vocab,
+                                        int64_t local_id) {
   if (c0 + 32 > vocab) {  // padding columns of the last tile
 #pragma unroll
     for (int j = 0; j < 32; ++j)
@@ -313,6 +333,51 @@ __device__ __forceinline__ void fold32(RowState& st, const uint32_t (&r)[32], in
     if (jn >= 0) st.first_nan = c0 + jn;
   }
   st.s += cs;
+}
+
+// Folds 32 consecutive columns (raw f32 bits from TMEM), rounded to bf16 in
+// pairs (one cvt per two) when the launch asks for it.
+__device__ __forceinline__ void fold32(RowState& st, const uint32_t (&r)[32], int64_t c0,
+                                       int64_t vocab, int64_t local_id, int round_bf16) {
+  float x[32];
+  if (round_bf16) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      uint32_t pk;  // upper half: column j + 1, lower half: column j
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+          : "=r"(pk)
+          : "f"(__uint_as_float(r[j + 1])), "f"(__uint_as_float(r[j])));
+      x[j] = __uint_as_float(pk << 16);
+      x[j + 1] = __uint_as_float(pk & 0xffff0000u);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r[j]);
+  }
+  fold32v(st, x, c0, vocab, local_id);
+}
+
+// The shard record of one row over one work unit's columns [c_lo, ...):
+// (max, sum of exp(x - max), global first argmax with the NaN flag, logit at
+// the row's token id).
+__device__ __forceinline__ void store_unit_record(const LmParams& p, const RowState& st,
+                                                  int64_t vg, int64_t row, int64_t c_lo,
+                                                  int64_t local_id) {
+  cid_shard_record_t rec;
+  rec.max_logit = st.m;
+  const bool special = !(st.m > -INFINITY && st.m < INFINITY) || st.s != st.s;
+  if (special) {
+    const int64_t local = st.first_nan >= 0 ? st.first_nan : (st.where >= 0 ? st.where : c_lo);
+    rec.sum_exp = st.m == -INFINITY ? 0.0f : __int_as_float(0x7fffffff);
+    rec.index = static_cast<int32_t>(p.vocab_offset + local) |
+                (st.first_nan >= 0 ? static_cast<int32_t>(0x80000000u) : 0);
+  } else {
+    const float top = ex2(fmaf(st.m, kLog2e, -st.off));
+    rec.sum_exp = __fdiv_rn(st.s, top);
+    rec.index = static_cast<int32_t>(p.vocab_offset + st.where);
+  }
+  rec.current = local_id >= 0 ? st.cur : 0.0f;
+  p.records[vg * p.rows + row] = rec;
 }
 
 // ---------------------------------------------------------------------------
@@ -507,23 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
-      if (valid) {
-        cid_shard_record_t rec;
-        rec.max_logit = st.m;
-        const bool special = !(st.m > -INFINITY && st.m < INFINITY) || st.s != st.s;
-        if (special) {
-          const int64_t local = st.first_nan >= 0 ? st.first_nan : (st.where >= 0 ? st.where : c_lo);
-          rec.sum_exp = st.m == -INFINITY ? 0.0f : __int_as_float(0x7fffffff);
-          rec.index = static_cast<int32_t>(p.vocab_offset + local) |
-                      (st.first_nan >= 0 ? static_cast<int32_t>(0x80000000u) : 0);
-        } else {
-          const float top = ex2(fmaf(st.m, kLog2e, -st.off));
-          rec.sum_exp = __fdiv_rn(st.s, top);
-          rec.index = static_cast<int32_t>(p.vocab_offset + st.where);
-        }
-        rec.current = local_id >= 0 ? st.cur : 0.0f;
-        p.records[vg * p.rows + row] = rec;
-      }
+      if (valid) store_unit_record(p, st, vg, row, c_lo, local_id);
     }
   }
 
@@ -535,6 +584,228 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
   }
 }
+
+// ---------------------------------------------------------------------------
+// The wide-tile kernel: 256 rows x 256 columns per CTA
+// ---------------------------------------------------------------------------
+//
+// Per K step the MMA warp issues two M=128 MMAs that share the weight slice:
+// rows 0-127 of the tile into TMEM columns 0-255, rows 128-255 into columns
+// 256-511.  The tile holds all of TMEM, so the epilogue cannot work on one
+// accumulator while the other fills; instead each of the eight epilogue
+// warps (two per TMEM lane quarter, one per half of the tile) reads its row's
+// 256 columns with tcgen05.ld, rounds them to bf16 pairs into 128 registers,
+// and releases the accumulator; the fold of those registers then overlaps
+// the next tile's MMAs.  The registers come from a setmaxnreg split: the
+// control warpgroup (warp 0 TMA, warp 1 MMA, warps 2-3 idle) gives up
+// registers, the two epilogue warpgroups take them.  Bitwise the same
+// records as the 128-row kernel: every logit is accumulated over K in the
+// same order and rounded the same way.
+__global__ void __launch_bounds__(kWThreads, 1)
+    lm_head_wide_kernel(const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_b, LmParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  unsigned char* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);  // 1024-byte aligned
+  unsigned char* stage_a = smem;
+  unsigned char* stage_b = smem + kWStages * kWStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWStages * kWStageBytes);
+  uint64_t* empty = full + kWStages;
+  uint64_t* acc_full = empty + kWStages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 8);  // one arrival per epilogue warp
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kWCtrlRegs));
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer ----------------
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0, issue_par = 0;  // per-stage bits: ever issued, parity of last issue
+      bool ok = true;
+      for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        int64_t rb, vg;
+        unit_coords(p, u, rb, vg);
+        const int64_t t0 = vg * p.group_tiles;
+        const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
+        for (int64_t t = t0; ok && t < t1; ++t) {
+          for (int64_t kt = 0; kt < p.ktiles; ++kt) {
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort, kWaitNs)) {
+              if (!*abort) raise_abort(abort, p.status);
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&full[s], kWStageBytes);
+            tma_load_2d(stage_a + s * kWStageA, &map_a, static_cast<int32_t>(kt * kBK),
+                        static_cast<int32_t>(rb * kWRows), &full[s]);
+            tma_load_2d(stage_b + s * kWStageB, &map_b, static_cast<int32_t>(kt * kBK),
+                        static_cast<int32_t>(t * kBN), &full[s]);
+            issued |= 1u << s;
+            issue_par = (issue_par & ~(1u << s)) | (ph << s);
+            if (++s == kWStages) {
+              s = 0;
+              ph ^= 1u;
+            }
+          }
+        }
+      }
+      // copies in flight land before the CTA exits (immediate unless aborted)
+      for (int i = 0; i < kWStages; ++i)
+        if (issued & (1u << i)) mbar_wait(&full[i], (issue_par >> i) & 1u, nullptr, kDrainNs);
+    } else if (warp == 1 && lane == 0) {
+      // ---------------- MMA issuer ----------------
+      int s = 0;
+      uint32_t ph = 0, aph = 0;
+      uint64_t* last_bar = nullptr;  // barrier of the last commit and its phase parity
+      uint32_t last_par = 0;
+      bool ok = true;
+      for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+        int64_t rb, vg;
+        unit_coords(p, u, rb, vg);
+        const int64_t t0 = vg * p.group_tiles;
+        const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
+        for (int64_t t = t0; ok && t < t1; ++t) {
+          if (!mbar_wait(acc_empty, aph ^ 1u, abort, kWaitNs)) {
+            if (!*abort) raise_abort(abort, p.status);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int64_t kt = 0; kt < p.ktiles; ++kt) {
+            if (!mbar_wait(&full[s], ph, abort, kWaitNs)) {
+              if (!*abort) raise_abort(abort, p.status);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(stage_a + s * kWStageA);
+            const uint32_t b0 = smem_u32(stage_b + s * kWStageB);
+#pragma unroll
+            for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+              // K advance inside the 128-byte swizzle atom: +32 bytes per 16
+              // elements; rows 128-255 of the hidden slice start 128 rows
+              // (16 KiB, sixteen 1024-byte atoms) further
+              const uint32_t acc = (kt | kk) != 0 ? 1u : 0u;
+              const uint64_t bd = sw128_desc(b0 + kk * 32);
+              umma_bf16(tmem_base, sw128_desc(a0 + kk * 32), bd, acc);
+              umma_bf16(tmem_base + kBN, sw128_desc(a0 + kBM * 128 + kk * 32), bd, acc);
+            }
+            umma_commit(&empty[s]);  // frees the stage once these MMAs are done
+            last_bar = &empty[s];
+            last_par = ph;
+            if (++s == kWStages) {
+              s = 0;
+              ph ^= 1u;
+            }
+          }
+          if (!ok) break;
+          umma_commit(acc_full);  // the tile is complete
+          last_bar = acc_full;
+          last_par = aph;
+          aph ^= 1u;
+        }
+      }
+      // MMAs in flight finish before the TMEM is freed (immediate unless aborted)
+      if (last_bar != nullptr) mbar_wait(last_bar, last_par, nullptr, kDrainNs);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kWEpiRegs));
+    // ---------------- epilogue: thread = row ----------------
+    const int half = (warp - 4) >> 2;  // tile rows 0-127 (TMEM columns 0-255) or 128-255
+    const int quarter = warp & 3;      // TMEM lanes 32*quarter .. +31
+    const int row_in_block = half * kBM + quarter * 32 + lane;
+    uint32_t aph = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; ok && u < p.units; u += gridDim.x) {
+      int64_t rb, vg;
+      unit_coords(p, u, rb, vg);
+      const int64_t t0 = vg * p.group_tiles;
+      const int64_t t1 = t0 + p.group_tiles < p.tiles ? t0 + p.group_tiles : p.tiles;
+      const int64_t row = rb * kWRows + row_in_block;
+      const bool valid = row < p.rows;
+      const int64_t c_lo = t0 * kBN;                                // weight columns
+      const int64_t c_hi = t1 * kBN < p.vocab ? t1 * kBN : p.vocab;  // of this unit
+      const int64_t id = valid ? p.ids[row] - p.vocab_offset : -1;
+      const int64_t local_id = (id >= c_lo && id < c_hi) ? id : INT64_MIN / 2;
+      RowState st{-INFINITY, -INFINITY, 0.0f, 0.0f, -1, -1, 0.0f};
+      for (int64_t t = t0; t < t1; ++t) {
+        bool got = mbar_wait(acc_full, aph, abort, kWaitNs);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          if (lane == 0 && !*abort) raise_abort(abort, p.status);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(half * kBN);
+        uint32_t pk[kBN / 2];  // bf16 pairs: columns 2j (low half) and 2j + 1
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t r[32];
+          tmem_issue32(taddr + static_cast<uint32_t>(c * 32), r);
+          tmem_wait32(r);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+                : "=r"(pk[c * 16 + j])
+                : "f"(__uint_as_float(r[2 * j + 1])), "f"(__uint_as_float(r[2 * j])));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);  // the next tile may accumulate
+        aph ^= 1u;
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) {
+          float x[32];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            x[2 * j] = __uint_as_float(pk[c * 16 + j] << 16);
+            x[2 * j + 1] = __uint_as_float(pk[c * 16 + j] & 0xffff0000u);
+          }
+          fold32v(st, x, t * kBN + c * 32, p.vocab, local_id);
+        }
+      }
+      if (!ok) break;
+      if (valid) store_unit_record(p, st, vg, row, c_lo, local_id);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {  // thread-safe one-time init
@@ -570,15 +841,39 @@ struct Plan {
   int64_t tiles, group_tiles, groups, row_blocks, units;
 };
 
-Plan plan(int64_t rows, int64_t vocab) {
+// Work units of a launch whose tiles are tile_rows high (the vocabulary
+// grouping, and so the workspace, does not depend on it).
+Plan plan(int64_t rows, int64_t vocab, int64_t tile_rows = kBM) {
   Plan pl;
   pl.tiles = (vocab + kBN - 1) / kBN;
   pl.group_tiles = (pl.tiles + kMaxGroups - 1) / kMaxGroups;
   if (pl.group_tiles < 4) pl.group_tiles = 4;
   pl.groups = (pl.tiles + pl.group_tiles - 1) / pl.group_tiles;
-  pl.row_blocks = (rows + kBM - 1) / kBM;
+  pl.row_blocks = (rows + tile_rows - 1) / tile_rows;
   pl.units = pl.row_blocks * pl.groups;
   return pl;
+}
+
+// Smallest launch served by the wide-tile kernel.  Measured at 128256 x 4096
+// against the 128-row kernel: 1024 rows 0.77 vs 0.90 ms, 2048 rows level,
+// 4096 rows 2.95 vs 3.29 ms, 8192 rows 6.03 vs 6.61 ms.  Fewer rows are a
+// handful of row blocks, where 256-row tiles leave SMs idle.
+constexpr int64_t kWideMinRows = 1024;
+
+// The wide kernel's setmaxnreg split is sized for kWLaunchRegs registers a
+// thread at launch; a build whose register allocation differs uses the
+// 128-row kernel instead (a split above the launch's registers would never
+// complete).
+bool wide_kernel_ready() {
+  static const bool ok = [] {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, lm_head_wide_kernel) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    return fa.numRegs == kWLaunchRegs;
+  }();
+  return ok;
 }
 
 }  // namespace
@@ -626,9 +921,12 @@ int launch_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const v
                    int64_t (&offsets)[kMaxGroups + 1], int& groups) {
   // TMA: row strides and base addresses 16-byte aligned
   if (workspace_bytes < cid_lm_head_workspace_bytes(rows, vocab)) return CID_ERR_SCRATCH_LIMIT;
-  const Plan pl = plan(rows, vocab);
+  const bool wide = round_bf16 && rows >= kWideMinRows && rows <= INT32_MAX - kWRows &&
+                    wide_kernel_ready();
+  const int64_t tile_rows = wide ? kWRows : kBM;
+  const Plan pl = plan(rows, vocab, tile_rows);
   CUtensorMap map_a, map_b;
-  int rc = make_map(&map_a, hidden, hidden_dim, rows, kBM);
+  int rc = make_map(&map_a, hidden, hidden_dim, rows, static_cast<int>(tile_rows));
   if (rc == CID_OK) rc = make_map(&map_b, weight, hidden_dim, vocab, kBN);
   if (rc != CID_OK) return rc;
   LmParams p = {};
@@ -641,17 +939,27 @@ int launch_lm_head(const void* hidden, int64_t rows, int64_t hidden_dim, const v
   p.groups = pl.groups;
   p.row_blocks = pl.row_blocks;
   p.units = pl.units;
+  p.row_group = wide ? kWRowGroup : kRowGroup;
   p.ids = token_ids;
   p.records = static_cast<cid_shard_record_t*>(workspace);
   p.status = status;
   p.round_bf16 = round_bf16 ? 1 : 0;
-  cudaError_t e = cudaFuncSetAttribute(lm_head_stats_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kSmemBytes));
-  if (e != cudaSuccess) return record_cuda_error(e);
   const int64_t grid = pl.units < sm_count() ? pl.units : sm_count();
-  lm_head_stats_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, as_stream(stream)>>>(
-      map_a, map_b, p);
+  if (wide) {
+    cudaError_t e = cudaFuncSetAttribute(lm_head_wide_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kWSmemBytes));
+    if (e != cudaSuccess) return record_cuda_error(e);
+    lm_head_wide_kernel<<<static_cast<unsigned>(grid), kWThreads, kWSmemBytes,
+                          as_stream(stream)>>>(map_a, map_b, p);
+  } else {
+    cudaError_t e = cudaFuncSetAttribute(lm_head_stats_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) return record_cuda_error(e);
+    lm_head_stats_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes,
+                           as_stream(stream)>>>(map_a, map_b, p);
+  }
   rc = launch_result();
   if (rc != CID_OK) return rc;
   groups = static_cast<int>(pl.groups);

@@ -76,8 +76,14 @@ def _check(ids, h, w, round_bf16):
     (5, 300, 64),        # one row block, two tiles, the last partial
     (300, 1000, 128),    # partial row block, 4 tiles
     (256, 5000, 72),     # hidden not a multiple of 64 (zero-filled K tail)
-    (1100, 32000, 256),  # many work units and vocabulary groups
+    (1000, 32000, 256),  # many work units and vocabulary groups
     (130, 70001, 64),    # groups of more than 4 tiles, odd vocabulary
+    # launches of 1024 rows and more run the wide (256-row) tiles when the
+    # logits are rounded to bf16
+    (1024, 4096, 128),   # whole 256-row blocks
+    (1100, 32000, 256),  # partial 256-row block
+    (2300, 32000, 72),   # partial 256-row block, K tail
+    (4100, 70001, 64),   # many raster groups, odd vocabulary
 ])
 def test_lm_head_matches_materialised_logits(rows, vocab, hidden, round_bf16) -> None:
     import cid_engine
@@ -85,6 +91,24 @@ def test_lm_head_matches_materialised_logits(rows, vocab, hidden, round_bf16) ->
     cid_engine.device_status(0, reset=True)
     ids, h, w = _inputs(rows, vocab, hidden, seed=rows + vocab)
     _check(ids, h, w, round_bf16)
+    assert cid_engine.device_status(0) == 0
+
+
+def test_lm_head_wide_and_128_row_tiles_agree_bitwise() -> None:
+    """The wide-tile kernel (launches of 1024 rows and more, bf16-rounded
+    logits) accumulates every logit over K in the order of the 128-row
+    kernel and rounds it the same way, so the statistics of a row are
+    bit-identical whichever kernel served the launch: the first 1023 rows
+    (128-row tiles) against the same rows of a 2600-row launch (wide tiles,
+    a partial last block)."""
+    import cid_engine
+
+    ids, h, w = _inputs(2600, 50001, 200, seed=11)
+    cid_engine.device_status(0, reset=True)
+    big = cid_engine.lm_head_display_statistics(ids, h, w)
+    small = cid_engine.lm_head_display_statistics(ids[:1023], h[:1023].contiguous(), w)
+    for a, b in zip(big, small):
+        assert torch.equal(a[:1023], b)
     assert cid_engine.device_status(0) == 0
 
 
