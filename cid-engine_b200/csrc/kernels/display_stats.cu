@@ -929,36 +929,126 @@ __device__ __forceinline__ int32_t peer_lead(const uint32_t* flag, uint32_t epoc
   return static_cast<int32_t>(f - epoch);
 }
 
+// The statistics of one row from its ranks' records in an inbox (16-byte
+// aligned slots, world <= kMaxPeers): each record read once, as one vector,
+// into registers; the arithmetic and order are combine_row's.
+__device__ __forceinline__ void combine_row_inbox(const CombineParams& p, int64_t row) {
+  const float qnan = __int_as_float(0x7fffffff);
+  float mx[kMaxPeers], se[kMaxPeers], cu[kMaxPeers];
+  int32_t ix[kMaxPeers];
+#pragma unroll
+  for (int r = 0; r < kMaxPeers; ++r) {
+    if (r < p.world) {
+      const uint4 v =
+          *reinterpret_cast<const uint4*>(p.records + static_cast<int64_t>(r) * p.stride + row);
+      mx[r] = __uint_as_float(v.x);
+      se[r] = __uint_as_float(v.y);
+      ix[r] = static_cast<int32_t>(v.z);
+      cu[r] = __uint_as_float(v.w);
+    } else {
+      mx[r] = -INFINITY;
+      se[r] = 0.0f;
+      ix[r] = 0;
+      cu[r] = 0.0f;
+    }
+  }
+  // NaN anywhere: the lowest rank's first NaN (ranks hold ascending columns)
+  int nan_rank = -1;
+#pragma unroll
+  for (int r = kMaxPeers - 1; r >= 0; --r)
+    if (r < p.world && ix[r] < 0) nan_rank = r;
+  if (nan_rank >= 0) {
+    int32_t idx = 0;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r == nan_rank) idx = ix[r];
+    p.predicted[row] = idx & 0x7fffffff;
+    p.confidence[row] = qnan;
+    p.current[row] = qnan;
+    return;
+  }
+  float M = -INFINITY;
+  int32_t idx = ix[0];
+#pragma unroll
+  for (int r = 0; r < kMaxPeers; ++r) {
+    if (r < p.world && mx[r] > M) {
+      M = mx[r];
+      idx = ix[r];
+    }
+  }
+  p.predicted[row] = idx;
+  if (!isfinite(M)) {
+    p.confidence[row] = qnan;
+    p.current[row] = qnan;
+    return;
+  }
+  float S = 0.0f;
+#pragma unroll
+  for (int r = 0; r < kMaxPeers; ++r) {
+    if (r >= p.world || mx[r] == -INFINITY) continue;
+    S += se[r] * ex2((mx[r] - M) * kLog2e);
+  }
+  const int64_t id = p.ids[row];
+  int owner = -1;
+  for (int r = 0; r < p.world; ++r)
+    if (id >= p.offsets[r] && id < p.offsets[r + 1]) owner = r;
+  float cur = qnan;
+  if (owner >= 0) {
+    float x = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r == owner) x = cu[r];
+    cur = __fdiv_rn(ex2((x - M) * kLog2e), S);
+  } else if (p.status) {
+    atomicOr(p.status, CID_STATUS_TOKEN_ID_OUT_OF_RANGE);
+  }
+  p.confidence[row] = __fdiv_rn(1.0f, S);
+  p.current[row] = cur;
+}
+
+// Lanes 0..world-1 of warp 0 wait for their rank's flag in parallel; the
+// CTA's verdict (0 go, else the status bit) is returned to every lane of the
+// warp.
+__device__ __forceinline__ uint32_t wait_flags(const uint32_t* flags, int world, uint32_t epoch,
+                                               unsigned long long wait_ns) {
+  const int lane = threadIdx.x & 31;
+  uint32_t bit = 0;
+  if (lane < world) {
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+      const int32_t lead = peer_lead(flags + lane, epoch);
+      if (lead == 0 || lead == 1) break;
+      if (lead > 1) {
+        bit = CID_STATUS_PEER_OUT_OF_STEP;
+        break;
+      }
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > wait_ns) {
+        bit = CID_STATUS_PEER_TIMEOUT;
+        break;
+      }
+      __nanosleep(256);
+    }
+  }
+  // out of step outranks a timeout (a peer that moved on explains the wait)
+  const unsigned oos = __ballot_sync(0xffffffffu, bit == CID_STATUS_PEER_OUT_OF_STEP);
+  const unsigned tmo = __ballot_sync(0xffffffffu, bit == CID_STATUS_PEER_TIMEOUT);
+  return oos ? CID_STATUS_PEER_OUT_OF_STEP : (tmo ? CID_STATUS_PEER_TIMEOUT : 0u);
+}
+
 __global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uint32_t epoch,
                                      unsigned long long wait_ns) {
   constexpr uint32_t kPoisoned = CID_STATUS_PEER_TIMEOUT | CID_STATUS_PEER_OUT_OF_STEP;
   __shared__ int ready;
-  if (threadIdx.x == 0) {
-    bool ok = !(p.status && (*reinterpret_cast<volatile uint32_t*>(p.status) & kPoisoned));
-    uint32_t bit = 0;
-    unsigned long long t0;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-    for (int q = 0; q < p.world && ok; ++q) {
-      for (;;) {
-        const int32_t lead = peer_lead(flags + q, epoch);
-        if (lead == 0 || lead == 1) break;
-        if (lead > 1) {
-          ok = false;
-          bit = CID_STATUS_PEER_OUT_OF_STEP;
-          break;
-        }
-        unsigned long long t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        if (t - t0 > wait_ns) {
-          ok = false;
-          bit = CID_STATUS_PEER_TIMEOUT;
-          break;
-        }
-        __nanosleep(256);
-      }
+  if (threadIdx.x < 32) {
+    const bool poisoned = p.status && (*reinterpret_cast<volatile uint32_t*>(p.status) & kPoisoned);
+    const uint32_t bit = poisoned ? 0u : wait_flags(flags, p.world, epoch, wait_ns);
+    if (threadIdx.x == 0) {
+      if (bit && p.status) atomicOr(p.status, bit);
+      ready = (!poisoned && bit == 0) ? 1 : 0;
     }
-    if (bit && p.status) atomicOr(p.status, bit);
-    ready = ok ? 1 : 0;
   }
   __syncthreads();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -970,15 +1060,12 @@ __global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uin
     }
     return;
   }
-  if (row < p.rows) combine_row(p, row);
+  if (row < p.rows) combine_row_inbox(p, row);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int q = 0; q < p.world; ++q) {
-      if (peer_lead(flags + q, epoch) > 1) {
-        if (p.status) atomicOr(p.status, CID_STATUS_PEER_OUT_OF_STEP);
-        break;
-      }
-    }
+  if (threadIdx.x < 32) {
+    const bool ahead = threadIdx.x < p.world && peer_lead(flags + threadIdx.x, epoch) > 1;
+    if (__ballot_sync(0xffffffffu, ahead) && threadIdx.x == 0 && p.status)
+      atomicOr(p.status, CID_STATUS_PEER_OUT_OF_STEP);
   }
 }
 
