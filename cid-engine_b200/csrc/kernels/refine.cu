@@ -1,4 +1,6 @@
-// Display refinement policy on the device: one CTA per display row.
+// Display refinement policy on the device: one warp per display row for
+// rows of up to 128 positions (refine_warp_kernel, no block barriers), one
+// CTA per row for longer rows (refine_kernel).
 //
 // Semantics are those of the reference CPU policy
 // (csrc/refine.cpp:93-429 of fwerkor/cid-engine v1.1.0), which there runs on
@@ -554,6 +556,288 @@ __global__ void __launch_bounds__(kT) refine_kernel(RefineParams p) {
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Warp-per-row refinement for short rows (tokens <= kWarpRowMax): the same
+// policy as refine_kernel with no block barrier in it.  A warp stages its row
+// in its own slice of shared memory, finds the first EOS with ballots, runs
+// the structural search with one start per lane and a shuffle arg-best, and
+// selects the reveal / revision top-k by counting, for each member, the
+// members of its class ahead of it in stable descending order: a member's
+// composite key is (order key << 32) | ~index, so "ahead" is one 64-bit
+// compare and the k members with rank < k are exactly those
+// std::stable_sort(>) puts first.  Decode steps refine few short rows, where
+// the CTA kernel's dozen barriers were most of the step's refinement time.
+// ---------------------------------------------------------------------------
+constexpr int kWarpPos = 4;                      // positions per lane
+constexpr int kWarpRowMax = 32 * kWarpPos;       // 128
+constexpr int kWarpRowsPerCta = 4;
+
+struct WarpRow {
+  int64_t tok[kWarpRowMax];
+  int64_t pred[kWarpRowMax];
+  int64_t res[kWarpRowMax];
+  uint64_t key[kWarpRowMax];  // composite selection key of a member
+  float gain[kWarpRowMax];
+  int8_t cls[kWarpRowMax];    // 0 reveal member, 1 revision member, -1 neither
+};
+
+// Warp-uniform first index in [lo, hi) where pred == value, -1 if none.
+__device__ __forceinline__ int warp_first_pred(const WarpRow& w, int lo, int hi, int64_t value) {
+  const int lane = threadIdx.x & 31;
+  for (int b = lo; b < hi; b += 32) {
+    const int i = b + lane;
+    const unsigned bits = __ballot_sync(0xffffffffu, i < hi && w.pred[i] == value);
+    if (bits) return b + __ffs(bits) - 1;
+  }
+  return -1;
+}
+
+__device__ __forceinline__ Candidate shfl_cand(const Candidate& c, int d) {
+  Candidate o;
+  o.anchor = __shfl_xor_sync(0xffffffffu, c.anchor, d);
+  o.gain = __shfl_xor_sync(0xffffffffu, c.gain, d);
+  o.neg_growth = __shfl_xor_sync(0xffffffffu, c.neg_growth, d);
+  o.start = __shfl_xor_sync(0xffffffffu, c.start, d);
+  o.kind = __shfl_xor_sync(0xffffffffu, c.kind, d);
+  o.del = __shfl_xor_sync(0xffffffffu, c.del, d);
+  o.ins = __shfl_xor_sync(0xffffffffu, c.ins, d);
+  o.valid = __shfl_xor_sync(0xffffffffu, c.valid, d);
+  return o;
+}
+
+__global__ void __launch_bounds__(32 * kWarpRowsPerCta) refine_warp_kernel(RefineParams p,
+                                                                           int64_t batch) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ WarpRow rows[kWarpRowsPerCta];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpRowsPerCta + warp;
+  if (row >= batch) return;  // warp-uniform; the kernel has no block barrier
+  WarpRow& w = rows[warp];
+  const int L = static_cast<int>(p.tokens);
+  const int64_t base = row * p.tokens;
+  const int64_t mask = p.mask_id, eos = p.eos_id;
+
+  // stage the row: every lane's loads issued before any store
+  int64_t t[kWarpPos], pr[kWarpPos];
+  float cf[kWarpPos], cu[kWarpPos];
+#pragma unroll
+  for (int j = 0; j < kWarpPos; ++j) {
+    const int i = lane + 32 * j;
+    if (i < L) {
+      t[j] = __ldg(p.ids + base + i);
+      pr[j] = __ldg(p.pred + base + i);
+      cf[j] = __ldg(p.conf + base + i);
+      cu[j] = __ldg(p.cur + base + i);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kWarpPos; ++j) {
+    const int i = lane + 32 * j;
+    if (i < L) {
+      w.tok[i] = t[j];
+      w.res[i] = t[j];
+      w.pred[i] = pr[j];
+      w.gain[i] = __fsub_rn(cf[j], cu[j]);  // refine.cpp:277
+    }
+  }
+  __syncwarp();
+
+  // 1. first EOS (refine.cpp:280-288)
+  int eos_pos = -1;
+  if (p.has_eos) {
+#pragma unroll
+    for (int j = 0; j < kWarpPos; ++j) {
+      const int i = lane + 32 * j;
+      const unsigned bits = __ballot_sync(0xffffffffu, i < L && t[j] == eos);
+      if (bits) {
+        eos_pos = 32 * j + __ffs(bits) - 1;
+        break;
+      }
+    }
+  }
+  bool structural_done = false;
+  // 2. structural edit (refine.cpp:290-319, 93-218): one start per lane, the
+  // offsets scanned as in refine_kernel, the best candidate by butterfly
+  if (eos_pos > 0 && p.revision != 0.0) {
+    constexpr int kChunk = 8;
+    int64_t budget = static_cast<int64_t>(ceil(static_cast<double>(eos_pos) * p.revision));
+    budget = imax(1, imin(32, budget));
+    const int64_t alen = eos_pos + 1;  // active = tok[0, eos_pos]
+    const int64_t Ll = L;
+    Candidate best{};
+    best.valid = 0;
+    for (int64_t s = lane; s < eos_pos; s += 32) {
+      const float gs = w.gain[s];
+      const int64_t ts = w.tok[s], ps = w.pred[s];
+      if (ps == ts || static_cast<double>(gs) < p.margin) continue;
+      const int64_t klen = imin(3, alen - s);
+      const int64_t qlast = imin(s + budget, Ll - klen);
+      const int64_t dlen = imin(3, Ll - s);
+      const int64_t rlast = dlen < 2 ? s : imin(imin(eos_pos - 1, s + budget), alen - dlen);
+      int64_t q_hit = -1, r_hit = -1;
+      for (int64_t o0 = 1; o0 <= budget && (q_hit < 0 || r_hit < 0); o0 += kChunk) {
+        int64_t pv[kChunk], tv[kChunk];
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) {
+          const int64_t o = s + o0 + j;
+          pv[j] = (q_hit < 0 && o <= qlast) ? w.pred[o] : ~ts;  // ~x never equals x
+          tv[j] = (r_hit < 0 && o <= rlast) ? w.tok[o] : ~ps;
+        }
+        unsigned qm = 0, rm = 0;
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) {
+          qm |= static_cast<unsigned>(pv[j] == ts) << j;
+          rm |= static_cast<unsigned>(tv[j] == ps) << j;
+        }
+        while (qm && q_hit < 0) {
+          const int64_t q = s + o0 + (__ffs(qm) - 1);
+          bool eq = true;
+          for (int64_t k = 1; k < klen && eq; ++k) eq = w.pred[q + k] == w.tok[s + k];
+          if (eq) q_hit = q;
+          qm &= qm - 1;
+        }
+        while (rm && r_hit < 0) {
+          const int64_t r = s + o0 + (__ffs(rm) - 1);
+          bool eq = true;
+          for (int64_t k = 1; k < dlen && eq; ++k) eq = w.tok[r + k] == w.pred[s + k];
+          if (eq) r_hit = r;
+          rm &= rm - 1;
+        }
+      }
+      if (q_hit >= 0) {
+        bool ok = true;  // pred[s, q) must hold neither mask nor EOS
+        for (int64_t k = s; k < q_hit && ok; ++k) ok = w.pred[k] != mask && w.pred[k] != eos;
+        if (ok) {
+          const int64_t anchor = match_run(w.pred, q_hit, Ll, w.tok, s, alen);
+          const int64_t growth = q_hit - s;
+          if (anchor >= 2 && static_cast<double>(gs) >= p.margin && eos_pos + 1 + growth <= Ll) {
+            const Candidate c{anchor, gs, -growth, s, 1, 0, growth, 1};
+            if (cand_better(c, best)) best = c;
+          }
+        }
+      }
+      if (r_hit >= 0) {
+        const int64_t anchor = match_run(w.pred, s, Ll, w.tok, r_hit, alen);
+        const int64_t del = r_hit - s;
+        if (anchor >= 2 && static_cast<double>(gs) >= p.margin && eos_pos + 1 - del <= Ll) {
+          const Candidate c{anchor, gs, -del, s, 0, del, 0, 1};
+          if (cand_better(c, best)) best = c;
+        }
+      }
+    }
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const Candidate o = shfl_cand(best, d);
+      if (cand_better(o, best)) best = o;
+    }
+    if (best.valid) {
+      // splice: tok[0, s) + pred[s, s+ins) + tok[s+del, eos] + mask fill
+      for (int64_t i = lane; i < Ll; i += 32) {
+        int64_t v;
+        if (i < best.start) v = w.tok[i];
+        else if (i < best.start + best.ins) v = w.pred[i];
+        else {
+          const int64_t j = i - best.ins + best.del;
+          v = j <= eos_pos ? w.tok[j] : mask;
+        }
+        w.res[i] = v;
+      }
+      structural_done = true;
+    }
+    __syncwarp();
+  }
+
+  if (!structural_done) {
+    const int stop = eos_pos >= 0 ? eos_pos : L;  // refine.cpp:321
+    const float margin_f = static_cast<float>(p.margin);
+    const bool revise = p.revision != 0.0;
+    // 3a/3b. reveal (refine.cpp:322-342) and revision (refine.cpp:344-379)
+    int c_of[kWarpPos];
+    unsigned nm = 0, nc = 0;
+#pragma unroll
+    for (int j = 0; j < kWarpPos; ++j) {
+      const int i = lane + 32 * j;
+      int c = -1;
+      if (i < stop) {
+        if (t[j] == mask) c = 0;
+        else if (revise && pr[j] != t[j] && w.gain[i] >= margin_f) c = 1;
+      }
+      c_of[j] = c;
+      nm += c == 0;
+      nc += c == 1;
+    }
+    nm = __reduce_add_sync(0xffffffffu, nm);
+    nc = __reduce_add_sync(0xffffffffu, nc);
+    int64_t k0 = 0, k1 = 0;
+    if (nm > 0 && p.reveal != 0.0)
+      k0 = static_cast<int64_t>(ceil(static_cast<double>(nm) * p.reveal));
+    if (revise && nc > 0)
+      k1 = imin(static_cast<int64_t>(ceil(static_cast<double>(stop - static_cast<int>(nm)) *
+                                          p.revision)),
+                static_cast<int64_t>(nc));
+    uint64_t my_key[kWarpPos];
+#pragma unroll
+    for (int j = 0; j < kWarpPos; ++j) {
+      const int i = lane + 32 * j;
+      int c = c_of[j];
+      if (c >= 0 && (c == 0 ? k0 : k1) <= 0) c = -1;
+      c_of[j] = c;
+      const uint32_t ok = c < 0 ? 0u : order_key(c == 0 ? cf[j] : w.gain[i]);
+      my_key[j] = (static_cast<uint64_t>(ok) << 32) | static_cast<uint32_t>(~static_cast<uint32_t>(i));
+      if (i < stop) {
+        w.key[i] = my_key[j];
+        w.cls[i] = static_cast<int8_t>(c);
+      }
+    }
+    __syncwarp();
+    if (k0 > 0 || k1 > 0) {
+      int rank[kWarpPos] = {};
+      for (int jj = 0; jj < stop; ++jj) {
+        const uint64_t kj = w.key[jj];  // same address in every lane: a broadcast
+        const int cj = w.cls[jj];
+#pragma unroll
+        for (int j = 0; j < kWarpPos; ++j) rank[j] += (cj == c_of[j] && kj > my_key[j]) ? 1 : 0;
+      }
+#pragma unroll
+      for (int j = 0; j < kWarpPos; ++j) {
+        const int i = lane + 32 * j;
+        if (c_of[j] >= 0 && rank[j] < (c_of[j] == 0 ? k0 : k1)) w.res[i] = pr[j];
+      }
+    }
+    __syncwarp();
+    // 3c. EOS expansion (refine.cpp:381-406), double margin; positions >= eos_pos
+    if (revise && eos_pos >= 0 && eos_pos + 1 < L && w.pred[eos_pos] != eos &&
+        static_cast<double>(w.gain[eos_pos]) >= p.margin) {
+      const int64_t basec = imax(1, eos_pos + 1);
+      const int64_t ebudget =
+          imax(1, static_cast<int64_t>(ceil(static_cast<double>(basec) * p.reveal)));
+      int new_eos = static_cast<int>(imin(L - 1, eos_pos + ebudget));
+      const int first = warp_first_pred(w, eos_pos + 1, new_eos + 1, eos);
+      if (first >= 0) new_eos = first;
+      for (int i = eos_pos + lane; i < new_eos; i += 32) w.res[i] = w.pred[i];
+      __syncwarp();
+      if (lane == 0) w.res[new_eos] = eos;
+    }
+    __syncwarp();
+  }
+
+  // 4. mask everything after the first EOS of the result (refine.cpp:410-423)
+  int cut = L;
+  if (p.has_eos) {
+    for (int b = 0; b < L; b += 32) {
+      const int i = b + lane;
+      const unsigned bits = __ballot_sync(0xffffffffu, i < L && w.res[i] == eos);
+      if (bits) {
+        cut = b + __ffs(bits) - 1;
+        break;
+      }
+    }
+  }
+  for (int i = lane; i < L; i += 32) p.out[base + i] = i > cut ? mask : w.res[i];
+}
+
 }  // namespace
 }  // namespace cid
 
@@ -591,6 +875,12 @@ extern "C" int cid_refine_display(const int64_t* token_ids, const float* confide
   p.revision = revision_fraction;
   p.margin = revision_margin;
   p.out = out;
+  if (tokens <= kWarpRowMax) {  // one warp per row
+    p.use_smem = 1;
+    const int64_t grid = (batch + kWarpRowsPerCta - 1) / kWarpRowsPerCta;
+    return launch_pdl(refine_warp_kernel, dim3(static_cast<unsigned>(grid)),
+                      dim3(32 * kWarpRowsPerCta), 0, as_stream(stream), p, batch);
+  }
   constexpr int64_t kRowBytes = 3 * 8 + 2 * 4;  // shared bytes per position
   p.use_smem = tokens <= kSmemLimit / kRowBytes;
   const int64_t smem = p.use_smem ? tokens * kRowBytes : 0;
