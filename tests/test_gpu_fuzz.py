@@ -92,13 +92,16 @@ def test_fuzz_refinement(seed, reveal, revision, margin, tokens, batch, with_eos
     assert torch.equal(got.cpu(), exp)
 
 
-@pytest.mark.parametrize("tokens", [1, 31, 32, 33, 127, 128, 129, 160])
+@pytest.mark.parametrize("tokens", [1, 31, 32, 33, 127, 128, 129, 160, 5535, 5536])
 @pytest.mark.parametrize("with_eos", [False, True])
-def test_refinement_at_the_warp_row_limit(tokens, with_eos) -> None:
+def test_refinement_at_the_kernel_limits(tokens, with_eos) -> None:
     """Rows of up to 128 positions are refined by one warp each, longer rows by
-    a CTA each: both sides of the limit, with structural-heavy rows (shifted
-    predictions), many rows per launch, against the oracle."""
-    ids, (conf, pred, cur) = cases.refine_inputs_large(tokens, 37, tokens, structural=0.5)
+    a CTA each, staged in shared memory up to 5535 positions (37 bytes a
+    position) and read from global memory beyond: both sides of each limit,
+    with structural-heavy rows (shifted predictions), many rows per launch,
+    against the oracle."""
+    ids, (conf, pred, cur) = cases.refine_inputs_large(tokens, 37 if tokens < 1000 else 3, tokens,
+                                                       structural=0.5)
     eos = 1 if with_eos else None
     for reveal, revision, margin in ((0.25, 0.1, 0.05), (1.0, 1.0, 0.0), (0.5, 0.0, 0.1)):
         got = torch.ops.cid_engine.refine_display_from_statistics(
