@@ -169,16 +169,18 @@ def test_lm_head_validation() -> None:
         cid_engine.lm_head_display_statistics(ids[:4], h, w)
 
 
+@pytest.mark.parametrize("rows", [300, 1100])
 @pytest.mark.parametrize("world", [2, 3])
-def test_lm_head_shard_records_combine_to_unsharded(world) -> None:
+def test_lm_head_shard_records_combine_to_unsharded(world, rows) -> None:
     """Vocabulary shards of the weight (as a vocabulary-parallel LM head holds
     them), reduced to records and combined, give the unsharded statistics:
     every column's logit is accumulated in the same order, so the argmax is
-    exact; the sums are regrouped (rtol 1e-5)."""
+    exact; the sums are regrouped (rtol 1e-5).  1100 rows run the wide-tile
+    kernel, whose records carry the shard's column offset too."""
     import cid_engine
     from cid_engine import parallel
 
-    rows, V, H = 300, 20011, 128
+    V, H = 20011, 128
     ids, h, w = _inputs(rows, V, H, seed=world)
     conf, pred, cur = cid_engine.lm_head_display_statistics(ids, h, w)
     offs = parallel.shard_offsets(V, world)
