@@ -1042,6 +1042,7 @@ __global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uin
                                      unsigned long long wait_ns) {
   constexpr uint32_t kPoisoned = CID_STATUS_PEER_TIMEOUT | CID_STATUS_PEER_OUT_OF_STEP;
   __shared__ int ready;
+  pdl_wait();
   if (threadIdx.x < 32) {
     const bool poisoned = p.status && (*reinterpret_cast<volatile uint32_t*>(p.status) & kPoisoned);
     const uint32_t bit = poisoned ? 0u : wait_flags(flags, p.world, epoch, wait_ns);
@@ -1051,6 +1052,7 @@ __global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uin
     }
   }
   __syncthreads();
+  pdl_trigger();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (!ready) {
     if (row < p.rows) {
@@ -1468,6 +1470,8 @@ __global__ void push_records_kernel(const cid_shard_record_t* src, PeerSlots slo
 // released into this rank's flag word of every inbox.  A rank that acquires
 // the flag (combine_inbox_kernel) sees every record of the epoch.
 __global__ void publish_epoch_kernel(PeerSlots slots, int world, uint32_t epoch) {
+  pdl_wait();  // the record kernel has completed and its stores are performed
+  pdl_trigger();
   __threadfence_system();
   const int q = threadIdx.x;
   if (q < world)
@@ -1596,8 +1600,8 @@ extern "C" int cid_display_shard_records_to_peers(
   rc = dispatch_stats<false, Mode::kRecord>(dtype, prm, as_stream(stream));
   if (rc != CID_OK) return rc;
   // a plain launch: it starts once every record store above has completed
-  publish_epoch_kernel<<<1, 32, 0, as_stream(stream)>>>(slots, world, epoch);
-  return launch_result();
+  return launch_pdl(publish_epoch_kernel, dim3(1), dim3(32), 0, as_stream(stream), slots, world,
+                    epoch);
 }
 
 extern "C" int cid_display_combine_inbox(void* inbox, int world,
@@ -1629,10 +1633,10 @@ extern "C" int cid_display_combine_inbox(void* inbox, int world,
   prm.status = status;
   const int threads = 256;
   const int64_t blocks = (rows + threads - 1) / threads;
-  combine_inbox_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(
-      prm, inbox_flags(inbox, world, rows_capacity), epoch,
-      static_cast<unsigned long long>(wait_seconds * 1e9));
-  return launch_result();
+  return launch_pdl(combine_inbox_kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0,
+                    as_stream(stream), prm,
+                    static_cast<const uint32_t*>(inbox_flags(inbox, world, rows_capacity)), epoch,
+                    static_cast<unsigned long long>(wait_seconds * 1e9));
 }
 
 extern "C" int cid_peer_push_records(const cid_shard_record_t* records, int64_t rows, int rank,
@@ -1653,6 +1657,6 @@ extern "C" int cid_peer_push_records(const cid_shard_record_t* records, int64_t 
       records, slots, world, rows);
   rc = launch_result();
   if (rc != CID_OK) return rc;
-  publish_epoch_kernel<<<1, 32, 0, as_stream(stream)>>>(slots, world, epoch);
-  return launch_result();
+  return launch_pdl(publish_epoch_kernel, dim3(1), dim3(32), 0, as_stream(stream), slots, world,
+                    epoch);
 }
