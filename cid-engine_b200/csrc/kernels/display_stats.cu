@@ -907,9 +907,9 @@ __global__ void combine_records_kernel(CombineParams p) {
 }
 
 // Combine from this rank's inbox once every rank has published `epoch` in
-// its flag word there (thread 0 of each CTA waits, acquire at system scope,
-// bounded by wait_ns; a wait that runs out sets CID_STATUS_PEER_TIMEOUT and
-// the CTA writes NaN statistics with predicted 0).
+// its flag word there (one warp waits, acquire at system scope, bounded by
+// wait_ns; a wait that runs out sets CID_STATUS_PEER_TIMEOUT and the merge
+// writes NaN statistics with predicted 0).
 //
 // A rank can run at most one epoch ahead of another while every combine
 // waits for all flags (its push of epoch e+2 is ordered after a combine of
@@ -917,8 +917,8 @@ __global__ void combine_records_kernel(CombineParams p) {
 // e), so a flag of epoch or epoch+1 means the parity slot of `epoch` holds
 // that epoch's records.  A flag two or more epochs ahead means that peer gave
 // up waiting on this rank earlier and may already have overwritten the slot:
-// the CTA then sets CID_STATUS_PEER_OUT_OF_STEP and writes NaN.  The flags
-// are read once more after the rows are combined, so a peer that overtook
+// the wait sets CID_STATUS_PEER_OUT_OF_STEP and the merge writes NaN.  The
+// flags are read once more after the rows are combined, so a peer that overtook
 // the slot while it was being read is caught too (the step's statistics are
 // then invalid and the bit says so).  Once either peer bit is set in the
 // status word the exchange is poisoned: later combines write NaN without
@@ -1038,21 +1038,37 @@ __device__ __forceinline__ uint32_t wait_flags(const uint32_t* flags, int world,
   return oos ? CID_STATUS_PEER_OUT_OF_STEP : (tmo ? CID_STATUS_PEER_TIMEOUT : 0u);
 }
 
-__global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uint32_t epoch,
-                                     unsigned long long wait_ns) {
+// The wait and the merge are two launches: one warp waits for the flags
+// (acquire at system scope, in wait_flags) and leaves its verdict in the
+// inbox's own verdict word; the merge kernel, launched as its programmatic
+// dependent, starts after the wait kernel has completed, so its plain loads
+// see every record the flags published, and none of its CTAs issues a
+// system-scope acquire (one per CTA cost tens of microseconds per step on
+// peer-mapped inboxes).
+__global__ void wait_inbox_kernel(const uint32_t* flags, uint32_t* verdict, int world,
+                                  uint32_t epoch, unsigned long long wait_ns, uint32_t* status) {
   constexpr uint32_t kPoisoned = CID_STATUS_PEER_TIMEOUT | CID_STATUS_PEER_OUT_OF_STEP;
-  __shared__ int ready;
   pdl_wait();
-  if (threadIdx.x < 32) {
-    const bool poisoned = p.status && (*reinterpret_cast<volatile uint32_t*>(p.status) & kPoisoned);
-    const uint32_t bit = poisoned ? 0u : wait_flags(flags, p.world, epoch, wait_ns);
-    if (threadIdx.x == 0) {
-      if (bit && p.status) atomicOr(p.status, bit);
-      ready = (!poisoned && bit == 0) ? 1 : 0;
-    }
-  }
-  __syncthreads();
   pdl_trigger();
+  const bool poisoned = status && (*reinterpret_cast<volatile uint32_t*>(status) & kPoisoned);
+  const uint32_t bit = poisoned ? 0u : wait_flags(flags, world, epoch, wait_ns);
+  if (threadIdx.x == 0) {
+    if (bit && status) atomicOr(status, bit);
+    *verdict = (!poisoned && bit == 0) ? epoch : ~epoch;
+  }
+}
+
+__device__ __forceinline__ int32_t peer_lead_relaxed(const uint32_t* flag, uint32_t epoch) {
+  uint32_t f;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(flag) : "memory");
+  return static_cast<int32_t>(f - epoch);
+}
+
+__global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags,
+                                     const uint32_t* verdict, uint32_t epoch) {
+  pdl_wait();  // the wait kernel has completed
+  pdl_trigger();
+  const bool ready = *verdict == epoch;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (!ready) {
     if (row < p.rows) {
@@ -1064,8 +1080,8 @@ __global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags, uin
   }
   if (row < p.rows) combine_row_inbox(p, row);
   __syncthreads();
-  if (threadIdx.x < 32) {
-    const bool ahead = threadIdx.x < p.world && peer_lead(flags + threadIdx.x, epoch) > 1;
+  if (threadIdx.x < 32) {  // a peer that overtook the slot while it was read
+    const bool ahead = threadIdx.x < p.world && peer_lead_relaxed(flags + threadIdx.x, epoch) > 1;
     if (__ballot_sync(0xffffffffu, ahead) && threadIdx.x == 0 && p.status)
       atomicOr(p.status, CID_STATUS_PEER_OUT_OF_STEP);
   }
@@ -1480,6 +1496,10 @@ __global__ void publish_epoch_kernel(PeerSlots slots, int world, uint32_t epoch)
 }
 
 constexpr size_t kInboxTail = 256;
+// Word of an inbox's tail (after the ranks' flag words) where this rank's
+// wait kernel leaves the epoch whose flags it saw complete; no peer writes it.
+constexpr int kVerdictWord = 32;
+static_assert(kMaxPeers <= kVerdictWord && (kVerdictWord + 1) * 4 <= kInboxTail, "inbox tail");
 
 size_t inbox_record_bytes(int world, int64_t capacity) {
   return 2 * static_cast<size_t>(world) * static_cast<size_t>(capacity) *
@@ -1633,10 +1653,15 @@ extern "C" int cid_display_combine_inbox(void* inbox, int world,
   prm.status = status;
   const int threads = 256;
   const int64_t blocks = (rows + threads - 1) / threads;
+  uint32_t* flags = inbox_flags(inbox, world, rows_capacity);
+  uint32_t* verdict = flags + kVerdictWord;
+  rc = launch_pdl(wait_inbox_kernel, dim3(1), dim3(32), 0, as_stream(stream),
+                  static_cast<const uint32_t*>(flags), verdict, world, epoch,
+                  static_cast<unsigned long long>(wait_seconds * 1e9), status);
+  if (rc != CID_OK) return rc;
   return launch_pdl(combine_inbox_kernel, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0,
-                    as_stream(stream), prm,
-                    static_cast<const uint32_t*>(inbox_flags(inbox, world, rows_capacity)), epoch,
-                    static_cast<unsigned long long>(wait_seconds * 1e9));
+                    as_stream(stream), prm, static_cast<const uint32_t*>(flags),
+                    static_cast<const uint32_t*>(verdict), epoch);
 }
 
 extern "C" int cid_peer_push_records(const cid_shard_record_t* records, int64_t rows, int rank,
