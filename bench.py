@@ -1351,8 +1351,9 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
             "parity": parity,
             "stages": stages,
             "e2e": e2e,
-            # records, push, publish, combine, refine (peers); records,
-            # combine, refine (NCCL; its all-gather kernel is NCCL's)
+            # records (storing into every inbox), publish, flag wait, merge,
+            # refine (peers); records, combine, refine (NCCL; its all-gather
+            # kernel is NCCL's)
             "gpu_launches": (5 if peers else 3) * K,
             "clocks": clk.summary(),
             "refine_loop": loop,
