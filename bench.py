@@ -1345,7 +1345,7 @@ def bench_vocab_parallel(args, display_inputs, ClockSampler, peaks, run_cpu_base
                          "traffic": (round(NCU_SHARD_TRAFFIC_PER_ROW[world] * rows)
                                      if world in NCU_SHARD_TRAFFIC_PER_ROW else None),
                          "kernel": "display_stats_rows_kernel<bf16, records> (per rank, max over ranks"
-                                   + ("; then pushed to the peers' inboxes)" if peers else ")"),
+                                   + ("; records stored into every rank's inbox)" if peers else ")"),
                          "peak_kind": peak_kind, "kernel_ms": round(kern_ms, 4),
                          "algorithmic_bytes_per_launch": alg},
             "parity": parity,
