@@ -1373,9 +1373,9 @@ def profile_case(name: str) -> None:
 
     import cid_engine
 
-    if name == "refine":  # refinement alone on rows [32, 1024] and [64, 4096]
+    if name == "refine":  # refinement alone: warp rows [1, 64], [64, 128]; CTA rows [32, 1024], [64, 4096]
         g = torch.Generator(device="cuda").manual_seed(1)
-        for B, L in ((32, 1024), (64, 4096)):
+        for B, L in ((1, 64), (64, 128), (32, 1024), (64, 4096)):
             ids = torch.randint(2, 32000, (B, L), generator=g, device="cuda")
             ids[torch.rand((B, L), generator=g, device="cuda") < 0.6] = MASK_ID
             ids[:, L // 2 + 7] = EOS_ID
