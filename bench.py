@@ -1464,7 +1464,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-loop", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--exchange", choices=("peers", "nccl"), default="peers",
                     help="N>1: record exchange inside the statistics kernel (peers) or NCCL all-gather")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
