@@ -803,6 +803,15 @@ def decode_suite(dev, graphs: bool) -> dict:
     return out
 
 
+def _time_into(res: dict, key: str, measure) -> None:
+    """res[key] = measure(), or None when the operator fails in this process
+    (an operator the loaded implementation does not support)."""
+    try:
+        res[key] = measure()
+    except Exception:  # noqa: BLE001 - recorded as a missing measurement
+        res[key] = None
+
+
 def secondary_suite(dev, graphs: bool) -> dict:
     """Per-call device time (us) of the operators the reference also ships as
     CUDA kernels, on the benchmark shapes, through whichever
@@ -854,6 +863,34 @@ def secondary_suite(dev, graphs: bool) -> dict:
     idx = torch.randint(0, 4096, (12,), generator=g).to(dev)
     res["snapshot_128x4096_bf16_us"] = timer(
         lambda: ops.materialize_cell_snapshot(sem, roles, unc, noise, life, sel, idx), 1000) * 1e3
+    # repetition statistics on the fp32 [4, 256, 32000] logits, two copies
+    # rotating (262 MB > L2)
+    rids, rlg = cases.display_f32_4x256x32000()
+    rids = rids.to(dev)
+    rcopies = [rlg.to(dev), rlg.to(dev)]
+    state = {"k": 0}
+
+    def rep_call():
+        lg = rcopies[state["k"] % 2]
+        state["k"] += 1
+        ops.display_token_statistics_with_repetition(rids, lg, MASK_ID, EOS_ID, 0.7)
+
+    _time_into(res, "repetition_stats_f32_4x256x32000_us", lambda: timer(rep_call, 64) * 1e3)
+    del rcopies
+    # display corruption at [64, 2048] over 50257 tokens (bench_small_workloads' inputs)
+    gd = torch.Generator().manual_seed(11)
+    B3, T3, V3 = 64, 2048, 50257
+    dc = [torch.randint(0, V3, (B3, T3), generator=gd), torch.rand(B3, generator=gd),
+          torch.rand(B3, T3, generator=gd) > 0.15, torch.rand(B3, T3, generator=gd),
+          torch.rand(B3, T3, generator=gd), torch.randint(1, V3, (B3, T3), generator=gd)]
+    dc = [t.to(dev) for t in dc]
+    _time_into(res, "display_corruption_64x2048_us", lambda: timer(
+        lambda: ops.display_corrupt_from_random(*dc, V3 - 1, EOS_ID, V3, 0.25), 1000) * 1e3)
+    # linear assignment: 4096 problems of 16 x 16 costs
+    costs = torch.randn(4096, 16, 16, generator=gd).to(dev)
+    counts = torch.full((4096,), 16, dtype=torch.int64).to(dev)
+    _time_into(res, "linear_assignment_4096x16x16_us", lambda: timer(
+        lambda: ops.batched_linear_assignment(costs, counts), 200) * 1e3)
     torch.cuda.empty_cache()
     return res
 
@@ -922,7 +959,8 @@ def bench_decode_and_reference_cuda(dev) -> dict:
     secondary = {}
     for k, v in sec.items():
         r = rsec.get(k)
-        secondary[k] = {"ours": round(v, 3), "reference_cuda": None if r is None else round(r, 3),
+        secondary[k] = {"ours": None if v is None else round(v, 3),
+                        "reference_cuda": None if r is None else round(r, 3),
                         "speedup": ratio(r, v)}
     return {"decode_rows": {"workload": "display statistics, logits bf16 [1, rows, 155136]; "
                                         "statistics + refinement at 64 rows",
