@@ -293,6 +293,34 @@ __device__ __forceinline__ int64_t wrap_vocab(int64_t id, int64_t offset, int64_
   return floor_mod(x, vocab);
 }
 
+// The four outputs of one position (ops.cpp:339-389): corrupted where the
+// uniform falls below the timestep on an eligible position, or at the row's
+// fallback position; a corrupted position whose replacement uniform is below
+// the replacement threshold takes the offset token (skipping the mask id, its
+// own id and EOS), every other corrupted position the mask id.
+__device__ __forceinline__ void write_display_corrupt(const DisplayCorruptParams& p, int64_t i,
+                                                      bool is_fallback, float t, bool el, float u,
+                                                      int64_t id, float rr, int64_t off) {
+  const bool pos = ((u < t) && el) || is_fallback;
+  bool rep = false;
+  int64_t value = id;
+  if (p.replace) {
+    rep = pos && (rr < p.repl_thr);  // ops.cpp:362-363
+    int64_t cand = wrap_vocab(id, off, p.vocab);
+    for (int it = 0; it < 3; ++it) {  // ops.cpp:366-376; cand stays in [0, vocab)
+      const bool forbidden = cand == p.mask_id || cand == id || (p.has_eos && cand == p.eos_id);
+      if (forbidden) cand = cand + 1 == p.vocab ? 0 : cand + 1;
+    }
+    if (rep) value = cand;
+  }
+  const bool msk = pos && !rep;
+  if (msk) value = p.mask_id;
+  p.corrupted[i] = value;
+  p.labels[i] = pos ? id : -100;  // ops.cpp:386-389
+  p.masked[i] = msk;
+  p.replaced[i] = rep;
+}
+
 constexpr int kCorruptBatch = 4;  // tokens per thread whose loads are issued together
 
 // One CTA of kBT threads per row, two passes over the row: the first finds
@@ -310,6 +338,46 @@ __global__ void __launch_bounds__(kBT) display_corrupt_kernel(DisplayCorruptPara
   const int64_t row = blockIdx.x;
   const int64_t base = row * p.tokens;
   const float t = load_float(p.tdt, p.ts, row);  // timesteps.to(float)
+  if (p.tokens <= int64_t{kBT} * U) {
+    // the row is one batch of loads: every input of the thread's tokens is
+    // loaded at once and kept in registers across the reductions (one memory
+    // round trip instead of two)
+    bool el[U];
+    float u[U], rr[U];
+    int64_t id[U], off[U];
+    int any = 0;
+    int64_t first = LLONG_MAX;
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t k = threadIdx.x + int64_t{j} * kBT;
+      const bool in = k < p.tokens;
+      el[j] = in && load_truthy(p.edt, p.elig, base + k);
+      u[j] = in ? load_float(p.rdt, p.crand, base + k) : 1.0f;
+      id[j] = in ? p.ids[base + k] : 0;
+      rr[j] = in && p.replace ? load_float(p.pdt, p.rrand, base + k) : 1.0f;
+      off[j] = in && p.replace ? p.roff[base + k] : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      any |= (u[j] < t) && el[j];  // ops.cpp:326-328
+      if (el[j] && first == LLONG_MAX) first = threadIdx.x + int64_t{j} * kBT;
+    }
+    any = __syncthreads_or(any);
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) first = min(first, __shfl_down_sync(0xffffffffu, first, d));
+    if ((threadIdx.x & 31) == 0) s_first[threadIdx.x >> 5] = first;
+    __syncthreads();
+    int64_t fe1 = s_first[0];
+#pragma unroll
+    for (int w = 1; w < kW; ++w) fe1 = min(fe1, s_first[w]);
+    const int64_t fb1 = (!any && t > 0.0f && fe1 != LLONG_MAX) ? fe1 : -1;
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int64_t k = threadIdx.x + int64_t{j} * kBT;
+      if (k < p.tokens) write_display_corrupt(p, base + k, k == fb1, t, el[j], u[j], id[j], rr[j], off[j]);
+    }
+    return;
+  }
   int any_corrupt = 0;
   int64_t first_elig = LLONG_MAX;
   for (int64_t k0 = threadIdx.x; k0 < p.tokens; k0 += int64_t{kBT} * U) {
@@ -355,26 +423,7 @@ __global__ void __launch_bounds__(kBT) display_corrupt_kernel(DisplayCorruptPara
     for (int j = 0; j < U; ++j) {
       const int64_t k = k0 + int64_t{j} * kBT;
       if (k >= p.tokens) break;
-      const int64_t i = base + k;
-      const bool pos = ((u[j] < t) && el[j]) || k == fallback;
-      bool rep = false;
-      int64_t value = id[j];
-      if (p.replace) {
-        rep = pos && (rr[j] < p.repl_thr);  // ops.cpp:362-363
-        int64_t cand = wrap_vocab(id[j], off[j], p.vocab);
-        for (int it = 0; it < 3; ++it) {  // ops.cpp:366-376; cand stays in [0, vocab)
-          const bool forbidden =
-              cand == p.mask_id || cand == id[j] || (p.has_eos && cand == p.eos_id);
-          if (forbidden) cand = cand + 1 == p.vocab ? 0 : cand + 1;
-        }
-        if (rep) value = cand;
-      }
-      const bool msk = pos && !rep;
-      if (msk) value = p.mask_id;
-      p.corrupted[i] = value;
-      p.labels[i] = pos ? id[j] : -100;  // ops.cpp:386-389
-      p.masked[i] = msk;
-      p.replaced[i] = rep;
+      write_display_corrupt(p, base + k, k == fallback, t, el[j], u[j], id[j], rr[j], off[j]);
     }
   }
 }
