@@ -912,7 +912,7 @@ __global__ void combine_records_kernel(CombineParams p) {
 // writes NaN statistics with predicted 0).
 //
 // A rank can run at most one epoch ahead of another while every combine
-// waits for all flags (its push of epoch e+2 is ordered after a combine of
+// waits for all flags (its records of epoch e+2 are ordered after a combine of
 // e+1 that needs this rank's e+1 records, which follow this rank's combine of
 // e), so a flag of epoch or epoch+1 means the parity slot of `epoch` holds
 // that epoch's records.  A flag two or more epochs ahead means that peer gave
@@ -1481,10 +1481,12 @@ __global__ void push_records_kernel(const cid_shard_record_t* src, PeerSlots slo
   for (int q = 0; q < others; ++q) slots.dst[q][row] = rec;
 }
 
-// Launched on the stream after the record and push kernels, so all their
-// stores have completed when it runs: a system-scope fence, then the epoch
-// released into this rank's flag word of every inbox.  A rank that acquires
-// the flag (combine_inbox_kernel) sees every record of the epoch.
+// Launched on the stream after the kernel that stored this rank's records
+// into every inbox (the record kernel, or push_records_kernel for records
+// made elsewhere), as a programmatic dependent that waits for its completion:
+// a system-scope fence, then the epoch released into this rank's flag word of
+// every inbox.  A rank that acquires the flag (wait_inbox_kernel) sees every
+// record of the epoch.
 __global__ void publish_epoch_kernel(PeerSlots slots, int world, uint32_t epoch) {
   pdl_wait();  // the record kernel has completed and its stores are performed
   pdl_trigger();
