@@ -837,7 +837,9 @@ __global__ void __launch_bounds__(kRowWarps * 32, kRep ? 7 : 0) display_stats_ro
 // Record combine (vocabulary-parallel statistics)
 // ---------------------------------------------------------------------------
 
-constexpr int kMaxWorld = 64;
+constexpr int kMaxWorld = 256;
+// Record merges over more ranks than this take a warp per row.
+constexpr int kWarpMergeWorld = 32;
 struct CombineParams {
   const cid_shard_record_t* records;
   int64_t stride;  // records between ranks (rows, or an inbox's capacity)
@@ -1085,6 +1087,117 @@ __global__ void combine_inbox_kernel(CombineParams p, const uint32_t* flags,
     if (__ballot_sync(0xffffffffu, ahead) && threadIdx.x == 0 && p.status)
       atomicOr(p.status, CID_STATUS_PEER_OUT_OF_STEP);
   }
+}
+
+// A row's merge over many ranks (the vocabulary groups of the fused LM head)
+// by one warp: lane l holds ranks l, l + 32, ... in ascending order; the
+// first NaN rank and the maximum (lowest rank on ties) are warp minima, the
+// sum is each lane's ascending partial sum, then a fixed butterfly over the
+// lanes.  Every lane returns the merged record of the row; `owner` is the
+// rank holding the row's token id (-1 when none does).
+struct WarpMerged {
+  cid_shard_record_t rec;  // max, sum of exp(x - max), index (NaN flag), current
+  int nan_rank;            // first rank with a NaN, kMaxWorld when none
+  bool owned;
+};
+
+__device__ __forceinline__ WarpMerged warp_merge_row(const CombineParams& p, int64_t row,
+                                                     int64_t id) {
+  const int lane = threadIdx.x & 31;
+  int nan_rank = kMaxWorld;
+  float mx = -INFINITY;
+  int mr = kMaxWorld;  // rank of the lane's first maximum
+  int owner = -1;
+  for (int r = lane; r < p.world; r += 32) {
+    const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
+    if (rec.index < 0 && nan_rank == kMaxWorld) nan_rank = r;
+    if (mr == kMaxWorld || rec.max_logit > mx) {  // the lane's first maximum
+      mx = rec.max_logit;
+      mr = r;
+    }
+    if (id >= p.offsets[r] && id < p.offsets[r + 1]) owner = r;
+  }
+  // maximum with the lowest rank on ties (NaN maxima never occur without a
+  // NaN flag, which takes the other path)
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, d);
+    const int orr = __shfl_xor_sync(0xffffffffu, mr, d);
+    if (om > mx || (om == mx && orr < mr)) {
+      mx = om;
+      mr = orr;
+    }
+    nan_rank = min(nan_rank, __shfl_xor_sync(0xffffffffu, nan_rank, d));
+    owner = max(owner, __shfl_xor_sync(0xffffffffu, owner, d));
+  }
+  WarpMerged out;
+  out.nan_rank = nan_rank;
+  out.owned = owner >= 0;
+  const int src = nan_rank < kMaxWorld ? nan_rank : (mr < kMaxWorld ? mr : 0);
+  const cid_shard_record_t pick = p.records[static_cast<int64_t>(src) * p.stride + row];
+  out.rec.index = pick.index;
+  out.rec.max_logit = nan_rank < kMaxWorld ? pick.max_logit : mx;
+  out.rec.current =
+      owner >= 0 ? p.records[static_cast<int64_t>(owner) * p.stride + row].current : 0.0f;
+  float S = 0.0f;
+  if (nan_rank == kMaxWorld && isfinite(mx)) {
+    for (int r = lane; r < p.world; r += 32) {
+      const cid_shard_record_t rec = p.records[static_cast<int64_t>(r) * p.stride + row];
+      if (rec.max_logit == -INFINITY) continue;
+      S += rec.sum_exp * ex2((rec.max_logit - mx) * kLog2e);
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(0xffffffffu, S, d);
+  }
+  out.rec.sum_exp = S;
+  return out;
+}
+
+// combine_records_kernel with a warp per row (world > kWarpMergeWorld).
+__global__ void combine_records_warp_kernel(CombineParams p) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= p.rows) return;  // warp-uniform
+  const int64_t id = p.ids[row];
+  const WarpMerged w = warp_merge_row(p, row, id);
+  if ((threadIdx.x & 31) != 0) return;
+  const float qnan = __int_as_float(0x7fffffff);
+  if (w.nan_rank < kMaxWorld) {
+    p.predicted[row] = w.rec.index & 0x7fffffff;
+    p.confidence[row] = qnan;
+    p.current[row] = qnan;
+    return;
+  }
+  const float M = w.rec.max_logit;
+  p.predicted[row] = w.rec.index;
+  if (!isfinite(M)) {
+    p.confidence[row] = qnan;
+    p.current[row] = qnan;
+    return;
+  }
+  const float S = w.rec.sum_exp;
+  float cur = qnan;
+  if (w.owned) {
+    cur = __fdiv_rn(ex2((w.rec.current - M) * kLog2e), S);
+  } else if (p.status) {
+    atomicOr(p.status, CID_STATUS_TOKEN_ID_OUT_OF_RANGE);
+  }
+  p.confidence[row] = __fdiv_rn(1.0f, S);
+  p.current[row] = cur;
+}
+
+// merge_records_kernel with a warp per row (world > kWarpMergeWorld).
+__global__ void merge_records_warp_kernel(CombineParams p, cid_shard_record_t* out) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (row >= p.rows) return;  // warp-uniform
+  const WarpMerged w = warp_merge_row(p, row, p.ids[row]);
+  if ((threadIdx.x & 31) != 0) return;
+  cid_shard_record_t m = w.rec;
+  if (w.nan_rank < kMaxWorld) {
+    m.sum_exp = __int_as_float(0x7fffffff);
+  } else if (!isfinite(m.max_logit)) {
+    m.sum_exp = m.max_logit == -INFINITY ? 0.0f : __int_as_float(0x7fffffff);
+  }
+  out[row] = m;
 }
 
 // Merges the records of W ascending column ranges of each row into the one
@@ -1416,6 +1529,12 @@ extern "C" int cid_display_merge_records(const cid_shard_record_t* records, int 
   prm.stride = rows;
   const int threads = 256;
   const int64_t blocks = (rows + threads - 1) / threads;
+  if (world > kWarpMergeWorld) {  // a warp per row
+    const int64_t wblocks = (rows * 32 + threads - 1) / threads;
+    merge_records_warp_kernel<<<static_cast<unsigned>(wblocks), threads, 0,
+                                as_stream(stream)>>>(prm, merged);
+    return launch_result();
+  }
   merge_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(prm,
                                                                                          merged);
   return launch_result();
@@ -1447,6 +1566,12 @@ extern "C" int cid_display_combine_records(const cid_shard_record_t* records, in
   prm.current = current_confidence;
   prm.status = status;
   const int threads = 256;
+  if (world > kWarpMergeWorld) {  // a warp per row
+    const int64_t blocks = (rows * 32 + threads - 1) / threads;
+    combine_records_warp_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                                  as_stream(stream)>>>(prm);
+    return launch_result();
+  }
   const int64_t blocks = (rows + threads - 1) / threads;
   combine_records_kernel<<<static_cast<unsigned>(blocks), threads, 0, as_stream(stream)>>>(prm);
   return launch_result();

@@ -56,16 +56,16 @@ constexpr int kStages = 4;
 constexpr int kAccBufs = 2;
 constexpr uint32_t kTmemCols = kAccBufs * kBN;  // 512: all of TMEM
 // Row blocks per raster group.  The CTAs running at once cover about
-// 148 / kRowGroup vocabulary groups (each 16 MB of weight at G = 8 tiles)
-// and kRowGroup hidden blocks (1 MB each); 32 keeps that set under the
+// 148 / kRowGroup vocabulary groups and kRowGroup hidden blocks (1 MB each);
+// with 8-tile units (16 MB of weight a group) 32 kept that set under the
 // 126 MB L2 (16 did not: ~150 MB), measured 1-2 % faster at 32768 x 128256
 // x 4096; 64 and 128 were slower.
 constexpr int kRowGroup = 32;
-constexpr int kMaxGroups = 64;                  // record combine limit
+constexpr int kMaxGroups = 256;                 // record combine limit
 // Wide tiles: 256 rows, 3 stages of 64 KiB (32 KiB hidden + 32 KiB weight).
 // Raster groups of 16 row blocks (4096 rows, the hidden set of kRowGroup
-// 128-row blocks): measured at 32768 x 128256 x 4096, DRAM reads 18.7 GB
-// with 16, 24.8 GB with 8, 34.6 GB with 4.
+// 128-row blocks): measured at 32768 x 128256 x 4096 with 8-tile units, DRAM
+// reads 18.7 GB with 16, 24.8 GB with 8, 34.6 GB with 4.
 constexpr int kWRows = 256;
 constexpr int kWStages = 3;
 constexpr int kWRowGroup = 16;
@@ -843,11 +843,19 @@ struct Plan {
 
 // Work units of a launch whose tiles are tile_rows high (the vocabulary
 // grouping, and so the workspace, does not depend on it).
+// Two vocabulary tiles per work unit (more when the vocabulary has more than
+// 2 * kMaxGroups tiles): many units balance the persistent CTAs' waves and let
+// every SM stream weight in launches of few row blocks.  Measured against 8
+// tiles at 128256 x 4096: 64 rows 177 vs 242 us, 1024 rows 727-759 vs
+// 813-878 us, 8192 rows 5.98 vs 6.03-6.12 ms, 32768 rows 23.9-24.2 vs
+// 24.6-24.7 ms.  It depends on the vocabulary only, so the workspace size
+// does too.
 Plan plan(int64_t rows, int64_t vocab, int64_t tile_rows = kBM) {
   Plan pl;
   pl.tiles = (vocab + kBN - 1) / kBN;
-  pl.group_tiles = (pl.tiles + kMaxGroups - 1) / kMaxGroups;
-  if (pl.group_tiles < 4) pl.group_tiles = 4;
+  pl.group_tiles = 2;
+  const int64_t least = (pl.tiles + kMaxGroups - 1) / kMaxGroups;
+  if (pl.group_tiles < least) pl.group_tiles = least;
   pl.groups = (pl.tiles + pl.group_tiles - 1) / pl.group_tiles;
   pl.row_blocks = (rows + tile_rows - 1) / tile_rows;
   pl.units = pl.row_blocks * pl.groups;

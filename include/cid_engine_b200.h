@@ -149,7 +149,7 @@ CID_API int cid_display_shard_records(cid_dtype_t dtype, const void* logits,
                               cid_shard_record_t* records, uint32_t* status,
                               void* stream);
 
-/* records: world x rows (rank-major), world <= 64.  shard_offsets: world+1
+/* records: world x rows (rank-major), world <= 256.  shard_offsets: world+1
  * ascending column offsets within [0, 2^31 - 1] on the HOST (shard r owns
  * [offsets[r], offsets[r+1])). */
 /* Merges records [world][rows] of ascending column ranges shard_offsets_host

@@ -330,9 +330,9 @@ static void fuzz_shard_records(input_t* in) {
 }
 
 static void fuzz_merge_combine(input_t* in, int combine) {
-  const int world = world_of(in, 64);
+  const int world = world_of(in, 256);
   int offsets_bad = 0;
-  int64_t* offs = offsets_of(in, world, 64, &offsets_bad);
+  int64_t* offs = offsets_of(in, world, 256, &offsets_bad);
   const cid_shard_record_t* rec = ptr_of(in, 0);
   int64_t* ids = ptr_of(in, 1);
   const int64_t rows = size_of(in);
