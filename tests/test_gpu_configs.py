@@ -150,11 +150,12 @@ def test_refine_large_rows_match_oracle(tokens: int) -> None:
         assert torch.equal(got.cpu(), exp)
 
 
-@pytest.mark.parametrize("world", [2, 3, 4, 8])
+@pytest.mark.parametrize("world", [2, 3, 4, 8, 40, 200])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_vocab_sharded_records_equal_unsharded(world: int, dtype: torch.dtype) -> None:
     """Vocabulary sharding emulated on one GPU: records of each shard,
-    combined, equal the unsharded statistics."""
+    combined, equal the unsharded statistics (past 32 shards the combine
+    takes a warp per row)."""
     from cid_engine import parallel
 
     g = torch.Generator().manual_seed(world)

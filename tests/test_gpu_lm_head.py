@@ -169,18 +169,19 @@ def test_lm_head_validation() -> None:
         cid_engine.lm_head_display_statistics(ids[:4], h, w)
 
 
-@pytest.mark.parametrize("rows", [300, 1100])
+@pytest.mark.parametrize("rows,V", [(300, 20011), (1100, 20011), (200, 70001)])
 @pytest.mark.parametrize("world", [2, 3])
-def test_lm_head_shard_records_combine_to_unsharded(world, rows) -> None:
+def test_lm_head_shard_records_combine_to_unsharded(world, rows, V) -> None:
     """Vocabulary shards of the weight (as a vocabulary-parallel LM head holds
     them), reduced to records and combined, give the unsharded statistics:
     every column's logit is accumulated in the same order, so the argmax is
     exact; the sums are regrouped (rtol 1e-5).  1100 rows run the wide-tile
-    kernel, whose records carry the shard's column offset too."""
+    kernel, whose records carry the shard's column offset too; 70001 columns
+    make more than 32 groups a shard, merged by a warp per row."""
     import cid_engine
     from cid_engine import parallel
 
-    V, H = 20011, 128
+    H = 128
     ids, h, w = _inputs(rows, V, H, seed=world)
     conf, pred, cur = cid_engine.lm_head_display_statistics(ids, h, w)
     offs = parallel.shard_offsets(V, world)
