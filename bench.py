@@ -683,7 +683,9 @@ def bench_small_workloads(dev) -> dict:
         "masked_diffusion_64x2048": {"workload": "ids [64,2048], mask id 50256",
                                   "us_per_call": round(ms3 * 1e3, 3),
                                   "GBps": round(2_753_032 / (ms3 * 1e-3) / 1e9, 1),
-                                  "launches_per_call": 2, "timing": "CUDA graph, 1000 calls"},
+                                  "launches_per_call": 1,
+                                  "timing": "CUDA graph, 1000 calls (captured: one kernel a call; "
+                                            "eager: two)"},
         "repetition_stats_f32_4x256x32000": {"workload": "fp32 [4,256,32000], mask 0, eos 1, multiplier 0.7",
                                   "us_per_call": round(ms_rep * 1e3, 2),
                                   "logits_GBps": round(131_072_000 / (ms_rep * 1e-3) / 1e9, 1),

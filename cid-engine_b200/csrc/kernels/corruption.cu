@@ -1,10 +1,12 @@
 // Training-corruption kernels (fwerkor/cid-engine v1.1.0 semantics):
-//  * masked diffusion (csrc/ops.cpp:394-444): one CTA per row (256 to
-//    1024 threads, four tokens' loads in flight per thread), mask =
-//    u < ratio, empty-row fallback on argmin(u); the two metrics are summed
-//    by a second one-block kernel in a fixed order from per-row counts kept
-//    in a caller-provided workspace, so they are bit-identical run to run
-//    (the reference CUDA kernel adds them with float atomics);
+//  * masked diffusion (csrc/ops.cpp:394-444): one CTA per row (256 or 512
+//    threads, eight or four tokens' loads in flight per thread), mask =
+//    u < ratio, empty-row fallback on argmin(u); the two metrics come from
+//    the exact integer count of masked tokens and a fixed-order double sum
+//    of the ratios, so they are bit-identical run to run (the reference CUDA
+//    kernel adds them with float atomics): eagerly a second one-block kernel
+//    sums per-row counts kept in a caller-provided workspace; inside a CUDA
+//    graph the row that finishes last computes them, in one kernel;
 //  * thought corruption (csrc/ops.cpp:258-290): one CTA per slot row, alpha
 //    computed once per row, every arithmetic step rounded to the storage
 //    dtype as ATen does;
@@ -20,7 +22,6 @@ namespace cid {
 namespace {
 
 constexpr int kT = 256;
-constexpr int kWarps = kT / 32;
 
 // ---------------------------------------------------------------------------
 // masked diffusion
@@ -37,8 +38,15 @@ struct MaskedParams {
   uint8_t* masked;
   float* ratio;
   float* metrics;
-  int64_t* counts;  // workspace: per-row masked count
+  int64_t* counts;  // workspace: per-row masked count (two-kernel form)
+  // One-kernel form: a zeroed accumulator, (rows done << 40) + masked
+  // tokens, that the row finishing last reads back and clears.
+  unsigned long long* slot;
 };
+
+constexpr int kSlotShift = 40;
+constexpr int64_t kSlotMaxRows = (int64_t{1} << (64 - kSlotShift)) - 1;
+constexpr int64_t kSlotMaxTokens = int64_t{1} << kSlotShift;
 
 // NaN-first argmin order of ATen min(1).
 __device__ __forceinline__ bool min_better(float v, int64_t i, float bv, int64_t bi) {
@@ -48,25 +56,66 @@ __device__ __forceinline__ bool min_better(float v, int64_t i, float bv, int64_t
   return v < bv || (v == bv && i < bi);
 }
 
-constexpr int kRowBatch = 4;  // tokens per thread whose loads are issued together
+// ratio = float32(float32(r * span) + lo) (ops.cpp:424-425)
+__device__ __forceinline__ float row_ratio(const MaskedParams& p, int64_t row) {
+  return __fadd_rn(__fmul_rn(p.ratio_random[row], p.span), p.lo);
+}
 
-// One CTA of kBT threads per row.  Each thread issues the loads of kRowBatch
-// tokens (kBT apart: every load instruction is coalesced) before it writes
-// any output, so a row costs one or two memory round trips, not one per
-// token a thread handles.
-template <int kBT>
+constexpr int kMetricThreads = 256;  // the ratio sum's order: 256 strided partial sums
+
+// The batch's ratio sum in the metrics kernel's order: thread t of the first
+// kMetricThreads adds rows t, t + 256, ... in double, the warps reduce by
+// shuffles, warp 0..7 sums are added in order.  `rq` is this thread's
+// partial sum; the caller provides s_r[8].  Returns the sum in thread 0.
+__device__ __forceinline__ double ratio_sum_tail(double rq, double* s_r) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) rq += __shfl_down_sync(0xffffffffu, rq, d);
+  if (threadIdx.x < kMetricThreads && (threadIdx.x & 31) == 0) s_r[threadIdx.x >> 5] = rq;
+  __syncthreads();
+  double tr = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < kMetricThreads / 32; ++w) tr += s_r[w];
+  return tr;
+}
+
+__device__ __forceinline__ void write_masked_metrics(float* metrics, int64_t masked_total,
+                                                     double ratio_sum, int64_t batch,
+                                                     int64_t tokens) {
+  metrics[0] = static_cast<float>(static_cast<double>(masked_total) /
+                                  static_cast<double>(batch * tokens));
+  metrics[1] = static_cast<float>(ratio_sum / static_cast<double>(batch));
+}
+
+// One CTA of kBT threads per row.  Each thread issues the loads of U tokens
+// (kBT apart: every load instruction is coalesced) before it writes any
+// output, so a row costs one or two memory round trips, not one per token a
+// thread handles.
+//
+// kOne: the whole op in one kernel.  Each CTA adds (1 << 40) + its row's
+// masked count to p.slot with one atomic; the CTA whose add completes the
+// batch has every row's count in the value it reads back, so no other data
+// crosses CTAs and no fence is needed.  It writes both metrics and clears
+// the slot for the next launch.  Batches of up to 256 rows: every CTA loads
+// the batch's ratio inputs beside its row and reduces them with its count,
+// so the last CTA only adds eight partial sums; larger batches: the last CTA
+// sums them after its add.
+template <int kBT, int U, bool kOne>
 __global__ void __launch_bounds__(kBT) masked_diffusion_kernel(MaskedParams p) {
+  static_assert(kBT >= kMetricThreads, "the ratio sum needs 256 threads");
   pdl_wait();
   pdl_trigger();
   constexpr int kW = kBT / 32;
-  constexpr int U = kRowBatch;
   __shared__ int64_t s_cnt[kW];
   __shared__ float s_min[kW];
   __shared__ int64_t s_idx[kW];
+  __shared__ double s_r[kMetricThreads / 32];
+  __shared__ unsigned long long s_old;
   const int64_t row = blockIdx.x;
   const int64_t base = row * p.tokens;
-  // ratio = float32(float32(r * span) + lo) (ops.cpp:424-425)
-  const float r = __fadd_rn(__fmul_rn(p.ratio_random[row], p.span), p.lo);
+  const float r = row_ratio(p, row);
+  const bool early_ratios = kOne && p.batch <= kMetricThreads;
+  double rq = 0.0;
+  if (early_ratios && threadIdx.x < p.batch) rq = static_cast<double>(row_ratio(p, threadIdx.x));
   int64_t cnt = 0;
   float bv = __int_as_float(0x7f800000);  // +inf
   int64_t bi = LLONG_MAX;
@@ -110,6 +159,11 @@ __global__ void __launch_bounds__(kBT) masked_diffusion_kernel(MaskedParams p) {
     s_min[warp] = bv;
     s_idx[warp] = bi;
   }
+  if (early_ratios) {  // uniform over the CTA
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) rq += __shfl_down_sync(0xffffffffu, rq, d);
+    if (threadIdx.x < kMetricThreads && (threadIdx.x & 31) == 0) s_r[warp] = rq;
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int64_t total = 0;
@@ -128,54 +182,91 @@ __global__ void __launch_bounds__(kBT) masked_diffusion_kernel(MaskedParams p) {
       total = 1;
     }
     p.ratio[row] = r;
-    p.counts[row] = total;
+    if constexpr (!kOne) {
+      p.counts[row] = total;
+    } else {
+      const unsigned long long add =
+          (1ull << kSlotShift) | static_cast<unsigned long long>(total);
+      const unsigned long long now = atomicAdd(p.slot, add) + add;
+      s_old = now;
+      if (early_ratios && static_cast<int64_t>(now >> kSlotShift) == p.batch) {
+        double tr = 0.0;
+        for (int w = 0; w < kMetricThreads / 32; ++w) tr += s_r[w];
+        write_masked_metrics(p.metrics,
+                             static_cast<int64_t>(now & ((1ull << kSlotShift) - 1)), tr,
+                             p.batch, p.tokens);
+        *p.slot = 0;
+      }
+    }
+  }
+  if constexpr (kOne) {
+    if (early_ratios) return;
+    __syncthreads();
+    const unsigned long long now = s_old;
+    if (static_cast<int64_t>(now >> kSlotShift) != p.batch) return;  // uniform over the CTA
+    double rs = 0.0;
+    if (threadIdx.x < kMetricThreads)
+      for (int64_t b = threadIdx.x; b < p.batch; b += kMetricThreads)
+        rs += static_cast<double>(row_ratio(p, b));
+    const double tr = ratio_sum_tail(rs, s_r);
+    if (threadIdx.x == 0) {
+      write_masked_metrics(p.metrics, static_cast<int64_t>(now & ((1ull << kSlotShift) - 1)),
+                           tr, p.batch, p.tokens);
+      *p.slot = 0;
+    }
   }
 }
 
-// Row kernel at the block size that covers a row in one batch of loads
-// where the row allows it.
-int launch_masked_rows(const MaskedParams& p, cudaStream_t s) {
+// Rows of up to 4096 tokens: 256 threads with eight tokens' loads in flight
+// each; longer rows: 512 threads with four.  (Config-3 rows of 2048 tokens:
+// 256 threads 3.1 us a launch, 512 threads 3.8 us, 1024 threads 5.5 us;
+// 8 rows of 16384: 512 threads fastest.)
+int launch_masked_rows(const MaskedParams& p, cudaStream_t s, bool one_kernel) {
   const dim3 grid(static_cast<unsigned>(p.batch));
-  if (p.tokens <= 256 * kRowBatch)
-    return launch_pdl(masked_diffusion_kernel<256>, grid, dim3(256), 0, s, p);
-  if (p.tokens <= 512 * kRowBatch)
-    return launch_pdl(masked_diffusion_kernel<512>, grid, dim3(512), 0, s, p);
-  return launch_pdl(masked_diffusion_kernel<1024>, grid, dim3(1024), 0, s, p);
+  if (p.tokens <= 4096)
+    return one_kernel ? launch_pdl(masked_diffusion_kernel<256, 8, true>, grid, dim3(256), 0, s, p)
+                      : launch_pdl(masked_diffusion_kernel<256, 8, false>, grid, dim3(256), 0, s, p);
+  return one_kernel ? launch_pdl(masked_diffusion_kernel<512, 4, true>, grid, dim3(512), 0, s, p)
+                    : launch_pdl(masked_diffusion_kernel<512, 4, false>, grid, dim3(512), 0, s, p);
 }
 
-__global__ void __launch_bounds__(kT) masked_metrics_kernel(const int64_t* counts,
-                                                            const float* ratio, int64_t batch,
-                                                            int64_t tokens, float* metrics) {
+__global__ void __launch_bounds__(kMetricThreads) masked_metrics_kernel(const int64_t* counts,
+                                                                        const float* ratio,
+                                                                        int64_t batch,
+                                                                        int64_t tokens,
+                                                                        float* metrics) {
   pdl_wait();
   pdl_trigger();
-  __shared__ int64_t s_c[kWarps];
-  __shared__ double s_r[kWarps];
+  constexpr int kMW = kMetricThreads / 32;
+  __shared__ int64_t s_c[kMW];
+  __shared__ double s_r[kMW];
   int64_t c = 0;
   double rs = 0.0;
-  for (int64_t b = threadIdx.x; b < batch; b += kT) {
+  for (int64_t b = threadIdx.x; b < batch; b += kMetricThreads) {
     c += counts[b];
     rs += static_cast<double>(ratio[b]);
   }
 #pragma unroll
-  for (int d = 16; d > 0; d >>= 1) {
-    c += __shfl_down_sync(0xffffffffu, c, d);
-    rs += __shfl_down_sync(0xffffffffu, rs, d);
-  }
-  if ((threadIdx.x & 31) == 0) {
-    s_c[threadIdx.x >> 5] = c;
-    s_r[threadIdx.x >> 5] = rs;
-  }
-  __syncthreads();
+  for (int d = 16; d > 0; d >>= 1) c += __shfl_down_sync(0xffffffffu, c, d);
+  if ((threadIdx.x & 31) == 0) s_c[threadIdx.x >> 5] = c;
+  const double tr = ratio_sum_tail(rs, s_r);
   if (threadIdx.x == 0) {
     int64_t tc = 0;
-    double tr = 0.0;
-    for (int w = 0; w < kWarps; ++w) {
-      tc += s_c[w];
-      tr += s_r[w];
-    }
-    metrics[0] = static_cast<float>(static_cast<double>(tc) / static_cast<double>(batch * tokens));
-    metrics[1] = static_cast<float>(tr / static_cast<double>(batch));
+    for (int w = 0; w < kMW; ++w) tc += s_c[w];
+    write_masked_metrics(metrics, tc, tr, batch, tokens);
   }
+}
+
+// Launches the masked-diffusion row kernel and its metrics: one kernel when
+// `slot` (a zeroed accumulator) is given, else the row kernel and the
+// one-block metrics kernel over p.counts.
+int launch_masked(MaskedParams p, unsigned long long* slot, cudaStream_t s) {
+  p.slot = slot;
+  int rc = launch_masked_rows(p, s, slot != nullptr);
+  if (rc != CID_OK || slot != nullptr) return rc;
+  return launch_pdl(masked_metrics_kernel, dim3(1), dim3(kMetricThreads), 0, s,
+                    static_cast<const int64_t*>(p.counts), static_cast<const float*>(p.ratio),
+                    p.batch, p.tokens, p.metrics);
 }
 
 // ---------------------------------------------------------------------------
@@ -462,6 +553,61 @@ extern "C" size_t cid_masked_diffusion_workspace_bytes(int64_t batch) {
   return batch > 0 && batch <= kMaxRows ? static_cast<size_t>(batch) * sizeof(int64_t) : 0;
 }
 
+// ---------------------------------------------------------------------------
+// Masked diffusion captured into a CUDA graph runs as one kernel.  Its
+// accumulator must be zero when the kernel starts and the kernel clears it
+// when it ends, so a launch takes a slot of its own for as long as the graph
+// exists: slots come from a zero-initialised array in the library's device
+// image and are never handed out twice.  A graph's replays run one after
+// another, so they share its slot safely; two instances of one graph (two
+// executable graphs made from it) must not run at the same time.  Eager
+// calls, calls captured before any eager call has looked the array up on
+// that device (the lookup could invalidate a capture) and calls beyond the
+// last slot run the two-kernel form over the caller's workspace, with
+// bit-identical results.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr int kMaskedSlots = 4096;
+constexpr int kSlotDevices = 64;
+static __device__ __align__(256) unsigned long long g_masked_slots[kMaskedSlots];
+
+std::mutex g_slot_mutex;
+unsigned long long* g_slot_base[kSlotDevices] = {};
+int g_slot_next[kSlotDevices] = {};
+
+// The slot for a launch on `s`, or nullptr for the two-kernel form.
+unsigned long long* masked_slot(cudaStream_t s, int64_t batch, int64_t tokens) {
+  if (batch > kSlotMaxRows || batch * tokens >= kSlotMaxTokens) return nullptr;
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &st) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kSlotDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_slot_mutex);
+  if (st != cudaStreamCaptureStatusActive) {
+    if (g_slot_base[dev] == nullptr) {
+      void* q = nullptr;
+      if (cudaGetSymbolAddress(&q, g_masked_slots) == cudaSuccess)
+        g_slot_base[dev] = static_cast<unsigned long long*>(q);
+      else
+        (void)cudaGetLastError();
+    }
+    return nullptr;
+  }
+  if (g_slot_base[dev] == nullptr || g_slot_next[dev] >= kMaskedSlots) return nullptr;
+  return g_slot_base[dev] + g_slot_next[dev]++;
+}
+
+}  // namespace
+
 extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const float* ratio_random,
                                             const float* mask_random, int64_t batch,
                                             int64_t tokens, int64_t mask_token_id,
@@ -488,11 +634,7 @@ extern "C" int cid_masked_diffusion_corrupt(const int64_t* clean_ids, const floa
   p.metrics = metrics;
   p.counts = static_cast<int64_t*>(workspace);
   cudaStream_t s = as_stream(stream);
-  rc = launch_masked_rows(p, s);
-  if (rc != CID_OK) return rc;
-  return launch_pdl(masked_metrics_kernel, dim3(1), dim3(kT), 0, s,
-                    static_cast<const int64_t*>(p.counts), static_cast<const float*>(ratio), batch,
-                    tokens, metrics);
+  return launch_masked(p, masked_slot(s, batch, tokens), s);
 }
 
 // ---------------------------------------------------------------------------
@@ -568,12 +710,7 @@ extern "C" int cid_masked_diffusion_corrupt_no_alloc(
   p.ratio = ratio;
   p.metrics = metrics;
   p.counts = scratch;
-  cudaStream_t s = as_stream(stream);
-  rc = launch_masked_rows(p, s);
-  if (rc != CID_OK) return rc;
-  return launch_pdl(masked_metrics_kernel, dim3(1), dim3(kT), 0, s,
-                    static_cast<const int64_t*>(p.counts), static_cast<const float*>(ratio), batch,
-                    tokens, metrics);
+  return launch_masked(p, nullptr, as_stream(stream));
 }
 
 extern "C" int cid_thought_corrupt(cid_dtype_t sem_dtype, const void* semantic,

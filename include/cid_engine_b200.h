@@ -284,7 +284,16 @@ CID_API size_t cid_masked_diffusion_workspace_bytes(int64_t batch);
  * (batch f32), metrics (2 f32: mean mask, mean ratio; summed in a fixed
  * order, so repeated calls give identical metrics).  workspace: device
  * scratch of cid_masked_diffusion_workspace_bytes(batch) bytes, 16-byte
- * aligned, contents need not be initialised. */
+ * aligned, contents need not be initialised.
+ * A call on a stream that is being captured into a CUDA graph is captured
+ * as one kernel (eagerly: two) once an eager call on the same device has
+ * run: it takes one of 4096 accumulator slots per device held in the
+ * library's device image, which the captured kernel keeps for the life of
+ * the process and clears after every run.  Outputs are bit-identical either
+ * way.  Two executable instances of one such graph must not run at the
+ * same time; replays of one instance are ordered by CUDA.  When the slots
+ * are spent, or batch >= 2^24, calls are captured as two kernels over the
+ * workspace. */
 CID_API int cid_masked_diffusion_corrupt(const int64_t* clean_ids,
                                  const float* ratio_random,
                                  const float* mask_random, int64_t batch,

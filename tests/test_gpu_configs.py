@@ -136,6 +136,68 @@ def test_masked_diffusion_row_shapes_match_oracle(batch: int, tokens: int) -> No
                            f"masked diffusion [{batch},{tokens}]")
 
 
+def _graph_kernel_nodes(graph) -> int:
+    """Kernel nodes of a captured torch.cuda.CUDAGraph(keep_graph=True)."""
+    import ctypes
+
+    cu = ctypes.CDLL("libcuda.so.1")
+    handle = ctypes.c_void_p(graph.raw_cuda_graph())
+    n = ctypes.c_size_t(0)
+    assert cu.cuGraphGetNodes(handle, None, ctypes.byref(n)) == 0
+    nodes = (ctypes.c_void_p * n.value)()
+    assert cu.cuGraphGetNodes(handle, nodes, ctypes.byref(n)) == 0
+    kinds = []
+    for node in nodes:
+        kind = ctypes.c_int(-1)
+        assert cu.cuGraphNodeGetType(ctypes.c_void_p(node), ctypes.byref(kind)) == 0
+        kinds.append(kind.value)
+    assert all(k == 0 for k in kinds), kinds  # CU_GRAPH_NODE_TYPE_KERNEL only
+    return len(kinds)
+
+
+def test_masked_diffusion_in_a_graph_is_one_kernel_and_matches_eager() -> None:
+    """Captured into a CUDA graph, each masked-diffusion call is one kernel
+    whose last row writes the metrics; its slot is cleared after each run,
+    so replays over new inputs must equal eager calls (two kernels) bit for
+    bit and the oracle.  Shapes: ratios summed by every row (64 rows of 2048),
+    by the last row alone (300 rows), 512-thread rows (8 rows of 9000), and
+    a single short row; a third of the rows take the empty-row fallback."""
+    shapes = [(64, 2048), (300, 100), (8, 9000), (1, 33)]
+    gen = torch.Generator().manual_seed(11)
+
+    def fresh(batch, tokens):
+        clean = torch.randint(0, 50257, (batch, tokens), generator=gen)
+        rr = torch.rand(batch, 1, generator=gen)
+        rr[::3] = 0.0
+        return clean, rr, torch.rand(batch, tokens, generator=gen)
+
+    static = [[t.cuda() for t in fresh(b, t)] for b, t in shapes]
+    md = torch.ops.cid_engine.masked_diffusion_corrupt_from_random
+    for clean, rr, mr in static:  # eager first: the one-kernel form needs it
+        md(clean, rr, mr, 50256, 1e-6, 1.0)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph(keep_graph=True)
+    with torch.cuda.graph(graph):
+        outs = [md(clean, rr, mr, 50256, 1e-6, 1.0) for clean, rr, mr in static]
+    assert _graph_kernel_nodes(graph) == len(shapes)
+    for rep in range(3):
+        if rep:
+            for (b, t), dst in zip(shapes, static):
+                for d, s in zip(dst, fresh(b, t)):
+                    d.copy_(s)
+        graph.replay()
+        torch.cuda.synchronize()
+        for (b, t), (clean, rr, mr), got in zip(shapes, static, outs):
+            want = md(clean, rr, mr, 50256, 1e-6, 1.0)
+            for x, y in zip(got, want):
+                assert torch.equal(x, y), (rep, b, t)
+            args = (clean.cpu(), rr.cpu(), mr.cpu(), 50256, 1e-6, 1.0)
+            compare.assert_matches("masked_diffusion_corrupt_from_random", got,
+                                   oracle.masked_diffusion_corrupt_from_random(*args),
+                                   f"graph masked diffusion [{b},{t}] replay {rep}")
+    del graph
+
+
 @pytest.mark.parametrize("tokens", [512, 4096, 8192])
 def test_refine_large_rows_match_oracle(tokens: int) -> None:
     """Decode-loop refine shape (B=256, L=512) plus long rows that exceed the
