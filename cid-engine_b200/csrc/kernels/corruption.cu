@@ -11,7 +11,8 @@
 //    computed once per row, every arithmetic step rounded to the storage
 //    dtype as ATen does;
 //  * display corruption (csrc/ops.cpp:292-391): one CTA of 256 to 1024
-//    threads per row, four tokens' loads in flight per thread.
+//    threads per row, two tokens' loads in flight per thread (four past
+//    2048 tokens).
 #include <climits>
 #include <cmath>
 #include <mutex>
@@ -412,19 +413,16 @@ __device__ __forceinline__ void write_display_corrupt(const DisplayCorruptParams
   p.replaced[i] = rep;
 }
 
-constexpr int kCorruptBatch = 4;  // tokens per thread whose loads are issued together
-
 // One CTA of kBT threads per row, two passes over the row: the first finds
 // whether any eligible position falls below the timestep and the first
 // eligible position (the fallback, ops.cpp:326-337); the second writes the
-// four outputs.  Each thread issues the loads of kCorruptBatch tokens
-// (kBT apart, so every load instruction is coalesced) before it uses them.
-template <int kBT>
+// four outputs.  Each thread issues the loads of U tokens (kBT apart, so
+// every load instruction is coalesced) before it uses them.
+template <int kBT, int U>
 __global__ void __launch_bounds__(kBT) display_corrupt_kernel(DisplayCorruptParams p) {
   pdl_wait();
   pdl_trigger();
   constexpr int kW = kBT / 32;
-  constexpr int U = kCorruptBatch;
   __shared__ int64_t s_first[kW];
   const int64_t row = blockIdx.x;
   const int64_t base = row * p.tokens;
@@ -780,12 +778,18 @@ extern "C" int cid_display_corrupt(const int64_t* token_ids, cid_dtype_t t_dtype
                          vocab_size, has_eos, replace,
                          static_cast<float>(replacement_fraction), corrupted, labels, masked,
                          replaced};
-  // a row's tokens in one batch of loads where the row allows it
+  // Two tokens a thread, a row in one batch of loads, up to 2048 tokens; four
+  // tokens a thread over 1024 threads beyond.  The per-token work (the
+  // replacement's wrap and skips) favours threads over loads in flight: at
+  // [64, 1024] 3.6 us against 5.1 with 256 threads x 4 tokens, at [64, 2048]
+  // 5.5 against 6.0 with 512 x 4 and 9.7 with 256 x 8 (CUDA-graph replays).
   const unsigned grid = static_cast<unsigned>(batch);
   cudaStream_t s = as_stream(stream);
-  if (tokens <= 256 * kCorruptBatch)
-    return launch_pdl(display_corrupt_kernel<256>, dim3(grid), dim3(256), 0, s, p);
-  if (tokens <= 512 * kCorruptBatch)
-    return launch_pdl(display_corrupt_kernel<512>, dim3(grid), dim3(512), 0, s, p);
-  return launch_pdl(display_corrupt_kernel<1024>, dim3(grid), dim3(1024), 0, s, p);
+  if (tokens <= 512)
+    return launch_pdl(display_corrupt_kernel<256, 2>, dim3(grid), dim3(256), 0, s, p);
+  if (tokens <= 1024)
+    return launch_pdl(display_corrupt_kernel<512, 2>, dim3(grid), dim3(512), 0, s, p);
+  if (tokens <= 2048)
+    return launch_pdl(display_corrupt_kernel<1024, 2>, dim3(grid), dim3(1024), 0, s, p);
+  return launch_pdl(display_corrupt_kernel<1024, 4>, dim3(grid), dim3(1024), 0, s, p);
 }
