@@ -1439,7 +1439,8 @@ def profile_case(name: str) -> None:
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": name, "mean_conf": float(c.mean())}))
         return
-    if name == "corruption":  # training corruption, two launches of each kernel
+    if name == "corruption":  # training corruption, two launches of each kernel (eager),
+        # then masked diffusion captured in a CUDA graph (one kernel) and replayed twice
         sys.path.insert(0, str(ROOT / "tests" / "golden"))
         import cases
 
@@ -1457,8 +1458,17 @@ def profile_case(name: str) -> None:
             d = ops.display_corrupt_from_random(*dc, V3 - 1, EOS_ID, V3, 0.25)
             t = ops.thought_corrupt_from_epsilon(*th)
         torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            mg = ops.masked_diffusion_corrupt_from_random(*md)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        same = all(torch.equal(a, b) for a, b in zip(m, mg))
+        del graph
         print(json.dumps({"profile_case": name, "masked": int(m[1].sum()),
-                          "replaced": int(d[3].sum()), "thought": float(t[0].sum())}))
+                          "replaced": int(d[3].sum()), "thought": float(t[0].sum()),
+                          "graph_equals_eager": same}))
         return
     if name == "decode64":  # decode shape: [1, 64, 155136] bf16, three launches over 16 copies
         ids = decode_ids(64, 16, "cuda")
