@@ -42,10 +42,9 @@ namespace cg = cooperative_groups;
 namespace cid {
 namespace {
 
-#ifndef CID_STATS_THREADS
-#define CID_STATS_THREADS 256
-#endif
-constexpr int kThreads = CID_STATS_THREADS;  // threads per CTA
+// Threads per CTA of the CTA (cluster) kernel: 256 by default; 128 and 512
+// where the launch's shape favours them (launch_stats).
+constexpr int kThreads = 256;
 constexpr int kMaxCluster = 16;  // above 8: non-portable, opted into per kernel
 constexpr float kGap = 5.0f;  // natural-log units; terms stay <= e^5
 constexpr int64_t kNone = LLONG_MAX;
@@ -517,6 +516,7 @@ __device__ __forceinline__ Partial warp_merge_n(Partial q, int n) {
 // Block-wide merge of per-thread partials in a fixed order: butterflies
 // within each warp, then the warps' partials by a butterfly in warp 0
 // (result valid in every thread).
+template <int kBT>
 __device__ Partial block_merge(Partial st, Partial* smem_warps, Partial* smem_out) {
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) st = merge(st, shfl_xor(st, d));
@@ -524,8 +524,8 @@ __device__ Partial block_merge(Partial st, Partial* smem_warps, Partial* smem_ou
   if (lane == 0) smem_warps[warp] = st;
   __syncthreads();
   if (warp == 0) {
-    Partial q = lane < kThreads / 32 ? smem_warps[lane] : empty_partial();
-    q = warp_merge_n(q, kThreads / 32);
+    Partial q = lane < kBT / 32 ? smem_warps[lane] : empty_partial();
+    q = warp_merge_n(q, kBT / 32);
     if (lane == 0) *smem_out = q;
   }
   __syncthreads();
@@ -534,6 +534,7 @@ __device__ Partial block_merge(Partial st, Partial* smem_warps, Partial* smem_ou
 
 // Minimum of v over the block, valid in thread 0 (the barrier on entry
 // makes `smem` reusable by consecutive calls).
+template <int kBT>
 __device__ __forceinline__ int64_t block_min_i64(int64_t v, int64_t* smem) {
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, d));
@@ -542,7 +543,7 @@ __device__ __forceinline__ int64_t block_min_i64(int64_t v, int64_t* smem) {
   if (lane == 0) smem[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    v = lane < kThreads / 32 ? smem[lane] : kNone;
+    v = lane < kBT / 32 ? smem[lane] : kNone;
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, d));
   }
@@ -634,21 +635,22 @@ __device__ void write_normal(const StatsParams& p, int64_t row, int64_t V, int64
 }
 
 // Resident CTAs per SM asked of the register allocator: 0 (no request) for
-// the plain statistics, whose natural allocation already fits four CTAs; the
-// repetition variant is held to four (62 registers, no spills; measured 13 %
-// faster than its natural 74 on fp32 [1024, 32000]).  An explicit 1 would lift
-// the default cap and raise the plain kernels to 92-124 registers.
-template <typename T, bool kRep, Mode kMode, int U>
-__global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(StatsParams p) {
+// the plain statistics, whose natural allocation already fits 1024 threads;
+// the repetition variant is held to 1024 threads (62 registers at 256
+// threads, no spills; measured 13 % faster than its natural 74 on fp32
+// [1024, 32000]).  An explicit 1 would lift the default cap and raise the
+// plain kernels to 92-124 registers.
+template <typename T, bool kRep, Mode kMode, int U, int kBT>
+__global__ void __launch_bounds__(kBT, kRep ? 1024 / kBT : 0) display_stats_kernel(StatsParams p) {
   pdl_wait();
   using VT = VecTraits<T>;
   constexpr int N = 2 * VT::N;
-  __shared__ Partial warp_parts[kThreads / 32];
+  __shared__ Partial warp_parts[kBT / 32];
   __shared__ Partial cta_part;               // this CTA's merged partial
   __shared__ Partial parts[kMaxCluster];     // rank 0: every CTA's partial
   __shared__ float2 heads[kMaxCluster];      // every CTA: (max, sum) of every CTA
   __shared__ int64_t cols[kMaxCluster];      // rank 0: every CTA's first column
-  __shared__ int64_t red[kThreads / 32];
+  __shared__ int64_t red[kBT / 32];
   __shared__ Patch patch;
 
   cg::cluster_group cluster = cg::this_cluster();
@@ -689,10 +691,10 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   int64_t cur_id = 0;
   float cur_x = 0.0f;
   if (writer) cur_id = __ldg(p.ids + row) - (kMode == Mode::kRecord ? p.vocab_offset : 0);
-  stream_row<T, kRep, kThreads, U>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
+  stream_row<T, kRep, kBT, U>(rowp, head, v_beg, v_end, h_end, t_beg, V, pt, a, threadIdx.x);
   if (writer && cur_id >= 0 && cur_id < V) cur_x = VT::scalar(rowp, cur_id);
   Partial mine{a.m, a.om, a.off, a.s0 + a.s1};
-  const Partial cta = block_merge(mine, warp_parts, &cta_part);
+  const Partial cta = block_merge<kBT>(mine, warp_parts, &cta_part);
 
   // The row's maximum (every CTA: its column search needs it) and, in rank
   // 0, the row's merged partial.  Lane k of warp 0 stores this CTA's
@@ -725,8 +727,8 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
 
   // first column of the maximum: threads that hold it re-read their chunk
   int64_t col = kNone;
-  if (!special) col = first_column<T, kRep, kThreads, U>(a, target, rowp, head, v_end, pt);
-  col = block_min_i64(col, red);  // valid in thread 0
+  if (!special) col = first_column<T, kRep, kBT, U>(a, target, rowp, head, v_end, pt);
+  col = block_min_i64<kBT>(col, red);  // valid in thread 0
   if (nrank > 1) {
     if (threadIdx.x == 0) *cluster.map_shared_rank(&cols[rank], 0) = col;
     cluster.sync();  // every CTA's column has landed in rank 0
@@ -749,14 +751,14 @@ __global__ void __launch_bounds__(kThreads, kRep ? 4 : 0) display_stats_kernel(S
   if (special) {
     // Rare path: first NaN column, else first column equal to the maximum.
     int64_t first_nan = kNone, first_max = kNone;
-    for (int64_t c = threadIdx.x; c < V; c += kThreads) {
+    for (int64_t c = threadIdx.x; c < V; c += kBT) {
       float x = VT::scalar(rowp, c);
       if (kRep) x = patched(pt, c, x);
       if (x != x && first_nan == kNone) first_nan = c;
       if (x == target && first_max == kNone) first_max = c;
     }
-    first_nan = block_min_i64(first_nan, red);
-    first_max = block_min_i64(first_max, red);
+    first_nan = block_min_i64<kBT>(first_nan, red);
+    first_max = block_min_i64<kBT>(first_max, red);
     if (threadIdx.x == 0) write_special<T, kMode>(p, row, cur_x, target, first_nan, first_max);
     return;
   }
@@ -1261,10 +1263,10 @@ constexpr int kUnroll = 4;
 // Largest cluster this kernel instance can be launched with: 16 where the
 // device schedules 16-CTA clusters of it (a non-portable size, opted into
 // once per instance), else the portable 8.
-template <typename T, bool kRep, Mode kMode>
+template <typename T, bool kRep, Mode kMode, int kBT>
 int max_cluster() {
   static const int n = [] {  // thread-safe one-time init
-    auto* fn = display_stats_kernel<T, kRep, kMode, kUnroll>;
+    auto* fn = display_stats_kernel<T, kRep, kMode, kUnroll, kBT>;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
         cudaSuccess) {
       cudaGetLastError();
@@ -1272,7 +1274,7 @@ int max_cluster() {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kMaxCluster);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kBT);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kMaxCluster;
@@ -1292,20 +1294,37 @@ int max_cluster() {
 
 // Cluster size: split rows over P CTAs (power of two) while the grid stays
 // within two CTAs per SM and each CTA keeps at least half a round of 32-byte
-// loads (kThreads * kUnroll / 2 vectors).  Measured on B200 over
-// [1, rows, 155136] bf16 (CUDA-graph replays): rows x P near 2 x SMs is
-// the fastest split (32 rows: P = 8, 9.5 us; 64: 4, 11.2 us; 128: 2,
+// loads (kBT * kUnroll / 2 vectors).  Measured on B200 over [1, rows,
+// 155136] bf16 with 256 threads (CUDA-graph replays): rows x P near 2 x SMs
+// is the fastest split (32 rows: P = 8, 9.5 us; 64: 4, 11.2 us; 128: 2,
 // 14.6 us; 256: 1, 21 us); larger clusters spend more in their merges than
 // the extra SMs save, smaller ones leave SMs idle.
-template <typename T, bool kRep, Mode kMode>
+template <typename T, bool kRep, Mode kMode, int kBT>
 int cluster_size(int64_t rows, int64_t vocab) {
   const int64_t target = 2LL * sm_count();
   const int64_t vecs = vocab * static_cast<int64_t>(sizeof(T)) / kVecBytes;
-  const int64_t min_vecs = static_cast<int64_t>(kThreads) * kUnroll / 2;
-  const int pmax = max_cluster<T, kRep, kMode>();
+  const int64_t min_vecs = static_cast<int64_t>(kBT) * kUnroll / 2;
+  const int pmax = max_cluster<T, kRep, kMode, kBT>();
   int P = 1;
   while (P < pmax && rows * P * 2 <= target && vecs / (2 * P) >= min_vecs) P *= 2;
   return P;
+}
+
+// CTAs of the 256-thread kernel resident on the device at once.
+template <typename T, bool kRep, Mode kMode>
+int64_t cta_slots() {
+  static const int64_t n = [] {  // thread-safe one-time init
+    int b = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &b, display_stats_kernel<T, kRep, kMode, kUnroll, kThreads>, kThreads, 0) !=
+            cudaSuccess ||
+        b <= 0) {
+      cudaGetLastError();
+      b = 4;
+    }
+    return static_cast<int64_t>(b) * sm_count();
+  }();
+  return n;
 }
 
 #ifndef CID_STATS_ROW_MODE
@@ -1330,13 +1349,13 @@ bool use_row_warps(int64_t rows) {
   return rows >= 2LL * sm_count() * warps_per_sm;
 }
 
-template <typename T, bool kRep, Mode kMode, int U>
+template <typename T, bool kRep, Mode kMode, int U, int kBT>
 int launch_cta_kernel(const StatsParams& prm, int P, cudaStream_t stream) {
   const int64_t blocks = prm.rows * P;
   if (blocks > INT_MAX) return CID_ERR_INVALID_ARGUMENT;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(blocks));
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kBT);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1347,9 +1366,23 @@ int launch_cta_kernel(const StatsParams& prm, int P, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return record_cuda_error(cudaLaunchKernelEx(&cfg, display_stats_kernel<T, kRep, kMode, U>, prm));
+  return record_cuda_error(
+      cudaLaunchKernelEx(&cfg, display_stats_kernel<T, kRep, kMode, U, kBT>, prm));
 }
 
+// The CTA kernel's block size from the bytes one CTA streams (with the
+// 256-thread cluster split) and the CTA count.  Measured on B200 (CUDA-graph
+// replays, 128 / 256 / 512 threads, us): bf16 [1, 155136] (19 KB a CTA)
+// 5.1 / 5.2 / 6.1; [8, 155136] (19 KB) 6.0 / 5.8 / 6.4; [32, 155136]
+// (39 KB) 6.7 / 7.9 / 8.2; [64, 155136] (78 KB) 8.8 / 9.2 / 10.3; [128,
+// 155136] (155 KB) 17.0 / 14.2 / 15.3; [256, 155136] (310 KB) 26.2 / 21.1 /
+// 19.4; fp32 [128, 155136] (310 KB) 30.5 / 19.3 / 17.9; fp32 [8, 32000]
+// (32 KB) 4.8 / 5.1 / 5.7; fp32 [512, 32000] (128 KB, one wave) 17.4 / 14.7 /
+// 17.7; fp32 [1024, 32000] (two waves at 256 threads) 25.0 / 26.5 / 33.4;
+// bf16 [4096, 32000] 48.6 / 57.0 / 85.4.  Fewer threads win where a CTA's
+// merges and barriers weigh against a short chunk, or where smaller CTAs fit
+// the whole grid in one wave; more threads where a long chunk needs more
+// loads in flight.
 template <typename T, bool kRep, Mode kMode>
 int launch_stats(const StatsParams& prm, cudaStream_t stream) {
   if (use_row_warps<T, kRep, kMode>(prm.rows)) {
@@ -1358,8 +1391,16 @@ int launch_stats(const StatsParams& prm, cudaStream_t stream) {
     return launch_pdl(display_stats_rows_kernel<T, kRep, kMode, kUnroll>,
                       dim3(static_cast<unsigned>(blocks)), dim3(kRowWarps * 32), 0, stream, prm);
   }
-  const int P = cluster_size<T, kRep, kMode>(prm.rows, prm.vocab);
-  return launch_cta_kernel<T, kRep, kMode, kUnroll>(prm, P, stream);
+  const int P = cluster_size<T, kRep, kMode, kThreads>(prm.rows, prm.vocab);
+  const int64_t chunk = prm.vocab * static_cast<int64_t>(sizeof(T)) / P;
+  if (chunk >= (int64_t{256} << 10))
+    return launch_cta_kernel<T, kRep, kMode, kUnroll, 512>(
+        prm, cluster_size<T, kRep, kMode, 512>(prm.rows, prm.vocab), stream);
+  if (prm.rows * P > cta_slots<T, kRep, kMode>() ||
+      (chunk > (int64_t{24} << 10) && chunk <= (int64_t{96} << 10)))
+    return launch_cta_kernel<T, kRep, kMode, kUnroll, 128>(
+        prm, cluster_size<T, kRep, kMode, 128>(prm.rows, prm.vocab), stream);
+  return launch_cta_kernel<T, kRep, kMode, kUnroll, kThreads>(prm, P, stream);
 }
 
 template <bool kRep, Mode kMode>
