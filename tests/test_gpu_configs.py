@@ -265,6 +265,43 @@ def test_out_of_range_ids_set_status_and_nan() -> None:
     assert cid_engine.device_status(0) == 0
 
 
+@pytest.mark.parametrize("kind", ["repetition", "records"])
+@pytest.mark.parametrize("shape,dtype", [
+    ((4, 256, 32000), torch.float32),     # 1024 rows: 128-thread CTAs (one wave)
+    ((1, 256, 155136), torch.bfloat16),   # 310 KB a CTA: 512-thread CTAs
+    ((1, 128, 155136), torch.float32),    # cluster of 2, 310 KB a CTA: 512 threads
+    ((1, 32, 155136), torch.bfloat16),    # cluster of 8, 39 KB a CTA: 128 threads
+])
+def test_stats_block_sizes_match_oracle(kind, shape, dtype) -> None:
+    """The repetition and vocabulary-shard record variants of the CTA kernel
+    at the shapes whose launch picks 128- and 512-thread CTAs (with and
+    without clusters), against the oracle; repeated ids make patches."""
+    B, L, V = shape
+    g = torch.Generator().manual_seed(B * L + V)
+    lg = (torch.randn(B, L, V, generator=g) * 2).to(dtype)
+    ids = torch.randint(V, (B, L), generator=g)
+    ids[:, 1::4] = ids[:, 0::4]  # adjacent repeats
+    lg[0, 2, V - 1] = 30.0
+    ids[0, 3] = 0  # mask id
+    if kind == "repetition":
+        got = torch.ops.cid_engine.display_token_statistics_with_repetition(
+            ids.cuda(), lg.cuda(), 0, 1, 0.7)
+        exp = oracle.display_token_statistics_with_repetition(ids, lg, 0, 1, 0.7)
+        compare.assert_matches("display_token_statistics_with_repetition", got, exp,
+                               f"repetition {shape} {dtype}")
+    else:
+        half = V // 2
+        got = torch.ops.cid_engine.display_shard_records(ids.cuda(), lg[..., half:].cuda(), half, V)
+        exp = oracle.display_shard_records(ids, lg[..., half:], half, V)
+        got = got.cpu().reshape(exp.shape)
+        # int32 records: max, argmax | NaN flag and the current logit exactly,
+        # the sum of exponentials (float32 bits) within the statistics tolerance
+        assert torch.equal(got[:, [0, 2, 3]], exp[:, [0, 2, 3]])
+        torch.testing.assert_close(got[:, 1].contiguous().view(torch.float32),
+                                   exp[:, 1].contiguous().view(torch.float32),
+                                   rtol=compare.STATS_RTOL, atol=compare.STATS_ATOL)
+
+
 def test_repetition_long_runs() -> None:
     """Runs longer than a warp (the ballot scan loops) and runs touching the
     sequence ends."""
