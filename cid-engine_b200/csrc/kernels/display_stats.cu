@@ -1298,7 +1298,10 @@ int max_cluster() {
 // 155136] bf16 with 256 threads (CUDA-graph replays): rows x P near 2 x SMs
 // is the fastest split (32 rows: P = 8, 9.5 us; 64: 4, 11.2 us; 128: 2,
 // 14.6 us; 256: 1, 21 us); larger clusters spend more in their merges than
-// the extra SMs save, smaller ones leave SMs idle.
+// the extra SMs save, smaller ones leave SMs idle.  A 16-CTA cluster only
+// while the grid keeps to one CTA per SM: at 16 rows of 155136 bf16, P = 8
+// with 128-thread CTAs took 6.5 us against 7.3 for P = 16 (256 threads) and
+// 7.0 for P = 16 (128 threads); at 8 rows P = 16 stays fastest (5.8 us).
 template <typename T, bool kRep, Mode kMode, int kBT>
 int cluster_size(int64_t rows, int64_t vocab) {
   const int64_t target = 2LL * sm_count();
@@ -1307,6 +1310,7 @@ int cluster_size(int64_t rows, int64_t vocab) {
   const int pmax = max_cluster<T, kRep, kMode, kBT>();
   int P = 1;
   while (P < pmax && rows * P * 2 <= target && vecs / (2 * P) >= min_vecs) P *= 2;
+  if (P > 8 && rows * P > sm_count()) P = 8;
   return P;
 }
 

@@ -62,7 +62,7 @@ def test_full_size_32x1024x128256_rows_match_oracle() -> None:
     assert bool((cur <= conf * (1 + 1e-6)).all())
 
 
-@pytest.mark.parametrize("rows", [1, 3, 32, 64, 128, 256, 512])
+@pytest.mark.parametrize("rows", [1, 3, 8, 16, 32, 64, 128, 256, 512])
 @pytest.mark.parametrize("dtype,vocab", [(torch.bfloat16, 155136), (torch.float32, 32000),
                                          (torch.float16, 50021)])
 def test_decode_rows_match_oracle(rows: int, dtype: torch.dtype, vocab: int) -> None:
