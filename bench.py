@@ -1543,15 +1543,23 @@ def main() -> None:
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    line_out = sys.stdout
+    if world > 1:
+        # Libraries write to file descriptor 1 during set-up (NCCL's version
+        # banner at communicator creation): send that to stderr and keep the
+        # original stdout for the one JSON line.
+        sys.stdout.flush()
+        line_out = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(bench_reference(args, world)))
+            print(json.dumps(bench_reference(args, world)), file=line_out, flush=True)
         return
     if world > 1:
         line = bench_vocab_parallel(args, display_inputs, ClockSampler, _peaks,
                                              run_cpu_baseline)
         if rank == 0:
-            print(json.dumps(line))
+            print(json.dumps(line), file=line_out, flush=True)
         return
     print(json.dumps(bench_single(args)))
 
