@@ -1383,10 +1383,13 @@ int launch_cta_kernel(const StatsParams& prm, int P, cudaStream_t stream) {
 // 19.4; fp32 [128, 155136] (310 KB) 30.5 / 19.3 / 17.9; fp32 [8, 32000]
 // (32 KB) 4.8 / 5.1 / 5.7; fp32 [512, 32000] (128 KB, one wave) 17.4 / 14.7 /
 // 17.7; fp32 [1024, 32000] (two waves at 256 threads) 25.0 / 26.5 / 33.4;
-// bf16 [4096, 32000] 48.6 / 57.0 / 85.4.  Fewer threads win where a CTA's
-// merges and barriers weigh against a short chunk, or where smaller CTAs fit
-// the whole grid in one wave; more threads where a long chunk needs more
-// loads in flight.
+// bf16 [4096, 32000] 48.6 / 57.0 / 85.4; whole rows at up to two CTAs per
+// SM: fp32 [256, 32000] (128 KB) 14.7 / 10.3 / 9.7, bf16 [256, 128256]
+// (250 KB) 22.9 / 18.2 / 17.1, fp16 [256, 50257] (100 KB) 14.4 / 10.6 /
+// 10.5; bf16 [1024, 128256] 45.6 / 47.6 / 51.0.  Fewer threads win where a
+// CTA's merges and barriers weigh against a short chunk, or where smaller
+// CTAs fit the whole grid in one wave; more threads where a long chunk needs
+// more loads in flight and the grid is small.
 template <typename T, bool kRep, Mode kMode>
 int launch_stats(const StatsParams& prm, cudaStream_t stream) {
   if (use_row_warps<T, kRep, kMode>(prm.rows)) {
@@ -1397,7 +1400,8 @@ int launch_stats(const StatsParams& prm, cudaStream_t stream) {
   }
   const int P = cluster_size<T, kRep, kMode, kThreads>(prm.rows, prm.vocab);
   const int64_t chunk = prm.vocab * static_cast<int64_t>(sizeof(T)) / P;
-  if (chunk >= (int64_t{256} << 10))
+  const bool few = prm.rows * P <= 2LL * sm_count();  // at most two CTAs per SM
+  if (few && (chunk >= (int64_t{256} << 10) || (P == 1 && chunk >= (int64_t{96} << 10))))
     return launch_cta_kernel<T, kRep, kMode, kUnroll, 512>(
         prm, cluster_size<T, kRep, kMode, 512>(prm.rows, prm.vocab), stream);
   if (prm.rows * P > cta_slots<T, kRep, kMode>() ||
